@@ -1,0 +1,75 @@
+"""Pin the CPU oracle to the reference: every golden vector in tests/golden/golden.npz was produced by the reference
+implementation itself (tests/golden/make_golden.py)."""
+import numpy as np
+import torch
+
+from golden_inputs import STREAM_MAX_SLOTS, gdn_raw, ring_inputs, sample_index, stream_script
+from oracle import kernels as K
+from oracle.pack import pack_inputs
+from oracle.stream import StreamOracle, score_complete
+from hs_guard_b200 import DEFAULT
+from hs_guard_b200 import weights as W
+
+PACK_CASES = [([[4, 5, 6]], [0], 2, 4, [7], 1),
+              ([[1], [2], [3]], [2, 0, 1], 4, 1, [5, 0, 9], 3),
+              ([[10, 11], [12, 13, 14, 15, 16], [17]], [1, 3, 0], 4, 8, [100, 3, 0, 511], 4)]
+
+
+def test_pack_inputs_matches_reference(golden):
+    for i, (chunks, slots, nb, lb, length, max_slots) in enumerate(PACK_CASES):
+        buf = np.full(nb * lb + 3 * nb, -7, dtype=np.int64)
+        lens = pack_inputs(chunks, slots, nb, lb, np.asarray(length), max_slots, buf)
+        np.testing.assert_array_equal(buf, golden[f"pack{i}_out"])
+        np.testing.assert_array_equal(lens, golden[f"pack{i}_lens"])
+
+
+def test_pack_inputs_contract_case():
+    # the reference's own unit test (tests/test_contract.py:14-18)
+    out = np.empty(2 * 4 + 3 * 2, dtype=np.int64)
+    lens = pack_inputs([[4, 5, 6]], [0], 2, 4, np.array([7]), 1, out)
+    assert lens.tolist() == [3] and out[:8].tolist() == [4, 5, 6, 0, 0, 0, 0, 0]
+    assert out[8:10].tolist() == [3, 0] and out[10:12].tolist() == [0, 1] and out[12:].tolist() == [7, 0]
+
+
+def test_gdn_step_matches_reference(golden):
+    for name, n, L, seed in (("gdn_a", 3, 5, 21), ("gdn_b", 2, 1, 22)):
+        packed, a, b, state = gdn_raw(n, L, seed)
+        zeros = torch.zeros(16)
+        o = K.gdn_slot_step(packed, a, b, zeros, zeros, state, torch.arange(n), torch.full((n,), L))
+        np.testing.assert_allclose(o.numpy(), golden[name + "_o"], rtol=1e-4, atol=1e-5)
+        np.testing.assert_allclose(state.pow(2).sum((-1, -2)).sqrt().numpy(), golden[name + "_state_norm"], rtol=1e-5)
+        sample = state.reshape(-1)[torch.from_numpy(sample_index(state.numel(), 4))].numpy()
+        np.testing.assert_allclose(sample, golden[name + "_state_sample"], rtol=1e-4, atol=1e-6)
+
+
+def test_ring_attention_matches_reference(golden):
+    for name, lb in (("ring_a", 1), ("ring_b", 3)):
+        o = K.ring_attention(*ring_inputs(lb=lb, seed=31 + lb), scale=256 ** -0.5, window=512)
+        np.testing.assert_allclose(o.numpy(), golden[name + "_o"], rtol=1e-4, atol=1e-4)
+
+
+def test_stream_oracle_matches_reference_engine(golden, weights_seed0):
+    """The whole streaming engine: per-token probs, lengths, ring positions (bit-exact) and state pools."""
+    sd = weights_seed0
+    assert W.state_dict_digest(sd) == str(golden["weights_digest"])
+    orc = StreamOracle(sd, DEFAULT, STREAM_MAX_SLOTS)
+    pu, pa = [], []
+    for tick in stream_script():
+        res = orc.step(tick)
+        pu += res["user"]
+        pa += res["assistant"]
+    np.testing.assert_allclose(np.concatenate(pu), golden["stream_probs_user"], atol=2e-5)
+    np.testing.assert_allclose(np.concatenate(pa), golden["stream_probs_assistant"], atol=2e-5)
+    np.testing.assert_array_equal(orc.length, golden["stream_length"])
+    np.testing.assert_array_equal(orc.ring_pos.numpy()[:STREAM_MAX_SLOTS], golden["stream_ring_pos"][:STREAM_MAX_SLOTS])
+    rec = orc.rec[:, :STREAM_MAX_SLOTS]
+    np.testing.assert_allclose(rec.pow(2).sum((-1, -2)).sqrt().numpy(), golden["stream_rec_norm"], rtol=1e-3)
+    sample = rec.reshape(-1)[torch.from_numpy(sample_index(rec.numel(), 1))].numpy()
+    ref = golden["stream_rec_sample"]
+    assert np.abs(sample - ref).max() <= 1e-3 * np.abs(ref).max()
+    conv = orc.conv[:, :STREAM_MAX_SLOTS]
+    np.testing.assert_allclose(conv.reshape(-1)[torch.from_numpy(sample_index(conv.numel(), 2))].numpy(),
+                               golden["stream_conv_sample"], atol=1e-4)
+    # complete-message scores of slot 0's stream agree with the streamed ones (the reference's own invariant)
+    cm = score_complete(sd, DEFAULT, [t for tick in stream_script() for s, ids in tick if s == 0 for t in ids])
+    np.testing.assert_allclose(cm.numpy(), golden["cm_slot0_probs"], atol=5e-5)
