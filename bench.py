@@ -1,0 +1,334 @@
+"""Benchmark of the HS-Guard streaming step on B200 (workload C4 of the reference's headline metric).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Per GPU: 352 slots, each prefilled with 512, 2,048 or 8,000 uniform-random token ids (one third each, seed 4),
+then single-token role=assistant steps (one token for every slot per step). One process per GPU (torchrun for
+N > 1); each rank owns its own 352 slots and full weight replica, no collective on the data path ("weak" scaling).
+
+Reported (rank 0, one JSON line):
+- value: scored tokens/s of the whole job with the packed ticks already resident in HBM (graph replays timed with
+  CUDA events, max over ranks); the per-tick working set (~17 GB) exceeds the 126 MB L2, so no flush is needed.
+- e2e: the same metric through the public API (StreamingGuard.step with host lists: validation, packing, host->device
+  copy, replay, device->host copy of the probabilities, 1 - p(safe)); latency_ms p50/P95 are of these steps.
+- roofline: the dominant kernel (gated-delta-rule step) timed live with CUDA events in an eager tick.
+- cpu_baseline: the CPU oracle port of the same step on this host's cores (bounded sample).
+--impl reference times the CPU oracle port of the reference's step instead (the reference itself is Triton/CUDA-only
+Python that is not shipped to the GPU host) and prints its own line.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "scored tokens/s/GPU at 352 slots; p50/P95 single-token step latency (ms)"
+PUBLISHED_TOKENS_PER_S = 15075.6   # reference, 1x L20, 352 streams
+CONTEXTS = (512, 2048, 8000)
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=30)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=("ours", "reference"))
+    ap.add_argument("--slots", type=int, default=352)
+    ap.add_argument("--contexts", default=",".join(map(str, CONTEXTS)))
+    ap.add_argument("--cpu-slots", type=int, default=32)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+def dist_env():
+    return int(os.environ.get("RANK", 0)), int(os.environ.get("WORLD_SIZE", 1)), int(os.environ.get("LOCAL_RANK", 0))
+
+
+def contexts_for(rank, slots, lens):
+    rng = np.random.Generator(np.random.PCG64(4 + 1000 * rank))
+    per = [lens[i % len(lens)] for i in range(slots)]
+    rng.shuffle(per)
+    return [[int(x) for x in rng.integers(0, 248320, n)] for n in per]
+
+
+# ---- clocks -------------------------------------------------------------------------------------------------------
+class Clocks:
+    FIELDS = "index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown," \
+             "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown," \
+             "clocks_event_reasons.sw_power_cap"
+
+    def __init__(self, gpu_index):
+        self.gpu, self.proc, self.path = gpu_index, None, f"/tmp/hsg_clocks_{os.getpid()}.csv"
+
+    def __enter__(self):
+        try:
+            self.out = open(self.path, "w")
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                                          "-i", str(self.gpu), "-lms", "200"], stdout=self.out,
+                                         stderr=subprocess.DEVNULL)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc:
+            self.proc.terminate()
+            self.proc.wait(timeout=10)
+            self.out.close()
+
+    def summary(self):
+        if not self.proc:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        sm, smax, reasons = [], None, set()
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        for line in open(self.path):
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                smax = float(f[2])
+            except ValueError:
+                continue
+            for name, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(name)
+        os.unlink(self.path)
+        return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": smax, "samples": len(sm),
+                "reasons": sorted(reasons)}
+
+
+# ---- CPU oracle port ------------------------------------------------------------------------------------------------
+def cpu_oracle_rate(sd, slots, steps, warmup):
+    """Tokens/s of the CPU oracle's single-token step (oracle.stream.StreamOracle: the reference's slot-engine
+    algorithm in fp32 torch) on ``slots`` slots whose state is synthetic but full-size (full 512-column rings,
+    random recurrent and conv state), i.e. the same per-step work as the GPU workload."""
+    import torch
+    from hs_guard_b200 import DEFAULT
+    from oracle.stream import StreamOracle
+    torch.set_num_threads(os.cpu_count() or 1)
+    orc = StreamOracle(sd, DEFAULT, slots)
+    g = torch.Generator().manual_seed(5)
+    orc.rec.normal_(0, 0.02, generator=g)
+    orc.conv.normal_(0, 1.0, generator=g)
+    orc.ring_k.normal_(0, 1.0, generator=g)
+    orc.ring_v.normal_(0, 1.0, generator=g)
+    start = 2048
+    for s in range(slots):
+        for p in range(start - 512, start):
+            orc.ring_pos[s, p % 512] = p
+    orc.length[:] = start
+    rng = np.random.default_rng(6)
+    times = []
+    for k in range(warmup + steps):
+        req = [(s, [int(rng.integers(0, 248320))]) for s in range(slots)]
+        t0 = time.perf_counter()
+        orc.step(req)
+        if k >= warmup:
+            times.append(time.perf_counter() - t0)
+    per_step = float(np.mean(times))
+    return {"value": slots / per_step, "unit": "tokens/s", "cores": torch.get_num_threads(), "kind": "port",
+            "sample": f"{slots} slots x {steps} single-token steps (after {warmup} warm-up) of the CPU oracle port "
+                      f"(fp32 torch), full 512-column rings, context position {start}",
+            "ms_per_step": per_step * 1e3}
+
+
+def run_reference(args):
+    rank, world, _ = dist_env()
+    if rank != 0:
+        return
+    from hs_guard_b200 import weights as W
+    sd = W.random_state_dict(0)
+    cb = cpu_oracle_rate(sd, args.cpu_slots, args.steps, args.warmup)
+    line = {"impl": "reference", "metric": METRIC, "value": cb["value"], "unit": "tokens/s", "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": cb["ms_per_step"], "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": f"C4 single-token streaming step, CPU sample of {args.cpu_slots} slots "
+                                   "(the reference path's algorithm, ported; host cores)",
+                       "slots_per_gpu": args.slots},
+            "cpu_baseline": {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")},
+            "e2e": {"value": cb["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+# ---- ours --------------------------------------------------------------------------------------------------------
+def gdn_bytes_per_launch(nb, lb):
+    """Algorithmic HBM bytes of one gated-delta-rule launch: per row, 16 heads x 64 KB state read + write, the fp32
+    conv history (3 x 6144) read + write, the projection columns it reads (q|k|v|z|a|b) and its bf16 hi/lo output."""
+    state = 16 * 128 * 128 * 4 * 2
+    conv = 3 * 6144 * 4 * 2
+    proj = lb * (6144 + 2048 + 32) * 4
+    out = lb * 2048 * 2 * 2
+    return nb * (state + conv + proj + out)
+
+
+def tick_bytes(nb, lb):
+    """Algorithmic HBM bytes of one whole tick: bf16 weights once (non-embedding), per row the fp32 recurrent state
+    (18 layers, read + write), fp32 conv history (read + write), the fp16 ring (6 layers x 2 heads x 512 x 256 x K,V
+    read) and embedding rows."""
+    weights = 498_113_344 * 2 + 2 * 512 * 1024 * 2
+    per_row = 18 * (16 * 128 * 128 * 4 * 2 + 3 * 6144 * 4 * 2) + 6 * 2 * 512 * 256 * 2 * 2 + lb * 1024 * 2
+    return weights + nb * per_row
+
+
+def run_ours(args):
+    import torch
+    rank, world, local = dist_env()
+    torch.cuda.set_device(local)
+    if world > 1:
+        import torch.distributed as dist
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=600), device_id=torch.device("cuda", local))
+    from hs_guard_b200 import _lib
+    from hs_guard_b200 import weights as W
+    from hs_guard_b200.build import build
+    from hs_guard_b200.engine import SlotEngine
+    from hs_guard_b200.pack import pack_inputs
+    from hs_guard_b200.runtime import DEFAULT_METADATA, StreamingGuard
+
+    if rank == 0:
+        build()
+    if world > 1:
+        torch.distributed.barrier()
+    S = args.slots
+    sd = W.random_state_dict(0)
+    eng = SlotEngine(sd, S)
+    guard = StreamingGuard.from_engine(eng, DEFAULT_METADATA)
+    lens = tuple(int(x) for x in args.contexts.split(","))
+    t0 = time.perf_counter()
+    eng.step(list(enumerate(contexts_for(rank, S, lens))))
+    torch.cuda.synchronize()
+    prefill_s = time.perf_counter() - t0
+
+    def barrier():
+        torch.cuda.synchronize()
+        if world > 1:
+            torch.distributed.barrier()
+        torch.cuda.synchronize()
+
+    def max_over_ranks(x):
+        if world == 1:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device="cuda")
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        return float(t.item())
+
+    rng = np.random.default_rng(100 + rank)
+    K, Wm = args.steps, args.warmup
+    slots = np.arange(S, dtype=np.int64)
+    # ---- device-resident ticks (value) ----
+    staged = []
+    length = eng.length.copy()
+    for k in range(Wm + K):
+        buf = np.zeros(S + 3 * S, dtype=np.int64)
+        pack_inputs([[int(t)] for t in rng.integers(0, 248320, S)], slots, S, 1, length, S, buf)
+        length[slots] += 1
+        staged.append(torch.from_numpy(buf).cuda())
+    L = eng._lib
+    for k in range(Wm):
+        _lib.check(L.hsg_launch(eng.handle, staged[k].data_ptr(), S, 1))
+    _lib.check(L.hsg_synchronize(eng.handle))
+    stream = torch.cuda.ExternalStream(L.hsg_stream(eng.handle))
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    with Clocks(local) as clk:
+        start.record(stream)
+        for k in range(Wm, Wm + K):
+            _lib.check(L.hsg_launch(eng.handle, staged[k].data_ptr(), S, 1))
+        end.record(stream)
+        end.synchronize()
+    _lib.check(L.hsg_fetch(eng.handle, S, 1, None))
+    eng.length[:] = length
+    dev_ms = max_over_ranks(start.elapsed_time(end) / K)
+    clocks = clk.summary()
+    launches = eng.launches_per_step(S, 1)
+
+    # ---- end to end through StreamingGuard.step (e2e) ----
+    lat = []
+    for k in range(Wm + K):
+        req = [(s, [int(t)]) for s, t in zip(range(S), rng.integers(0, 248320, S))]
+        barrier() if k == Wm else None
+        t0 = time.perf_counter()
+        guard.step(req, role="assistant")
+        if k >= Wm:
+            lat.append((time.perf_counter() - t0) * 1e3)
+    e2e_ms = max_over_ranks(float(np.mean(lat)))
+    p50 = max_over_ranks(float(np.percentile(lat, 50)))
+    p95 = max_over_ranks(float(np.percentile(lat, 95)))
+
+    # ---- live roofline of the dominant kernel (eager tick with per-kernel CUDA events) ----
+    req = [[int(t)] for t in rng.integers(0, 248320, S)]
+    _, prof = eng.profile_tick(req, slots)
+    gdn_ms, gdn_n = prof["gdn"]
+    gdn_avg_ms = gdn_ms / max(gdn_n, 1)
+    peaks = {}
+    try:
+        peaks = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))
+    except (OSError, ValueError):
+        pass
+    hbm_peak, peak_src = (peaks["hbm_gbs"], "measured") if "hbm_gbs" in peaks else (6650.0, "fallback")
+    gdn_bytes = gdn_bytes_per_launch(S, 1)
+    achieved = gdn_bytes / (gdn_avg_ms * 1e-3) / 1e9
+    traffic = None
+    try:
+        traffic = json.load(open(os.path.join(ROOT, "profiles", "traffic.json")))["gdn_step_c4"]["bytes_per_launch"]
+    except (OSError, ValueError, KeyError):
+        pass
+    step_bytes = tick_bytes(S, 1)
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cb = cpu_oracle_rate(sd, args.cpu_slots, 3, 1)
+        cpu = {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")}
+
+    if rank == 0:
+        value = S * world / (dev_ms * 1e-3)
+        line = {
+            "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": K, "warmup": Wm,
+            "ms_per_step": dev_ms, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": value / world / PUBLISHED_TOKENS_PER_S,
+            "dtype": "f32 (state, norms, accumulation; bf16 hi/lo tensor-core operands, fp16 ring)",
+            "data": "synthetic (uniform random token ids; random-init weights, seed 0)",
+            "config": {"workload": "C4: full-model streaming, 352 slots per GPU prefilled with 512/2048/8000 "
+                                   "random tokens (1/3 each, seed 4), then single-token role=assistant steps",
+                       "slots_per_gpu": S, "contexts": list(lens), "parallelism": f"slot-sharded x{world}",
+                       "l2": "no flush: each tick touches ~17 GB (> 126 MB L2)", "prefill_s": round(prefill_s, 2)},
+            "latency_ms": {"p50": p50, "p95": p95, "device_per_step": dev_ms},
+            "e2e": {"value": S * world / (e2e_ms * 1e-3), "unit": "tokens/s", "h2d_bytes_per_step": (S + 3 * S) * 8,
+                    "d2h_bytes_per_step": 2 * S * 3 * 4 + 4},
+            "gpu_launches": launches * K,
+            "clocks": clocks,
+            "roofline": {"kernel": "gdn_step_kernel (fused conv + gated delta rule + gated norm)", "bound": "hbm",
+                         "achieved": achieved, "peak": hbm_peak, "unit": "GB/s", "frac": achieved / hbm_peak,
+                         "peak_source": peak_src, "traffic": traffic, "algorithmic_bytes": gdn_bytes,
+                         "avg_launch_ms": gdn_avg_ms},
+            "step_roofline": {"bytes": step_bytes, "achieved_gbs": step_bytes / (dev_ms * 1e-3) / 1e9,
+                              "frac": step_bytes / (dev_ms * 1e-3) / 1e9 / hbm_peak},
+            "kernel_ms_eager": {k: round(v[0], 4) for k, v in prof.items() if v[1]},
+            "cpu_baseline": cpu,
+        }
+        print(json.dumps(line), flush=True)
+    eng.close()
+    if world > 1:
+        torch.distributed.barrier()
+        torch.distributed.destroy_process_group()
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

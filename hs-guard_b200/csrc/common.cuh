@@ -1,0 +1,234 @@
+// Shared device helpers for the HS-Guard B200 engine (sm_100a): error reporting, mbarriers with bounded waits,
+// bulk/tensor TMA copies, tcgen05 (TMEM allocation, MMA, commit, loads) and small math utilities.
+#pragma once
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace hsg {
+
+// ---- architecture constants (the kernels are specialised to the HS-Guard backbone) ----------------------------
+constexpr int HIDDEN = 1024;
+constexpr int INTER = 3584;
+constexpr int GDN_H = 16;             // key heads == value heads
+constexpr int GDN_D = 128;            // dk == dv
+constexpr int KEY_DIM = GDN_H * GDN_D;  // 2048
+constexpr int CONV_DIM = 3 * KEY_DIM;   // 6144 (q | k | v channels)
+constexpr int CONV_K = 4;
+constexpr int CONV_KEEP = CONV_K - 1;
+constexpr int GDN_IN = 8320;          // fused GDN projection rows: qkv 6144 | z 2048 | b 16 | a 16 | pad
+constexpr int GDN_Z_OFF = CONV_DIM;
+constexpr int GDN_B_OFF = CONV_DIM + KEY_DIM;
+constexpr int GDN_A_OFF = GDN_B_OFF + GDN_H;
+constexpr int ATT_HQ = 8;
+constexpr int ATT_HKV = 2;
+constexpr int ATT_G = ATT_HQ / ATT_HKV;
+constexpr int ATT_D = 256;
+constexpr int ATT_IN = 2 * ATT_HQ * ATT_D + 2 * ATT_HKV * ATT_D;  // 5120: q(+gate) 4096 | k 512 | v 512
+constexpr int ATT_K_OFF = 2 * ATT_HQ * ATT_D;
+constexpr int ATT_V_OFF = ATT_K_OFF + ATT_HKV * ATT_D;
+constexpr int ROT = 64;               // rotary dims (partial_rotary_factor 0.25 of 256)
+constexpr int WIN = 512;              // attention window; rings hold WIN+1 columns (column WIN is scratch)
+constexpr int HEAD_E = 512;           // classifier head width
+constexpr int N_ROLES = 2;
+constexpr int N_CLS = 3;
+constexpr int MAX_LB = 64;            // largest token bucket of a tick
+
+// ---- error reporting: kernels never trap; they record the first error code and skip the faulty access --------
+enum : int {
+  ERR_NONE = 0,
+  ERR_TIMEOUT_TMA = 1,     // a bounded wait on a TMA/bulk-copy barrier gave up
+  ERR_TIMEOUT_MMA = 2,     // a bounded wait on an MMA-completion barrier gave up
+  ERR_BAD_SLOT = 3,        // slot index outside [0, max_slots]
+  ERR_BAD_TOKEN = 4,       // token id outside the vocabulary
+  ERR_BAD_LEN = 5,         // row length outside [0, lb]
+};
+
+__device__ __forceinline__ void set_error(int* err, int code) {
+  if (err) atomicCAS(err, 0, code);
+}
+
+// ---- shared-memory addresses and mbarriers ---------------------------------------------------------------------
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void fence_barrier_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void fence_proxy_async() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.release.cta.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
+               "r"(bytes) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t done;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, 100000;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(done)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return done != 0;
+}
+
+__device__ __forceinline__ uint64_t global_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+constexpr uint64_t WAIT_LIMIT_NS = 2000000000ull;  // 2 s: far above any legitimate wait in these kernels
+
+// Bounded wait on an mbarrier phase. Gives up after WAIT_LIMIT_NS of wall time (recording `code` in *err), or at
+// once when another CTA has already recorded a timeout (the pipeline is broken; waiting longer only delays the
+// error). Returns false when it gave up; the caller skips the dependent work.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err, int code) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = global_ns();
+  while (true) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if (err) {
+      const int e = *reinterpret_cast<volatile int*>(err);
+      if (e == ERR_TIMEOUT_TMA || e == ERR_TIMEOUT_MMA) return false;
+    }
+    if (global_ns() - t0 > WAIT_LIMIT_NS) {
+      set_error(err, code);
+      return false;
+    }
+  }
+}
+
+// ---- TMA: 1-D bulk copy and 2-D tiled tensor copy (global -> shared, completion on an mbarrier) ---------------
+__device__ __forceinline__ void bulk_g2s(void* smem_dst, const void* gmem_src, uint32_t bytes, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          smem_u32(smem_dst)),
+      "l"(gmem_src), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+
+__device__ __forceinline__ void tma_load_2d(void* smem_dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::
+          "r"(smem_u32(smem_dst)),
+      "l"(map), "r"(x), "r"(y), "r"(smem_u32(bar))
+      : "memory");
+}
+
+__device__ __forceinline__ void prefetch_tmap(const CUtensorMap* map) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(map) : "memory");
+}
+
+// ---- tcgen05: tensor memory, MMA, commit, loads ----------------------------------------------------------------
+__device__ __forceinline__ void tmem_alloc(uint32_t* smem_result, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(smem_result)),
+               "r"(ncols) : "memory");
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+
+// D[tmem] (+)= A[smem] * B[smem]^T, kind::f16 (bf16 inputs, fp32 accumulate), one CTA.
+__device__ __forceinline__ void mma_bf16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                         uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// Arrive on an mbarrier once every tcgen05.mma issued so far by this thread has completed.
+__device__ __forceinline__ void mma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+
+// 32 lanes x 16 consecutive 32-bit columns: thread i of the warp receives lane (taddr.lane + i), columns c..c+15.
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
+  uint32_t r[16];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// Shared-memory matrix descriptor for a K-major bf16 tile written by TMA with 128-byte swizzle: rows of 128 bytes
+// (64 elements), 8-row swizzle atoms of 1024 bytes (stride byte offset), descriptor version 1 (sm_100).
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr >> 4) & 0x3FFF);
+  d |= (uint64_t)1 << 16;                 // leading byte offset (unused for swizzled K-major), 16 B
+  d |= (uint64_t)(1024 >> 4) << 32;       // stride byte offset: 8 rows x 128 B
+  d |= (uint64_t)1 << 46;                 // version
+  d |= (uint64_t)2 << 61;                 // SWIZZLE_128B
+  return d;
+}
+
+// Instruction descriptor: kind::f16, A = B = bf16, D = fp32, both K-major, M x N.
+__host__ __device__ constexpr uint32_t idesc_bf16(int m, int n) {
+  return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(m >> 4) << 24);
+}
+
+// ---- math -------------------------------------------------------------------------------------------------------
+__device__ __forceinline__ float silu(float x) { return x / (1.0f + expf(-x)); }
+__device__ __forceinline__ float sigmoidf_(float x) { return 1.0f / (1.0f + expf(-x)); }
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+// Split an fp32 value into a bf16 pair (hi, lo) with hi + lo == x to ~16 mantissa bits: the activation operand of
+// the tensor-core GEMMs is fed as two bf16 matrices so that x*W is accurate to near fp32 for bf16 weights.
+__device__ __forceinline__ void split_bf16(float x, __nv_bfloat16& hi, __nv_bfloat16& lo) {
+  hi = __float2bfloat16_rn(x);
+  lo = __float2bfloat16_rn(x - __bfloat162float(hi));
+}
+
+// Sum over a thread block of `nthreads` (multiple of 32) using `scratch` (>= nthreads/32 floats).
+__device__ __forceinline__ float block_sum(float v, float* scratch, int nthreads) {
+  v = warp_sum(v);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  __syncthreads();
+  if (lane == 0) scratch[warp] = v;
+  __syncthreads();
+  float t = 0.f;
+  for (int w = 0; w < nthreads / 32; ++w) t += scratch[w];
+  return t;
+}
+
+}  // namespace hsg

@@ -1,0 +1,788 @@
+// HS-Guard B200 streaming engine: state pools, the per-tick kernel sequence, CUDA-graph capture per (rows, tokens)
+// bucket, and the C ABI declared in include/hsg.h.
+#include <cudaTypedefs.h>
+
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <map>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "../../include/hsg.h"
+#include "attn.cuh"
+#include "common.cuh"
+#include "gdn.cuh"
+#include "gemm.cuh"
+#include "norm.cuh"
+
+using namespace hsg;
+
+// ---- error plumbing ---------------------------------------------------------------------------------------------
+static thread_local std::string g_last_error;
+
+static int fail(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_last_error = buf;
+  return code;
+}
+
+#define CU(call)                                                                                   \
+  do {                                                                                             \
+    cudaError_t e_ = (call);                                                                       \
+    if (e_ != cudaSuccess) return fail(HSG_ERR_CUDA, "%s: %s (%s:%d)", #call, cudaGetErrorString(e_), \
+                                       __FILE__, __LINE__);                                        \
+  } while (0)
+
+static const char* device_error_text(int code) {
+  switch (code) {
+    case ERR_TIMEOUT_TMA: return "a bounded wait for a TMA copy timed out";
+    case ERR_TIMEOUT_MMA: return "a bounded wait for tensor-core completion timed out";
+    case ERR_BAD_SLOT: return "a slot index was outside [0, max_slots]";
+    case ERR_BAD_TOKEN: return "a token id was outside the vocabulary";
+    case ERR_BAD_LEN: return "a row length was outside [0, lb]";
+    default: return "unknown device error";
+  }
+}
+
+// ---- TMA descriptors --------------------------------------------------------------------------------------------
+static PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+
+static int get_encoder() {
+  static std::once_flag once;
+  static int status = 0;
+  std::call_once(once, [] {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess || !fn)
+      status = fail(HSG_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
+    g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+  });
+  return g_encode ? HSG_OK : HSG_ERR_CUDA;
+}
+
+// 2-D bf16 [rows][k] row-major, box [64 k][box_rows], 128-byte swizzle.
+static int make_map(CUtensorMap* map, const void* base, int rows, int k, int box_rows) {
+  if (get_encoder() != HSG_OK) return HSG_ERR_CUDA;
+  if ((reinterpret_cast<uintptr_t>(base) & 15) || (k % 64) || box_rows < 16 || box_rows > 256)
+    return fail(HSG_ERR_INVALID, "bad tensor map (base %p, k %d, box %d)", base, k, box_rows);
+  cuuint64_t dims[2] = {(cuuint64_t)k, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)k * 2};
+  cuuint32_t box[2] = {64, (cuuint32_t)box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(HSG_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+  return HSG_OK;
+}
+
+// ---- GEMM planning ----------------------------------------------------------------------------------------------
+struct GemmPlan {
+  int tb, tn, splits, kps, stages, smem;
+};
+
+static constexpr int SM_COUNT = 148;
+static constexpr int SMEM_MAX = 227 * 1024;
+
+static int gemm_smem(int tn, int use_lo, int stages) {
+  return stages * gemm_stage_bytes(tn, use_lo) + (2 * stages + 1) * 8 + 16 + 64 * 16 * 4 + 1024;
+}
+
+// Choose token blocking (tb blocks of tn tokens), K splits (atomic mode only) and pipeline depth so that the grid
+// fills the 148 SMs in as few waves as possible; cost ~ waves x tokens per CTA x K blocks per CTA.
+static GemmPlan plan_gemm(int n_w, int K, int M, int mode, int use_lo) {
+  const int tiles = n_w / 128, KB = K / 64;
+  GemmPlan best{0, 0, 0, 0, 0, 0};
+  long best_cost = -1;
+  const int max_tb = (M + 15) / 16;
+  for (int tb = 1; tb <= max_tb; ++tb) {
+    const int tn = ((M + tb - 1) / tb + 15) / 16 * 16;
+    if (tn > 256) continue;
+    int splits = 1;
+    if (mode == GEMM_ATOMIC) splits = std::max(1, std::min(KB / 2, SM_COUNT / (tiles * tb)));
+    const int kps = (KB + splits - 1) / splits;
+    splits = (KB + kps - 1) / kps;
+    const long ctas = (long)tiles * tb * splits;
+    const long waves = (ctas + SM_COUNT - 1) / SM_COUNT;
+    const long cost = waves * tn * kps;
+    if (best_cost < 0 || cost < best_cost) {
+      best_cost = cost;
+      best = {tb, tn, splits, kps, 0, 0};
+    }
+  }
+  int stages = 4;
+  while (stages > 2 && gemm_smem(best.tn, use_lo, stages) > SMEM_MAX) --stages;
+  best.stages = std::min(stages, std::max(2, best.kps));
+  best.smem = gemm_smem(best.tn, use_lo, best.stages);
+  return best;
+}
+
+static int launch_gemm(cudaStream_t st, const void* w, int n_w, int K, const void* xhi, const void* xlo, int m_alloc,
+                       int M, int mode, float* y, int ldy, __nv_bfloat16* ahi, __nv_bfloat16* alo, int ld_act,
+                       int* err, int force_splits = 0) {
+  const int use_lo = xlo != nullptr;
+  GemmPlan p = plan_gemm(n_w, K, M, mode, use_lo);
+  if (force_splits > 0 && mode == GEMM_ATOMIC) {
+    const int KB = K / 64;
+    p.kps = (KB + force_splits - 1) / force_splits;
+    p.splits = (KB + p.kps - 1) / p.kps;
+  }
+  CUtensorMap tw, th, tl;
+  int rc;
+  if ((rc = make_map(&tw, w, n_w, K, 128)) != HSG_OK) return rc;
+  if ((rc = make_map(&th, xhi, m_alloc, K, p.tn)) != HSG_OK) return rc;
+  if ((rc = make_map(&tl, use_lo ? xlo : xhi, m_alloc, K, p.tn)) != HSG_OK) return rc;
+  GemmArgs a;
+  a.k_blocks_per_split = p.kps;
+  a.k_blocks_total = K / 64;
+  a.tn = p.tn;
+  a.use_lo = use_lo;
+  a.m_store = M;
+  a.stages = p.stages;
+  a.mode = mode;
+  a.y = y;
+  a.ldy = ldy;
+  a.act_hi = ahi;
+  a.act_lo = alo;
+  a.ld_act = ld_act;
+  a.err = err;
+  dim3 grid(p.tb, n_w / 128, p.splits);
+  gemm_tc_kernel<<<grid, GEMM_THREADS, p.smem, st>>>(tw, th, tl, a);
+  CU(cudaGetLastError());
+  return HSG_OK;
+}
+
+static int set_kernel_attributes() {
+  CU(cudaFuncSetAttribute(gemm_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_MAX));
+  CU(cudaFuncSetAttribute(gdn_step_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, gdn_smem_bytes(MAX_LB)));
+  CU(cudaFuncSetAttribute(gdn_step_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                          gdn_smem_bytes(MAX_LB)));
+  CU(cudaFuncSetAttribute(ring_attn_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, attn_smem_bytes(4)));
+  CU(cudaFuncSetAttribute(ring_attn_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, attn_smem_bytes(8)));
+  return HSG_OK;
+}
+
+// ---- engine -----------------------------------------------------------------------------------------------------
+struct Bucket {
+  cudaGraphExec_t exec = nullptr;
+  int launches = 0;
+};
+
+struct hsg_engine {
+  hsg_config cfg;
+  hsg_weights w;
+  int S = 0, device = 0, flags = 0;
+  int n_gdn = 0, n_attn = 0;
+  int max_tokens = 0, m_alloc = 0;
+  cudaStream_t stream = nullptr;
+  // pools
+  float* rec = nullptr;
+  float* conv = nullptr;
+  __half* ring_k = nullptr;
+  __half* ring_v = nullptr;
+  int64_t* ring_pos = nullptr;
+  // per-tick buffers
+  int64_t* packed = nullptr;
+  float* hidden = nullptr;
+  __nv_bfloat16 *xhi = nullptr, *xlo = nullptr, *ohi = nullptr, *olo = nullptr, *ahi = nullptr, *alo = nullptr;
+  float* proj = nullptr;
+  float* qbuf = nullptr;
+  __half *knew = nullptr, *vnew = nullptr;
+  float* hbuf = nullptr;
+  float* probs = nullptr;
+  int* err = nullptr;
+  int* err_host = nullptr;
+  std::map<std::pair<int, int>, Bucket> graphs;
+  std::vector<void*> allocations;
+  // profiling
+  std::vector<cudaEvent_t> events;
+  std::vector<int> event_class;
+  bool profiling = false;
+  int launch_count = 0;
+
+  size_t rec_slot() const { return (size_t)GDN_H * GDN_D * GDN_D; }
+  size_t conv_slot() const { return (size_t)CONV_KEEP * CONV_DIM; }
+  size_t ring_slot() const { return (size_t)ATT_HKV * RING_COLS * ATT_D; }
+};
+
+template <class T>
+static int dalloc(hsg_engine* e, T** p, size_t count) {
+  void* q = nullptr;
+  CU(cudaMalloc(&q, count * sizeof(T)));
+  e->allocations.push_back(q);
+  *p = static_cast<T*>(q);
+  return HSG_OK;
+}
+
+static int check_config(const hsg_config* c) {
+  if (!c) return fail(HSG_ERR_INVALID, "config is NULL");
+  if (c->hidden != HIDDEN || c->intermediate != INTER || c->n_layers != HSG_N_LAYERS || c->full_attn_interval != 4 ||
+      c->gdn_heads != GDN_H || c->gdn_head_dim != GDN_D || c->conv_kernel != CONV_K || c->attn_heads != ATT_HQ ||
+      c->kv_heads != ATT_HKV || c->attn_head_dim != ATT_D || c->rotary_dim != ROT || c->window != WIN ||
+      c->head_hidden != HEAD_E || c->n_classes != N_CLS || c->n_roles != N_ROLES || c->vocab <= 0)
+    return fail(HSG_ERR_UNSUPPORTED, "unsupported architecture: the kernels are built for the HS-Guard backbone");
+  return HSG_OK;
+}
+
+static bool is_attn_layer(int i) { return (i + 1) % 4 == 0; }
+
+// Record timing events around one launch when profiling; always count launches.
+struct ProfScope {
+  hsg_engine* e;
+  int cls;
+  ProfScope(hsg_engine* e_, int c) : e(e_), cls(c) {
+    e->launch_count++;
+    if (e->profiling) {
+      cudaEvent_t ev;
+      cudaEventCreate(&ev);
+      cudaEventRecord(ev, e->stream);
+      e->events.push_back(ev);
+      e->event_class.push_back(cls);
+    }
+  }
+  ~ProfScope() {
+    if (e->profiling) {
+      cudaEvent_t ev;
+      cudaEventCreate(&ev);
+      cudaEventRecord(ev, e->stream);
+      e->events.push_back(ev);
+      e->event_class.push_back(-1);
+    }
+  }
+};
+
+// The whole tick as a sequence of kernels on e->stream (captured into a graph, or run eagerly when profiling).
+static int enqueue_step(hsg_engine* e, int nb, int lb) {
+  const int M = nb * lb;
+  cudaStream_t st = e->stream;
+  const int64_t* ids = e->packed;
+  const int64_t* lens = ids + M;
+  const int64_t* slots = lens + nb;
+  const int64_t* starts = slots + nb;
+  const int use_lo = !(e->flags & HSG_FLAG_BF16_ACT);
+  const float eps = e->cfg.rms_eps;
+  int rc;
+  auto lo = [&](__nv_bfloat16* p) { return use_lo ? p : nullptr; };
+  {
+    ProfScope ps(e, HSG_PROF_EMBED);
+    embed_norm_kernel<<<M, NORM_THREADS, 0, st>>>(ids, static_cast<const __nv_bfloat16*>(e->w.embed), e->cfg.vocab,
+                                                  e->w.layers[0].norm_in, eps, e->hidden, e->xhi, e->xlo, M, e->err);
+    CU(cudaGetLastError());
+  }
+  int gi = 0, ai = 0;
+  for (int i = 0; i < HSG_N_LAYERS; ++i) {
+    const hsg_layer_weights& L = e->w.layers[i];
+    if (!is_attn_layer(i)) {
+      {
+        ProfScope ps(e, HSG_PROF_GEMM_IN);
+        if ((rc = launch_gemm(st, L.w_in, GDN_IN, HIDDEN, e->xhi, lo(e->xlo), e->m_alloc, M, GEMM_STORE, e->proj,
+                              GDN_IN, nullptr, nullptr, 0, e->err)) != HSG_OK)
+          return rc;
+      }
+      GdnArgs g{};
+      g.slots = slots; g.lens = lens; g.nb = nb; g.lb = lb; g.max_slots = e->S;
+      g.proj = e->proj;
+      g.conv_pool = e->conv + (size_t)gi * (e->S + 1) * e->conv_slot();
+      g.conv_w = L.conv_w; g.gnorm_w = L.gnorm_w; g.eps = eps;
+      g.out_hi = e->ohi; g.out_lo = e->olo;
+      g.A_log = L.A_log; g.dt_bias = L.dt_bias;
+      g.state = e->rec + (size_t)gi * (e->S + 1) * e->rec_slot();
+      g.err = e->err;
+      {
+        ProfScope ps(e, HSG_PROF_GDN);
+        gdn_step_kernel<true><<<dim3(GDN_H, nb), GDN_THREADS, gdn_smem_bytes(lb), st>>>(g);
+        CU(cudaGetLastError());
+      }
+      ++gi;
+    } else {
+      {
+        ProfScope ps(e, HSG_PROF_GEMM_IN);
+        if ((rc = launch_gemm(st, L.w_in, ATT_IN, HIDDEN, e->xhi, lo(e->xlo), e->m_alloc, M, GEMM_STORE, e->proj,
+                              ATT_IN, nullptr, nullptr, 0, e->err)) != HSG_OK)
+          return rc;
+      }
+      AttnArgs a{};
+      a.slots = slots; a.lens = lens; a.starts = starts; a.nb = nb; a.lb = lb; a.max_slots = e->S;
+      a.proj = e->proj; a.q_norm = L.q_norm; a.k_norm = L.k_norm; a.inv_freq = e->w.inv_freq; a.eps = eps;
+      a.qbuf = e->qbuf; a.knew = e->knew; a.vnew = e->vnew;
+      a.ring_k = e->ring_k + (size_t)ai * (e->S + 1) * e->ring_slot();
+      a.ring_v = e->ring_v + (size_t)ai * (e->S + 1) * e->ring_slot();
+      a.ring_pos = e->ring_pos;
+      a.out_hi = e->ohi; a.out_lo = e->olo; a.out_raw = nullptr;
+      a.write_ring = lb == 1;
+      a.scale = 1.0f / 16.0f;  // 256^-1/2
+      a.err = e->err;
+      {
+        ProfScope ps(e, HSG_PROF_ATTN_PREP);
+        attn_prep_kernel<<<M, 256, 0, st>>>(a);
+        CU(cudaGetLastError());
+      }
+      {
+        ProfScope ps(e, HSG_PROF_RING_ATTN);
+        if (lb == 1) {
+          ring_attn_kernel<4><<<dim3(nb, ATT_HKV, 1), ATT_THREADS, attn_smem_bytes(4), st>>>(a);
+        } else {
+          ring_attn_kernel<8><<<dim3(nb, ATT_HKV, (ATT_G * lb + 7) / 8), ATT_THREADS, attn_smem_bytes(8), st>>>(a);
+        }
+        CU(cudaGetLastError());
+      }
+      if (lb > 1) {
+        ProfScope ps(e, HSG_PROF_RING_APPEND);
+        ring_append_kernel<<<dim3(nb, ATT_HKV), ATT_D, 0, st>>>(a);
+        CU(cudaGetLastError());
+      }
+      ++ai;
+    }
+    {
+      ProfScope ps(e, HSG_PROF_GEMM_OUT);
+      if ((rc = launch_gemm(st, L.w_out, HIDDEN, KEY_DIM, e->ohi, lo(e->olo), e->m_alloc, M, GEMM_ATOMIC, e->hidden,
+                            HIDDEN, nullptr, nullptr, 0, e->err)) != HSG_OK)
+        return rc;
+    }
+    {
+      ProfScope ps(e, HSG_PROF_NORM);
+      resid_norm_kernel<<<M, NORM_THREADS, 0, st>>>(e->hidden, L.norm_post, eps, e->xhi, e->xlo, M);
+      CU(cudaGetLastError());
+    }
+    {
+      ProfScope ps(e, HSG_PROF_GEMM_GU);
+      if ((rc = launch_gemm(st, L.w_gu, 2 * INTER, HIDDEN, e->xhi, lo(e->xlo), e->m_alloc, M, GEMM_SILU_MUL, nullptr,
+                            0, e->ahi, e->alo, INTER, e->err)) != HSG_OK)
+        return rc;
+    }
+    {
+      ProfScope ps(e, HSG_PROF_GEMM_DOWN);
+      if ((rc = launch_gemm(st, L.w_down, HIDDEN, INTER, e->ahi, lo(e->alo), e->m_alloc, M, GEMM_ATOMIC, e->hidden,
+                            HIDDEN, nullptr, nullptr, 0, e->err)) != HSG_OK)
+        return rc;
+    }
+    {
+      ProfScope ps(e, HSG_PROF_NORM);
+      const float* nxt = i + 1 < HSG_N_LAYERS ? e->w.layers[i + 1].norm_in : e->w.final_norm;
+      resid_norm_kernel<<<M, NORM_THREADS, 0, st>>>(e->hidden, nxt, eps, e->xhi, e->xlo, M);
+      CU(cudaGetLastError());
+    }
+  }
+  {
+    ProfScope ps(e, HSG_PROF_HEAD_GEMM);
+    if ((rc = launch_gemm(st, e->w.head_w1, N_ROLES * HEAD_E, HIDDEN, e->xhi, lo(e->xlo), e->m_alloc, M, GEMM_STORE,
+                          e->hbuf, N_ROLES * HEAD_E, nullptr, nullptr, 0, e->err)) != HSG_OK)
+      return rc;
+  }
+  {
+    ProfScope ps(e, HSG_PROF_HEAD);
+    head_finish_kernel<<<M, 256, 0, st>>>(e->hbuf, e->w.head_b1, e->w.head_ln_w, e->w.head_ln_b, e->w.head_w2,
+                                          e->w.head_b2, e->cfg.head_ln_eps, e->probs, M);
+    CU(cudaGetLastError());
+  }
+  {
+    ProfScope ps(e, HSG_PROF_COMMIT);
+    ring_commit_kernel<<<(M + 255) / 256, 256, 0, st>>>(slots, lens, starts, nb, lb, e->S, e->ring_pos);
+    CU(cudaGetLastError());
+  }
+  return HSG_OK;
+}
+
+static int check_shape(const hsg_engine* e, int nb, int lb) {
+  if (!e) return fail(HSG_ERR_INVALID, "engine is NULL");
+  if (lb < 1 || lb > MAX_LB) return fail(HSG_ERR_INVALID, "lb must be in [1, %d], got %d", MAX_LB, lb);
+  if (nb < 1 || nb > e->S || nb * lb > e->max_tokens)
+    return fail(HSG_ERR_INVALID, "nb must be in [1, max_slots=%d], got %d", e->S, nb);
+  return HSG_OK;
+}
+
+// Host-side validation of a packed tick (the kernels also bound-check and report through the error flag).
+static int validate_packed(const hsg_engine* e, const int64_t* packed, int nb, int lb) {
+  if (!packed) return fail(HSG_ERR_INVALID, "packed is NULL");
+  const int64_t* lens = packed + (size_t)nb * lb;
+  const int64_t* slots = lens + nb;
+  const int64_t* starts = slots + nb;
+  std::vector<char> seen(e->S + 1, 0);
+  for (int n = 0; n < nb; ++n) {
+    if (lens[n] < 0 || lens[n] > lb) return fail(HSG_ERR_INVALID, "row %d: length %lld outside [0, %d]", n,
+                                                 (long long)lens[n], lb);
+    if (slots[n] < 0 || slots[n] > e->S) return fail(HSG_ERR_INVALID, "row %d: slot %lld outside [0, %d]", n,
+                                                     (long long)slots[n], e->S);
+    if (lens[n] > 0) {
+      if (slots[n] == e->S) return fail(HSG_ERR_INVALID, "row %d: the scratch slot cannot carry tokens", n);
+      if (seen[slots[n]]) return fail(HSG_ERR_INVALID, "slot %lld appears twice in one tick", (long long)slots[n]);
+      seen[slots[n]] = 1;
+      if (starts[n] < 0) return fail(HSG_ERR_INVALID, "row %d: negative start", n);
+    }
+    for (int t = 0; t < lens[n]; ++t) {
+      const int64_t id = packed[(size_t)n * lb + t];
+      if (id < 0 || id >= e->cfg.vocab) return fail(HSG_ERR_INVALID, "token id %lld outside [0, %d)",
+                                                    (long long)id, e->cfg.vocab);
+    }
+  }
+  return HSG_OK;
+}
+
+static int get_graph(hsg_engine* e, int nb, int lb, Bucket** out) {
+  auto key = std::make_pair(nb, lb);
+  auto it = e->graphs.find(key);
+  if (it != e->graphs.end()) {
+    *out = &it->second;
+    return HSG_OK;
+  }
+  Bucket b;
+  cudaGraph_t g = nullptr;
+  e->launch_count = 0;
+  CU(cudaStreamBeginCapture(e->stream, cudaStreamCaptureModeThreadLocal));
+  int rc = enqueue_step(e, nb, lb);
+  cudaError_t ce = cudaStreamEndCapture(e->stream, &g);
+  if (rc != HSG_OK) {
+    if (g) cudaGraphDestroy(g);
+    return rc;
+  }
+  if (ce != cudaSuccess) return fail(HSG_ERR_CUDA, "graph capture failed: %s", cudaGetErrorString(ce));
+  ce = cudaGraphInstantiate(&b.exec, g, 0);
+  cudaGraphDestroy(g);
+  if (ce != cudaSuccess) return fail(HSG_ERR_CUDA, "graph instantiate failed: %s", cudaGetErrorString(ce));
+  b.launches = e->launch_count;
+  e->graphs[key] = b;
+  *out = &e->graphs[key];
+  return HSG_OK;
+}
+
+extern "C" {
+
+const char* hsg_last_error(void) { return g_last_error.c_str(); }
+const char* hsg_version(void) { return "hsg-b200 0.1 (sm_100a)"; }
+
+int hsg_create(const hsg_config* cfg, const hsg_weights* w, int max_slots, int device, int flags, hsg_engine** out) {
+  int rc;
+  if (!out || !w) return fail(HSG_ERR_INVALID, "NULL argument");
+  *out = nullptr;
+  if ((rc = check_config(cfg)) != HSG_OK) return rc;
+  if (max_slots < 1 || max_slots > 4096) return fail(HSG_ERR_INVALID, "max_slots must be in [1, 4096]");
+  CU(cudaSetDevice(device));
+  cudaDeviceProp prop;
+  CU(cudaGetDeviceProperties(&prop, device));
+  if (prop.major != 10) return fail(HSG_ERR_UNSUPPORTED, "device %d is sm_%d%d; the kernels are built for sm_100a",
+                                    device, prop.major, prop.minor);
+  if ((rc = set_kernel_attributes()) != HSG_OK) return rc;
+  if ((rc = get_encoder()) != HSG_OK) return rc;
+  hsg_engine* e = new hsg_engine();
+  e->cfg = *cfg;
+  e->w = *w;
+  e->S = max_slots;
+  e->device = device;
+  e->flags = flags;
+  e->n_gdn = 18;
+  e->n_attn = 6;
+  e->max_tokens = max_slots * MAX_LB;
+  e->m_alloc = e->max_tokens + 256;
+  const size_t S1 = (size_t)max_slots + 1, M = e->m_alloc;
+#define TRY(x)                 \
+  if ((rc = (x)) != HSG_OK) {  \
+    hsg_destroy(e);            \
+    return rc;                 \
+  }
+  TRY(dalloc(e, &e->rec, (size_t)e->n_gdn * S1 * e->rec_slot()));
+  TRY(dalloc(e, &e->conv, (size_t)e->n_gdn * S1 * e->conv_slot()));
+  TRY(dalloc(e, &e->ring_k, (size_t)e->n_attn * S1 * e->ring_slot()));
+  TRY(dalloc(e, &e->ring_v, (size_t)e->n_attn * S1 * e->ring_slot()));
+  TRY(dalloc(e, &e->ring_pos, S1 * RING_COLS));
+  TRY(dalloc(e, &e->packed, M + 3 * S1));
+  TRY(dalloc(e, &e->hidden, M * HIDDEN));
+  TRY(dalloc(e, &e->xhi, M * HIDDEN));
+  TRY(dalloc(e, &e->xlo, M * HIDDEN));
+  TRY(dalloc(e, &e->proj, M * GDN_IN));
+  TRY(dalloc(e, &e->ohi, M * KEY_DIM));
+  TRY(dalloc(e, &e->olo, M * KEY_DIM));
+  TRY(dalloc(e, &e->ahi, M * INTER));
+  TRY(dalloc(e, &e->alo, M * INTER));
+  TRY(dalloc(e, &e->qbuf, M * ATT_HQ * ATT_D));
+  TRY(dalloc(e, &e->knew, M * ATT_HKV * ATT_D));
+  TRY(dalloc(e, &e->vnew, M * ATT_HKV * ATT_D));
+  TRY(dalloc(e, &e->hbuf, M * N_ROLES * HEAD_E));
+  TRY(dalloc(e, &e->probs, (size_t)N_ROLES * M * N_CLS));
+  TRY(dalloc(e, &e->err, 1));
+#undef TRY
+  if (cudaMallocHost(&e->err_host, sizeof(int)) != cudaSuccess) {
+    hsg_destroy(e);
+    return fail(HSG_ERR_CUDA, "cudaMallocHost failed");
+  }
+  if (cudaStreamCreateWithFlags(&e->stream, cudaStreamNonBlocking) != cudaSuccess) {
+    hsg_destroy(e);
+    return fail(HSG_ERR_CUDA, "cudaStreamCreate failed");
+  }
+  // activation buffers start clean so padded GEMM rows never read uninitialised memory
+  cudaMemsetAsync(e->xhi, 0, M * HIDDEN * 2, e->stream);
+  cudaMemsetAsync(e->xlo, 0, M * HIDDEN * 2, e->stream);
+  cudaMemsetAsync(e->ohi, 0, M * KEY_DIM * 2, e->stream);
+  cudaMemsetAsync(e->olo, 0, M * KEY_DIM * 2, e->stream);
+  cudaMemsetAsync(e->ahi, 0, M * INTER * 2, e->stream);
+  cudaMemsetAsync(e->alo, 0, M * INTER * 2, e->stream);
+  cudaMemsetAsync(e->err, 0, sizeof(int), e->stream);
+  *out = e;
+  rc = hsg_reset_all(e);
+  if (rc != HSG_OK) {
+    hsg_destroy(e);
+    *out = nullptr;
+  }
+  return rc;
+}
+
+int hsg_destroy(hsg_engine* e) {
+  if (!e) return HSG_OK;
+  cudaSetDevice(e->device);
+  if (e->stream) cudaStreamSynchronize(e->stream);
+  for (auto& kv : e->graphs)
+    if (kv.second.exec) cudaGraphExecDestroy(kv.second.exec);
+  for (void* p : e->allocations) cudaFree(p);
+  if (e->err_host) cudaFreeHost(e->err_host);
+  if (e->stream) cudaStreamDestroy(e->stream);
+  delete e;
+  return HSG_OK;
+}
+
+void* hsg_stream(hsg_engine* e) { return e ? (void*)e->stream : nullptr; }
+
+int hsg_synchronize(hsg_engine* e) {
+  if (!e) return fail(HSG_ERR_INVALID, "engine is NULL");
+  CU(cudaStreamSynchronize(e->stream));
+  return HSG_OK;
+}
+
+int hsg_stage(hsg_engine* e, const int64_t* packed, int nb, int lb) {
+  int rc;
+  if ((rc = check_shape(e, nb, lb)) != HSG_OK) return rc;
+  if ((rc = validate_packed(e, packed, nb, lb)) != HSG_OK) return rc;
+  CU(cudaSetDevice(e->device));
+  CU(cudaMemcpyAsync(e->packed, packed, ((size_t)nb * lb + 3 * nb) * sizeof(int64_t), cudaMemcpyHostToDevice,
+                     e->stream));
+  return HSG_OK;
+}
+
+int hsg_launch(hsg_engine* e, const int64_t* packed_dev, int nb, int lb) {
+  int rc;
+  if ((rc = check_shape(e, nb, lb)) != HSG_OK) return rc;
+  CU(cudaSetDevice(e->device));
+  if (packed_dev)
+    CU(cudaMemcpyAsync(e->packed, packed_dev, ((size_t)nb * lb + 3 * nb) * sizeof(int64_t),
+                       cudaMemcpyDeviceToDevice, e->stream));
+  Bucket* b = nullptr;
+  if ((rc = get_graph(e, nb, lb, &b)) != HSG_OK) return rc;
+  CU(cudaGraphLaunch(b->exec, e->stream));
+  return HSG_OK;
+}
+
+int hsg_fetch(hsg_engine* e, int nb, int lb, float* out_probs) {
+  int rc;
+  if ((rc = check_shape(e, nb, lb)) != HSG_OK) return rc;
+  CU(cudaSetDevice(e->device));
+  if (out_probs)
+    CU(cudaMemcpyAsync(out_probs, e->probs, (size_t)N_ROLES * nb * lb * N_CLS * sizeof(float),
+                       cudaMemcpyDeviceToHost, e->stream));
+  CU(cudaMemcpyAsync(e->err_host, e->err, sizeof(int), cudaMemcpyDeviceToHost, e->stream));
+  CU(cudaStreamSynchronize(e->stream));
+  if (*e->err_host) {
+    const int code = *e->err_host;
+    CU(cudaMemsetAsync(e->err, 0, sizeof(int), e->stream));
+    CU(cudaStreamSynchronize(e->stream));
+    return fail(HSG_ERR_DEVICE, "device error %d: %s", code, device_error_text(code));
+  }
+  return HSG_OK;
+}
+
+int hsg_step(hsg_engine* e, const int64_t* packed, int nb, int lb, float* out_probs) {
+  int rc;
+  if ((rc = hsg_stage(e, packed, nb, lb)) != HSG_OK) return rc;
+  if ((rc = hsg_launch(e, nullptr, nb, lb)) != HSG_OK) return rc;
+  return hsg_fetch(e, nb, lb, out_probs);
+}
+
+int hsg_launches_per_step(const hsg_engine* e, int nb, int lb) {
+  if (check_shape(e, nb, lb) != HSG_OK) return -1;
+  auto it = e->graphs.find(std::make_pair(nb, lb));
+  return it == e->graphs.end() ? -1 : it->second.launches;
+}
+
+int hsg_profile_step(hsg_engine* e, const int64_t* packed, int nb, int lb, float* out_probs, float* kernel_ms,
+                     int* launches) {
+  int rc;
+  if ((rc = hsg_stage(e, packed, nb, lb)) != HSG_OK) return rc;
+  e->profiling = true;
+  e->events.clear();
+  e->event_class.clear();
+  e->launch_count = 0;
+  rc = enqueue_step(e, nb, lb);
+  e->profiling = false;
+  if (rc != HSG_OK) return rc;
+  if ((rc = hsg_fetch(e, nb, lb, out_probs)) != HSG_OK) return rc;
+  for (size_t i = 0; i + 1 < e->events.size(); i += 2) {
+    float ms = 0.f;
+    cudaEventElapsedTime(&ms, e->events[i], e->events[i + 1]);
+    const int c = e->event_class[i];
+    if (c >= 0 && c < HSG_PROF_N) {
+      if (kernel_ms) kernel_ms[c] += ms;
+      if (launches) launches[c] += 1;
+    }
+  }
+  for (cudaEvent_t ev : e->events) cudaEventDestroy(ev);
+  e->events.clear();
+  e->event_class.clear();
+  return HSG_OK;
+}
+
+int hsg_reset_all(hsg_engine* e) {
+  if (!e) return fail(HSG_ERR_INVALID, "engine is NULL");
+  CU(cudaSetDevice(e->device));
+  const size_t S1 = (size_t)e->S + 1;
+  CU(cudaMemsetAsync(e->rec, 0, (size_t)e->n_gdn * S1 * e->rec_slot() * sizeof(float), e->stream));
+  CU(cudaMemsetAsync(e->conv, 0, (size_t)e->n_gdn * S1 * e->conv_slot() * sizeof(float), e->stream));
+  CU(cudaMemsetAsync(e->ring_k, 0, (size_t)e->n_attn * S1 * e->ring_slot() * sizeof(__half), e->stream));
+  CU(cudaMemsetAsync(e->ring_v, 0, (size_t)e->n_attn * S1 * e->ring_slot() * sizeof(__half), e->stream));
+  CU(cudaMemsetAsync(e->ring_pos, 0xFF, S1 * RING_COLS * sizeof(int64_t), e->stream));  // -1
+  CU(cudaStreamSynchronize(e->stream));
+  return HSG_OK;
+}
+
+// (pool base, bytes per slot, layers) of the four per-layer pools and ring_pos (one "layer").
+struct PoolView {
+  char* base;
+  size_t slot_bytes;
+  int layers;
+};
+
+static void pool_views(const hsg_engine* e, PoolView v[5]) {
+  v[0] = {(char*)e->rec, e->rec_slot() * sizeof(float), e->n_gdn};
+  v[1] = {(char*)e->conv, e->conv_slot() * sizeof(float), e->n_gdn};
+  v[2] = {(char*)e->ring_k, e->ring_slot() * sizeof(__half), e->n_attn};
+  v[3] = {(char*)e->ring_v, e->ring_slot() * sizeof(__half), e->n_attn};
+  v[4] = {(char*)e->ring_pos, RING_COLS * sizeof(int64_t), 1};
+}
+
+size_t hsg_slot_state_bytes(const hsg_engine* e) {
+  if (!e) return 0;
+  PoolView v[5];
+  pool_views(e, v);
+  size_t total = 0;
+  for (auto& p : v) total += p.slot_bytes * p.layers;
+  return total;
+}
+
+int hsg_reset_slot(hsg_engine* e, int slot) {
+  if (!e) return fail(HSG_ERR_INVALID, "engine is NULL");
+  if (slot < 0 || slot >= e->S) return fail(HSG_ERR_INVALID, "slot %d outside [0, %d)", slot, e->S);
+  CU(cudaSetDevice(e->device));
+  PoolView v[5];
+  pool_views(e, v);
+  const size_t S1 = (size_t)e->S + 1;
+  for (int i = 0; i < 5; ++i) {
+    const size_t pitch = v[i].slot_bytes * S1;
+    CU(cudaMemset2DAsync(v[i].base + slot * v[i].slot_bytes, pitch, i == 4 ? 0xFF : 0, v[i].slot_bytes,
+                         v[i].layers, e->stream));
+  }
+  CU(cudaStreamSynchronize(e->stream));
+  return HSG_OK;
+}
+
+static int copy_slot(hsg_engine* e, int slot, char* buf, bool to_buf) {
+  if (!e || !buf) return fail(HSG_ERR_INVALID, "NULL argument");
+  if (slot < 0 || slot >= e->S) return fail(HSG_ERR_INVALID, "slot %d outside [0, %d)", slot, e->S);
+  CU(cudaSetDevice(e->device));
+  PoolView v[5];
+  pool_views(e, v);
+  const size_t S1 = (size_t)e->S + 1;
+  size_t off = 0;
+  for (int i = 0; i < 5; ++i) {
+    const size_t pitch = v[i].slot_bytes * S1, w = v[i].slot_bytes;
+    char* pool = v[i].base + slot * w;
+    if (to_buf) CU(cudaMemcpy2DAsync(buf + off, w, pool, pitch, w, v[i].layers, cudaMemcpyDeviceToDevice, e->stream));
+    else CU(cudaMemcpy2DAsync(pool, pitch, buf + off, w, w, v[i].layers, cudaMemcpyDeviceToDevice, e->stream));
+    off += w * v[i].layers;
+  }
+  CU(cudaStreamSynchronize(e->stream));
+  return HSG_OK;
+}
+
+int hsg_snapshot_slot(hsg_engine* e, int slot, void* dst) { return copy_slot(e, slot, (char*)dst, true); }
+int hsg_restore_slot(hsg_engine* e, int slot, const void* src) { return copy_slot(e, slot, (char*)src, false); }
+
+int hsg_get_pools(const hsg_engine* e, hsg_pools* out) {
+  if (!e || !out) return fail(HSG_ERR_INVALID, "NULL argument");
+  out->rec = e->rec;
+  out->conv = e->conv;
+  out->ring_k = e->ring_k;
+  out->ring_v = e->ring_v;
+  out->ring_pos = e->ring_pos;
+  out->max_slots = e->S;
+  out->n_gdn = e->n_gdn;
+  out->n_attn = e->n_attn;
+  return HSG_OK;
+}
+
+// ---- isolated kernels ---------------------------------------------------------------------------------------------
+int hsg_gdn_step(const void* packed, const float* a, const float* b, const float* A_log, const float* dt_bias,
+                 float* state, const int64_t* slots, const int64_t* lens, int n, int lb, int max_slots, float* o,
+                 int* err, void* stream) {
+  if (!packed || !a || !b || !A_log || !dt_bias || !state || !slots || !lens || !o)
+    return fail(HSG_ERR_INVALID, "NULL argument");
+  if (n < 1 || lb < 1 || lb > MAX_LB || max_slots < 1) return fail(HSG_ERR_INVALID, "bad shape n=%d lb=%d", n, lb);
+  if (reinterpret_cast<uintptr_t>(state) & 15) return fail(HSG_ERR_INVALID, "state must be 16-byte aligned");
+  int rc;
+  if ((rc = set_kernel_attributes()) != HSG_OK) return rc;
+  GdnArgs g{};
+  g.slots = slots; g.lens = lens; g.nb = n; g.lb = lb; g.max_slots = max_slots;
+  g.packed = static_cast<const __nv_bfloat16*>(packed);
+  g.a_raw = a; g.b_raw = b; g.o_raw = o;
+  g.A_log = A_log; g.dt_bias = dt_bias; g.state = state; g.err = err;
+  gdn_step_kernel<false><<<dim3(GDN_H, n), GDN_THREADS, gdn_smem_bytes(lb), (cudaStream_t)stream>>>(g);
+  CU(cudaGetLastError());
+  return HSG_OK;
+}
+
+int hsg_ring_attention(const float* q, void* ring_k, void* ring_v, const void* new_k, const void* new_v,
+                       const int64_t* ring_pos, const int64_t* slots, const int64_t* starts, const int64_t* lens,
+                       int n, int lb, int max_slots, float scale, float* out, int write_ring, int* err, void* stream) {
+  if (!q || !ring_k || !ring_v || !new_k || !new_v || !ring_pos || !slots || !starts || !lens || !out)
+    return fail(HSG_ERR_INVALID, "NULL argument");
+  if (n < 1 || lb < 1 || lb > MAX_LB || max_slots < 1) return fail(HSG_ERR_INVALID, "bad shape n=%d lb=%d", n, lb);
+  if (write_ring && lb != 1) return fail(HSG_ERR_INVALID, "write_ring needs lb == 1");
+  for (const void* p : {(const void*)ring_k, (const void*)ring_v, new_k, new_v})
+    if (reinterpret_cast<uintptr_t>(p) & 15) return fail(HSG_ERR_INVALID, "K/V pointers must be 16-byte aligned");
+  int rc;
+  if ((rc = set_kernel_attributes()) != HSG_OK) return rc;
+  AttnArgs a{};
+  a.slots = slots; a.lens = lens; a.starts = starts; a.nb = n; a.lb = lb; a.max_slots = max_slots;
+  a.qbuf = const_cast<float*>(q);
+  a.knew = static_cast<__half*>(const_cast<void*>(new_k));
+  a.vnew = static_cast<__half*>(const_cast<void*>(new_v));
+  a.ring_k = static_cast<__half*>(ring_k);
+  a.ring_v = static_cast<__half*>(ring_v);
+  a.ring_pos = const_cast<int64_t*>(ring_pos);
+  a.out_raw = out;
+  a.write_ring = write_ring;
+  a.scale = scale;
+  a.err = err;
+  cudaStream_t st = (cudaStream_t)stream;
+  if (lb == 1) ring_attn_kernel<4><<<dim3(n, ATT_HKV, 1), ATT_THREADS, attn_smem_bytes(4), st>>>(a);
+  else ring_attn_kernel<8><<<dim3(n, ATT_HKV, (ATT_G * lb + 7) / 8), ATT_THREADS, attn_smem_bytes(8), st>>>(a);
+  CU(cudaGetLastError());
+  return HSG_OK;
+}
+
+int hsg_gemm(const void* w, int n, int k, const void* x_hi, const void* x_lo, int m, int m_alloc, float* y,
+             void* act_hi, void* act_lo, int mode, int splits, int* err, void* stream) {
+  if (!w || !x_hi) return fail(HSG_ERR_INVALID, "NULL argument");
+  if (n <= 0 || n % 128 || k <= 0 || k % 64 || m < 1 || m_alloc < m) return fail(HSG_ERR_INVALID, "bad GEMM shape");
+  if (mode < 0 || mode > 2) return fail(HSG_ERR_INVALID, "bad mode %d", mode);
+  if (mode != GEMM_SILU_MUL && !y) return fail(HSG_ERR_INVALID, "y is NULL");
+  if (mode == GEMM_SILU_MUL && (!act_hi || !act_lo)) return fail(HSG_ERR_INVALID, "act_hi/act_lo are NULL");
+  int rc;
+  if ((rc = set_kernel_attributes()) != HSG_OK) return rc;
+  return launch_gemm((cudaStream_t)stream, w, n, k, x_hi, x_lo, m_alloc, m, mode, y, n,
+                     static_cast<__nv_bfloat16*>(act_hi), static_cast<__nv_bfloat16*>(act_lo), n / 2, err, splits);
+}
+
+}  // extern "C"

@@ -1,0 +1,113 @@
+"""Whole-engine parity on a B200: the reference's own streaming engine and complete-message scorer produced the golden
+vectors (tests/golden/make_golden.py); here the same script of ticks runs through the C-ABI engine."""
+import numpy as np
+import pytest
+import torch
+
+from golden_inputs import STREAM_MAX_SLOTS, sample_index, stream_script
+from hs_guard_b200 import weights as W
+
+pytestmark = pytest.mark.gpu
+
+P_TOL = 2e-3       # |delta p| per class (the north-star bound on p(safe))
+STATE_RTOL = 1e-2  # recurrent state vs the reference streaming path
+
+
+@pytest.fixture(scope="module")
+def engine_run(golden, weights_seed0):
+    from hs_guard_b200.engine import SlotEngine
+    assert W.state_dict_digest(weights_seed0) == str(golden["weights_digest"])
+    eng = SlotEngine(weights_seed0, STREAM_MAX_SLOTS)
+    pu, pa = [], []
+    for tick in stream_script():
+        res = eng.step(tick)
+        pu += res["user"]
+        pa += res["assistant"]
+    yield eng, np.concatenate(pu), np.concatenate(pa)
+    eng.close()
+
+
+def test_stream_probs_match_reference(golden, engine_run):
+    _, pu, pa = engine_run
+    du = np.abs(pu - golden["stream_probs_user"]).max()
+    da = np.abs(pa - golden["stream_probs_assistant"]).max()
+    print(f"max |dp| user {du:.3g} assistant {da:.3g}")
+    assert du < P_TOL and da < P_TOL, (du, da)
+
+
+def test_stream_matches_complete_message_scores(golden, engine_run):
+    """Slot 0's streamed scores against the reference's complete-message forward over the same 605 tokens."""
+    _, pu, pa = engine_run
+    order = [(s, len(ids)) for tick in stream_script() for s, ids in tick]
+    idx, off = [], 0
+    for s, n in order:
+        if s == 0:
+            idx += list(range(off, off + n))
+        off += n
+    d = max(np.abs(pu[idx] - golden["cm_slot0_probs"][0]).max(), np.abs(pa[idx] - golden["cm_slot0_probs"][1]).max())
+    print(f"max |dp| vs complete message {d:.3g}")
+    assert d < P_TOL, d
+
+
+def test_ring_and_lengths_bit_exact(golden, engine_run):
+    eng, _, _ = engine_run
+    np.testing.assert_array_equal(eng.length, golden["stream_length"])
+    rp = eng.pools()["ring_pos"].cpu().numpy()
+    np.testing.assert_array_equal(rp[:STREAM_MAX_SLOTS], golden["stream_ring_pos"][:STREAM_MAX_SLOTS])
+
+
+def test_state_pools_match_reference(golden, engine_run):
+    eng, _, _ = engine_run
+    pools = eng.pools()
+    rec = pools["rec"][:, :STREAM_MAX_SLOTS].cpu()
+    norms = rec.pow(2).sum((-1, -2)).sqrt().numpy()
+    np.testing.assert_allclose(norms, golden["stream_rec_norm"], rtol=STATE_RTOL)
+    sample = rec.reshape(-1)[torch.from_numpy(sample_index(rec.numel(), 1))].numpy()
+    ref = golden["stream_rec_sample"]
+    assert np.abs(sample - ref).max() <= STATE_RTOL * np.abs(ref).max()
+    conv = pools["conv"][:, :STREAM_MAX_SLOTS].cpu()
+    cs = conv.reshape(-1)[torch.from_numpy(sample_index(conv.numel(), 2))].numpy()
+    ref = golden["stream_conv_sample"]
+    assert np.abs(cs - ref).max() <= STATE_RTOL * np.abs(ref).max()
+    rk = pools["ring_k"][:, :STREAM_MAX_SLOTS].float().cpu()
+    ks = rk.reshape(-1)[torch.from_numpy(sample_index(rk.numel(), 3))].numpy()
+    ref = golden["stream_ringk_sample"]
+    assert np.abs(ks - ref).max() <= STATE_RTOL * np.abs(ref).max()
+
+
+def test_snapshot_restore_and_reset_slot(engine_run):
+    eng, _, _ = engine_run
+    ids = [11, 22, 33]
+    snap = eng.snapshot_slot(1)
+    a = eng.step([(1, ids)])["assistant"][0]
+    eng.restore_slot(1, snap)
+    b = eng.step([(1, ids)])["assistant"][0]
+    np.testing.assert_allclose(a, b, atol=1e-5)
+    eng.reset_slot(2)
+    c = eng.step([(2, ids)])["assistant"][0]
+    eng.reset()
+    d = eng.step([(0, ids)])["assistant"][0]
+    np.testing.assert_allclose(c, d, atol=1e-5)
+    eng.reset()
+    assert int(eng.pools()["ring_pos"].max().item()) == -1
+
+
+def test_streaming_guard_api(golden, weights_seed0):
+    from hs_guard_b200.runtime import DEFAULT_METADATA, StreamingGuard
+    guard = StreamingGuard(weights_seed0, DEFAULT_METADATA, max_slots=STREAM_MAX_SLOTS)
+    out = []
+    for tick in stream_script()[:3]:
+        res = guard.step(tick, role="user")
+        assert [r["slot"] for r in res] == [s for s, _ in tick]
+        for r, (_, ids) in zip(res, tick):
+            assert len(r["cut_scores"]) == len(ids) and r["threshold"] == DEFAULT_METADATA["thresholds"]["user"]
+            out += r["cut_scores"]
+    ref = 1 - golden["stream_probs_user"][:len(out), 0]
+    assert np.abs(np.asarray(out) - ref).max() < P_TOL
+    for bad in ([], [(0, [1]), (0, [2])], [(3, [1])], [(0, [248320])], [(0, [])]):
+        with pytest.raises(ValueError):
+            guard.step(bad)
+    with pytest.raises(ValueError):
+        guard.step([(0, [1])], role="system")
+    guard.reset()
+    guard.engine.close()

@@ -1,0 +1,138 @@
+"""Host-side logic on the CPU: packing, validation, buckets, weight layout, slot sharding, and the C ABI surface."""
+import ctypes
+import os
+import re
+
+import numpy as np
+import pytest
+import torch
+
+from golden_inputs import stream_script
+from hs_guard_b200 import DEFAULT, HsgConfig
+from hs_guard_b200 import weights as W
+from hs_guard_b200.engine import bucket, default_session_buckets
+from hs_guard_b200.pack import pack_inputs
+from hs_guard_b200.runtime import validate_requests
+from hs_guard_b200.shard import route, slot_range, split_requests
+from oracle.pack import pack_inputs as oracle_pack
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def test_pack_matches_oracle_and_reference_cases(golden):
+    cases = [([[4, 5, 6]], [0], 2, 4, [7], 1),
+             ([[1], [2], [3]], [2, 0, 1], 4, 1, [5, 0, 9], 3),
+             ([[10, 11], [12, 13, 14, 15, 16], [17]], [1, 3, 0], 4, 8, [100, 3, 0, 511], 4)]
+    for i, (chunks, slots, nb, lb, length, max_slots) in enumerate(cases):
+        buf = np.full(nb * lb + 3 * nb, -7, dtype=np.int64)
+        lens = pack_inputs(chunks, slots, nb, lb, np.asarray(length), max_slots, buf)
+        np.testing.assert_array_equal(buf, golden[f"pack{i}_out"])
+        np.testing.assert_array_equal(lens, golden[f"pack{i}_lens"])
+    rng = np.random.default_rng(0)
+    for _ in range(50):
+        nb, lb = int(rng.choice([1, 2, 4, 8])), int(rng.choice([1, 2, 4, 16, 64]))
+        n = int(rng.integers(1, nb + 1))
+        slots = rng.permutation(10)[:n]
+        chunks = [list(rng.integers(0, 1000, int(rng.integers(1, lb + 1)))) for _ in range(n)]
+        length = rng.integers(0, 9000, 10)
+        a, b = np.zeros(nb * lb + 3 * nb, np.int64), np.zeros(nb * lb + 3 * nb, np.int64)
+        np.testing.assert_array_equal(pack_inputs(chunks, slots, nb, lb, length, 10, a),
+                                      oracle_pack(chunks, slots, nb, lb, length, 10, b))
+        np.testing.assert_array_equal(a, b)
+
+
+def test_buckets():
+    assert default_session_buckets(352)[-1] == 352 and 320 in default_session_buckets(352)
+    assert default_session_buckets(3) == (1, 2, 3)
+    assert default_session_buckets(1) == (1,)
+    assert bucket(33, (1, 2, 4, 8, 16, 32, 64)) == 64
+    with pytest.raises(ValueError):
+        bucket(65, (1, 64))
+
+
+def test_validation_matches_reference():
+    ok = [(0, [1, 2]), (1, [3])]
+    validate_requests(ok, "user", 2, 100)
+    bad = [([], "user"), (ok, "system"), ([(0, [1]), (0, [2])], "user"), ([(2, [1])], "user"),
+           ([(0, [])], "user"), ([(0, [100])], "user"), ([(0, [-1])], "user"), ([(0, [1.0])], "user"),
+           ([(True and 0.5, [1])], "user")]
+    for req, role in bad:
+        with pytest.raises(ValueError):
+            validate_requests(req, role, 2, 100)
+
+
+def test_config_and_parameter_count():
+    assert DEFAULT.check() is DEFAULT
+    assert sum(int(np.prod(s)) for _, s, _ in W.parameter_specs()) == 754_519_918
+    assert DEFAULT.n_gdn == 18 and DEFAULT.n_attn == 6 and DEFAULT.gdn_in_rows == 8320
+    with pytest.raises(ValueError):
+        HsgConfig(hidden=2048).check()
+
+
+def test_engine_layout_interleave_and_concat():
+    cfg = DEFAULT
+    names = {n for n, _, _ in W.parameter_specs(cfg)}
+    sd = W.random_state_dict(3, cfg, names={n for n in names if "layers.0." in n or "layers.3." in n or
+                                           not n.startswith("backbone.layers")})
+    # fill the other layers with zeros of the right shape so engine_layout can run
+    for n, shape, _ in W.parameter_specs(cfg):
+        if n not in sd:
+            sd[n] = torch.zeros(shape, dtype=torch.bfloat16 if n.startswith("backbone") else torch.float32)
+    dev = W.engine_layout(sd, cfg, "cpu")
+    L0, L3 = dev["layers"][0], dev["layers"][3]
+    assert L0["w_in"].shape == (8320, 1024) and L3["w_in"].shape == (5120, 1024)
+    p = "backbone.layers.0.linear_attn."
+    assert torch.equal(L0["w_in"][:6144], sd[p + "in_proj_qkv.weight"])
+    assert torch.equal(L0["w_in"][8192:8208], sd[p + "in_proj_b.weight"])
+    assert torch.equal(L0["w_in"][8208:8224], sd[p + "in_proj_a.weight"])
+    assert not L0["w_in"][8224:].any()
+    g, u = sd["backbone.layers.0.mlp.gate_proj.weight"], sd["backbone.layers.0.mlp.up_proj.weight"]
+    assert torch.equal(L0["w_gu"][128 * 5:128 * 5 + 64], g[64 * 5:64 * 6])
+    assert torch.equal(L0["w_gu"][128 * 5 + 64:128 * 6], u[64 * 5:64 * 6])
+    assert torch.allclose(dev["inv_freq"], 1.0 / (10000 ** (torch.arange(0, 64, 2).float() / 64)))
+
+
+def test_random_weights_deterministic():
+    a = W.random_state_dict(0, names={"backbone.layers.5.linear_attn.A_log", "heads.user.risk.weight"})
+    b = W.random_state_dict(0, names={"backbone.layers.5.linear_attn.A_log", "heads.user.risk.weight"})
+    assert W.state_dict_digest(a) == W.state_dict_digest(b)
+    assert a["heads.user.risk.weight"].dtype == torch.float32
+    assert torch.equal(a["heads.user.risk.weight"], a["heads.user.risk.weight"].bfloat16().float())
+
+
+def test_slot_sharding_partition():
+    for world in (1, 2, 3, 4, 8):
+        total = 2816
+        owned = []
+        for r in range(world):
+            lo, hi = slot_range(r, world, total)
+            owned += list(range(lo, hi))
+        assert owned == list(range(total))
+        for s in (0, 351, 352, 2815):
+            r, local = route(s, world, total)
+            lo, _ = slot_range(r, world, total)
+            assert lo + local == s
+    reqs = [(5, [1]), (400, [2]), (2000, [3])]
+    assert split_requests(reqs, 1, 8, 2816) == [(400 - 352, [2])]
+
+
+def test_stream_script_shape():
+    ticks = stream_script()
+    assert len(ticks) == 32 and sum(len(ids) for t in ticks for _, ids in t) == 779
+
+
+def _header_symbols():
+    text = open(os.path.join(ROOT, "include", "hsg.h")).read()
+    return sorted(set(re.findall(r"\b(hsg_[a-z_0-9]+)\s*\(", text)))
+
+
+def test_library_exports_every_header_symbol():
+    from hs_guard_b200 import _lib
+    from hs_guard_b200.build import build
+    build()
+    L = ctypes.CDLL(_lib.LIB_PATH)
+    syms = _header_symbols()
+    assert len(syms) >= 20
+    for s in syms:
+        assert hasattr(L, s), s
+    assert _lib.lib().hsg_version().startswith(b"hsg-b200")
