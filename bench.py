@@ -74,6 +74,7 @@ class Clocks:
             self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
                                           "-i", str(self.gpu), "-lms", "200"], stdout=self.out,
                                          stderr=subprocess.DEVNULL)
+            time.sleep(1.0)  # nvidia-smi needs a moment before its first sample
         except (OSError, FileNotFoundError):
             self.proc = None
         return self
@@ -238,17 +239,16 @@ def run_ours(args):
     _lib.check(L.hsg_synchronize(eng.handle))
     stream = torch.cuda.ExternalStream(L.hsg_stream(eng.handle))
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    clk = Clocks(local).__enter__()
     barrier()
-    with Clocks(local) as clk:
-        start.record(stream)
-        for k in range(Wm, Wm + K):
-            _lib.check(L.hsg_launch(eng.handle, staged[k].data_ptr(), S, 1))
-        end.record(stream)
-        end.synchronize()
+    start.record(stream)
+    for k in range(Wm, Wm + K):
+        _lib.check(L.hsg_launch(eng.handle, staged[k].data_ptr(), S, 1))
+    end.record(stream)
+    end.synchronize()
     _lib.check(L.hsg_fetch(eng.handle, S, 1, None))
     eng.length[:] = length
     dev_ms = max_over_ranks(start.elapsed_time(end) / K)
-    clocks = clk.summary()
     launches = eng.launches_per_step(S, 1)
 
     # ---- end to end through StreamingGuard.step (e2e) ----
@@ -260,6 +260,8 @@ def run_ours(args):
         guard.step(req, role="assistant")
         if k >= Wm:
             lat.append((time.perf_counter() - t0) * 1e3)
+    clk.__exit__(None, None, None)
+    clocks = clk.summary()
     e2e_ms = max_over_ranks(float(np.mean(lat)))
     p50 = max_over_ranks(float(np.percentile(lat, 50)))
     p95 = max_over_ranks(float(np.percentile(lat, 95)))

@@ -1,32 +1,33 @@
-// Gated delta rule ("GDN") slot step: one CTA per (session row, head), 128 threads.
+// Gated delta rule ("GDN") slot step as a persistent, head-stationary, warp-specialised TMA pipeline (sm_100a).
 //
-// The per-(slot, head) state S is a 128 x 128 fp32 tile (64 KB, contiguous in the pool [S+1][16][128][128]). It is
-// staged into shared memory with one TMA bulk copy issued before anything else, so the HBM read overlaps the
-// prologue. Each thread then owns a 32-row x 4-column block of S in registers (thread t: columns 4*(t%32)..+3, rows
-// 32*(t/32)..+31) and, per token,
-//     S <- e^g S;  delta = beta (v - S^T k);  S <- S + k delta^T;  o = S^T q
-// using  S^T k  and  S^T q  from one pass over the registers (o = e^g S_old^T q + (k.q) delta), with the four
-// row-group partial sums combined through shared memory (double-buffered, one barrier per token). The final state
-// is written back with coalesced 16-byte stores.
+// Work item = (session row n, head h). The grid is (16 heads, P) with P = 9 CTAs per head (144 CTAs, one per SM);
+// CTA (h, p) serves rows p, p + P, p + 2P, ... of head h, so its conv and gated-norm weights, A_log and dt_bias stay
+// in registers for the whole launch.
 //
-// FUSED variant (engine): the prologue is the causal depthwise conv (kernel 4) + SiLU over the head's 384 q/k/v
-// channels of the fused input projection, rolling the slot's fp32 conv history; the epilogue is the gated RMSNorm
-// over dv = 128 with z (Qwen3_5RMSNormGated) and writes the out_proj operand as a bf16 hi/lo pair.
-// RAW variant (isolated kernel, reference engine/fused_kernels.py:140-211 contract): q/k/v come post-conv as bf16,
-// the output o is fp32.
-//
-// Reference math: q, k L2-normalised with eps 1e-6 and q scaled by dk^-1/2; g = -exp(A_log) softplus(a + dt_bias)
-// (softplus threshold 20); beta = sigmoid(b) (fused_kernels.py:166-188; transformers torch_recurrent_gated_delta_rule).
+// Producer warp (warp 16): for each item, waits until its shared-memory stage is free, writes the previous occupant's
+// updated 64 KB state back to HBM with one TMA bulk store, then loads the item's inputs with TMA bulk copies -- the
+// state tile (contiguous in the pool [S+1][16][128][128]), the head's q/k/v/z projection slices for the tick's tokens
+// and the slot's 3-row conv history -- completing on the stage's `full` barrier. It runs up to STAGES items ahead.
+// Consumer warps (16 warps; thread t owns state column t % 128, rows 32*(t/128)..+31, in registers), per item:
+//   conv: silu(causal depthwise conv, kernel 4) over [history | new tokens] in place, history rolled to global;
+//   q, k L2-normalised (eps 1e-6), q scaled by 128^-1/2; g = -exp(A_log) softplus(a + dt_bias) (threshold 20),
+//   beta = sigmoid(b)  (reference engine/fused_kernels.py:140-194, transformers torch_recurrent_gated_delta_rule);
+//   per token: S <- e^g S; delta = beta (v - S^T k); S <- S + k delta^T; o = S^T q, computed as
+//   o = e^g S_old^T q + (k.q) delta from one pass over the registers, the four row-group partial sums combined in
+//   shared memory; the new state goes back into the stage; output = gated RMSNorm w * (o * rsqrt(mean(o^2)+eps)) *
+//   silu(z) as the out_proj operand (bf16 hi/lo pair); then every consumer arrives on the stage's `empty` barrier.
+// RAW variant (isolated kernel, contract of the reference's gdn_slot_v8, fused_kernels.py:197-211): q/k/v arrive
+// post-conv as bf16 [n][lb][6144], a/b as fp32 [n][lb][16], the output o is fp32 [n][lb][16][128].
 #pragma once
 #include "common.cuh"
 
 namespace hsg {
 
 struct GdnArgs {
-  // session rows
   const int64_t* slots;  // [nb]
   const int64_t* lens;   // [nb]
   int nb, lb, max_slots;
+  int stages;            // shared-memory stages (host: gdn_stages(lb))
   // FUSED inputs
   const float* proj;     // [nb*lb, GDN_IN] fp32 output of the fused input projection
   float* conv_pool;      // [max_slots+1, 3, CONV_DIM] fp32 history (this layer)
@@ -47,96 +48,147 @@ struct GdnArgs {
   int* err;
 };
 
-constexpr int GDN_THREADS = 128;
+constexpr int GDN_CONSUMERS = 512;
+constexpr int GDN_THREADS = GDN_CONSUMERS + 32;  // + one producer warp
+constexpr int GDN_CWARPS = GDN_CONSUMERS / 32;
+constexpr int GDN_RG = GDN_CONSUMERS / GDN_D;    // 4 row groups of 32 rows
 constexpr int GDN_TILE_BYTES = GDN_D * GDN_D * 4;
+constexpr int GDN_CTAS_PER_HEAD = 9;             // 16 x 9 = 144 persistent CTAs on the 148 SMs
+constexpr int GDN_SMEM_LIMIT = 227 * 1024;
 
-__host__ __device__ inline int gdn_smem_bytes(int lb) {
-  // state tile | q,k,v,o [lb][128] | partial sums [2][4][128] float2 | g, beta, qk [lb] | mbarrier
-  return GDN_TILE_BYTES + 4 * lb * GDN_D * 4 + 2 * 4 * GDN_D * 8 + 3 * MAX_LB * 4 + 64 + 128;
+struct GdnMeta {  // per stage, written by the producer before it arrives on `full`
+  int64_t slot;
+  int len, pad;
+};
+
+// Stage layout: state tile | x [lb][4][128] fp32 (q, k, v, z slices; RAW: q, k, v bf16 in the first half) |
+// hist [3][3][128] fp32 (q, k, v channel blocks).
+__host__ __device__ inline int gdn_stage_bytes(int lb) { return GDN_TILE_BYTES + lb * 4 * GDN_D * 4 + 9 * GDN_D * 4; }
+__host__ __device__ inline int gdn_fixed_bytes() {
+  // partial sums [2][4][128] float2 | g, beta, q.k [64] | meta [3] | full, empty barriers [3] | alignment slack
+  return 2 * GDN_RG * GDN_D * 8 + 3 * MAX_LB * 4 + 3 * 16 + 6 * 8 + 128;
 }
+__host__ __device__ inline int gdn_stages(int lb) {
+  int s = (GDN_SMEM_LIMIT - gdn_fixed_bytes()) / gdn_stage_bytes(lb);
+  return s > 3 ? 3 : (s < 1 ? 1 : s);
+}
+__host__ __device__ inline int gdn_smem_bytes(int lb) { return gdn_stages(lb) * gdn_stage_bytes(lb) + gdn_fixed_bytes(); }
 
 template <bool FUSED>
-__global__ void __launch_bounds__(GDN_THREADS, 3) gdn_step_kernel(const GdnArgs args) {
+__global__ void __launch_bounds__(GDN_THREADS, 1) gdn_step_kernel(const GdnArgs args) {
   extern __shared__ __align__(128) uint8_t gdn_smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(gdn_smem_raw) + 127) & ~uintptr_t(127));
-  const int lb = args.lb;
-  float* st = reinterpret_cast<float*>(smem);
-  float* qs = st + GDN_D * GDN_D;
-  float* ks = qs + lb * GDN_D;
-  float* vs = ks + lb * GDN_D;
-  float* os = vs + lb * GDN_D;
-  float2* red = reinterpret_cast<float2*>(os + lb * GDN_D);  // [2][4][128]
-  float* gv = reinterpret_cast<float*>(red + 2 * 4 * GDN_D);
-  float* bv = gv + MAX_LB;
-  float* qk = bv + MAX_LB;
-  uint64_t* bar = reinterpret_cast<uint64_t*>(qk + MAX_LB);
+  const int lb = args.lb, S = args.stages;
+  const int sbytes = gdn_stage_bytes(lb);
+  uint8_t* fixed = smem + S * sbytes;
+  float2* red = reinterpret_cast<float2*>(fixed);                  // [2][4][128]
+  float* gv = reinterpret_cast<float*>(red + 2 * GDN_RG * GDN_D);  // decay factors e^g per token
+  float* bv = gv + MAX_LB;                                         // beta per token
+  float* qk = bv + MAX_LB;                                         // q.k per token
+  GdnMeta* meta = reinterpret_cast<GdnMeta*>(qk + MAX_LB);         // [3]
+  uint64_t* full = reinterpret_cast<uint64_t*>(meta + 3);          // [3]
+  uint64_t* empty = full + 3;                                      // [3]
 
-  const int h = blockIdx.x, n = blockIdx.y, tid = threadIdx.x;
-  const int warp = tid >> 5, lane = tid & 31;
-  int len = (int)args.lens[n];
-  int64_t slot = args.slots[n];
-  if (len < 0 || len > lb) {
-    if (tid == 0) set_error(args.err, ERR_BAD_LEN);
-    len = 0;
-  }
-  if (len > 0 && (slot < 0 || slot > args.max_slots)) {
-    if (tid == 0) set_error(args.err, ERR_BAD_SLOT);
-    len = 0;
-  }
-  float* gstate = args.state + ((size_t)slot * GDN_H + h) * (GDN_D * GDN_D);
+  const int h = blockIdx.x, p = blockIdx.y, P = gridDim.y;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int n_items = args.nb > p ? (args.nb - p + P - 1) / P : 0;
+  auto row_of = [&](int i) { return p + i * P; };
+  auto stage_ptr = [&](int s) { return smem + s * sbytes; };
 
-  if (len == 0) {  // padding row: zero output, no state or history update
-    for (int t = 0; t < lb; ++t) {
-      const size_t row = (size_t)n * lb + t;
+  if (tid == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], GDN_CONSUMERS);
+    }
+    fence_barrier_init();
+  }
+  __syncthreads();
+
+  if (warp == GDN_CWARPS) {
+    // ===================================== producer =====================================
+    int64_t held_slot[3] = {0, 0, 0};
+    int held_len[3] = {0, 0, 0};
+    for (int i = 0; i < n_items + S; ++i) {
+      const int s = i % S, r = i / S;
+      if (r > 0 && i - S < n_items) {
+        // the consumers are done with item i - S in stage s: write its state back
+        if (!mbar_wait(&empty[s], (r - 1) & 1, args.err, ERR_TIMEOUT_TMA)) break;
+        if (lane == 0 && held_len[s] > 0) {
+          bulk_s2g(args.state + ((size_t)held_slot[s] * GDN_H + h) * (GDN_D * GDN_D), stage_ptr(s), GDN_TILE_BYTES);
+          bulk_commit();
+        }
+      }
+      if (i >= n_items) continue;
+      if (lane == 0 && r > 0) bulk_wait_read_all();  // the store has read the stage
+      __syncwarp();
+      const int n = row_of(i);
+      int len = (int)args.lens[n];
+      const int64_t slot = args.slots[n];
+      if (len < 0 || len > lb) {
+        if (lane == 0) set_error(args.err, ERR_BAD_LEN);
+        len = 0;
+      }
+      if (len > 0 && (slot < 0 || slot > args.max_slots)) {
+        if (lane == 0) set_error(args.err, ERR_BAD_SLOT);
+        len = 0;
+      }
+      held_slot[s] = slot;
+      held_len[s] = len;
+      uint8_t* st = stage_ptr(s);
+      float* x = reinterpret_cast<float*>(st + GDN_TILE_BYTES);
+      float* hist = x + lb * 4 * GDN_D;
+      if (lane == 0) {
+        meta[s].slot = slot;
+        meta[s].len = len;
+        fence_proxy_async();
+        if (len > 0)
+          mbar_arrive_expect_tx(&full[s], GDN_TILE_BYTES +
+                                              (FUSED ? len * 4 * GDN_D * 4 + 9 * GDN_D * 4 : len * 3 * GDN_D * 2));
+        else
+          mbar_arrive(&full[s]);
+      }
+      __syncwarp();
+      if (len == 0) continue;
+      if (lane == 0) bulk_g2s(st, args.state + ((size_t)slot * GDN_H + h) * (GDN_D * GDN_D), GDN_TILE_BYTES, &full[s]);
       if (FUSED) {
-        args.out_hi[row * KEY_DIM + h * GDN_D + tid] = __float2bfloat16_rn(0.f);
-        args.out_lo[row * KEY_DIM + h * GDN_D + tid] = __float2bfloat16_rn(0.f);
+        for (int j = lane; j < len * 4; j += 32) {  // q, k, v, z slices of each token: 4 x 512 B
+          const int t = j >> 2, part = j & 3;
+          const float* src = args.proj + ((size_t)n * lb + t) * GDN_IN + part * KEY_DIM + h * GDN_D;
+          bulk_g2s(x + (t * 4 + part) * GDN_D, src, GDN_D * 4, &full[s]);
+        }
+        if (lane < 9) {  // conv history: 3 rows x (q, k, v) channel blocks
+          const int rr = lane / 3, part = lane % 3;
+          const float* src = args.conv_pool + ((size_t)slot * CONV_KEEP + rr) * CONV_DIM + part * KEY_DIM + h * GDN_D;
+          bulk_g2s(hist + (rr * 3 + part) * GDN_D, src, GDN_D * 4, &full[s]);
+        }
       } else {
-        args.o_raw[(row * GDN_H + h) * GDN_D + tid] = 0.f;
+        __nv_bfloat16* xb = reinterpret_cast<__nv_bfloat16*>(x);
+        for (int j = lane; j < len * 3; j += 32) {
+          const int t = j / 3, part = j % 3;
+          const __nv_bfloat16* src = args.packed + ((size_t)n * lb + t) * CONV_DIM + part * KEY_DIM + h * GDN_D;
+          bulk_g2s(xb + (t * 3 + part) * GDN_D, src, GDN_D * 2, &full[s]);
+        }
       }
     }
+    if (lane == 0) bulk_wait_all();
     return;
   }
-  if (tid == 0) {
-    mbar_init(bar, 1);
-    fence_barrier_init();
-    mbar_arrive_expect_tx(bar, GDN_TILE_BYTES);
-    bulk_g2s(st, gstate, GDN_TILE_BYTES, bar);
-  }
 
-  // ---- prologue: q, k, v for the head into shared memory ----
-  if (FUSED) {
-    const int chan[3] = {h * GDN_D + tid, KEY_DIM + h * GDN_D + tid, 2 * KEY_DIM + h * GDN_D + tid};
-    float* dst[3] = {qs, ks, vs};
-    float* hist = args.conv_pool + (size_t)slot * CONV_KEEP * CONV_DIM;
-#pragma unroll
-    for (int c3 = 0; c3 < 3; ++c3) {
-      const int c = chan[c3];
-      const float4 w = *reinterpret_cast<const float4*>(args.conv_w + (size_t)c * CONV_K);
-      float e0 = hist[c], e1 = hist[CONV_DIM + c], e2 = hist[2 * CONV_DIM + c];
-      for (int t = 0; t < len; ++t) {
-        const float x = args.proj[((size_t)n * lb + t) * GDN_IN + c];
-        float acc = w.x * e0;
-        acc = fmaf(w.y, e1, acc);
-        acc = fmaf(w.z, e2, acc);
-        acc = fmaf(w.w, x, acc);
-        dst[c3][t * GDN_D + tid] = silu(acc);
-        e0 = e1; e1 = e2; e2 = x;
-      }
-      hist[c] = e0;
-      hist[CONV_DIM + c] = e1;
-      hist[2 * CONV_DIM + c] = e2;
-    }
-  } else {
-    for (int t = 0; t < len; ++t) {
-      const __nv_bfloat16* src = args.packed + ((size_t)n * lb + t) * CONV_DIM + h * GDN_D + tid;
-      qs[t * GDN_D + tid] = __bfloat162float(src[0]);
-      ks[t * GDN_D + tid] = __bfloat162float(src[KEY_DIM]);
-      vs[t * GDN_D + tid] = __bfloat162float(src[2 * KEY_DIM]);
-    }
-  }
-  if (tid < len) {
-    float a, b;
+  // ===================================== consumers =====================================
+  const int col = tid & (GDN_D - 1), rg = tid >> 7;
+  float4 cw = make_float4(0.f, 0.f, 0.f, 0.f);  // thread t < 384 owns conv channel t % 128 of block t / 128
+  if (FUSED && tid < 3 * GDN_D)
+    cw = *reinterpret_cast<const float4*>(args.conv_w + (size_t)((tid >> 7) * KEY_DIM + h * GDN_D + col) * CONV_K);
+  const float4 gw = FUSED ? reinterpret_cast<const float4*>(args.gnorm_w)[lane] : make_float4(0.f, 0.f, 0.f, 0.f);
+  const float negA = -expf(args.A_log[h]), dtb = args.dt_bias[h];
+
+  // a, b of an item (thread t < lb holds token t), loaded one item ahead so the latency hides behind compute
+  auto load_ab = [&](int i, float& a, float& b) {
+    a = 0.f;
+    b = 0.f;
+    if (i >= n_items || tid >= lb) return;
+    const int n = row_of(i);
+    if (tid >= args.lens[n]) return;
     if (FUSED) {
       const float* row = args.proj + ((size_t)n * lb + tid) * GDN_IN;
       a = row[GDN_A_OFF + h];
@@ -145,112 +197,168 @@ __global__ void __launch_bounds__(GDN_THREADS, 3) gdn_step_kernel(const GdnArgs 
       a = args.a_raw[((size_t)n * lb + tid) * GDN_H + h];
       b = args.b_raw[((size_t)n * lb + tid) * GDN_H + h];
     }
-    const float x = a + args.dt_bias[h];
-    const float sp = x > 20.f ? x : log1pf(expf(x));
-    gv[tid] = expf(-expf(args.A_log[h]) * sp);   // decay factor e^g
-    bv[tid] = sigmoidf_(b);
-  }
-  __syncthreads();
-  // L2 norms (eps 1e-6) and q.k per token; warp w takes tokens w, w+4, ...
-  const float scale = 0.08838834764831845f;  // 128^-1/2, correctly rounded
-  for (int t = warp; t < len; t += 4) {
-    float4 q4 = reinterpret_cast<float4*>(qs + t * GDN_D)[lane];
-    float4 k4 = reinterpret_cast<float4*>(ks + t * GDN_D)[lane];
-    float sq = warp_sum(q4.x * q4.x + q4.y * q4.y + q4.z * q4.z + q4.w * q4.w);
-    float sk = warp_sum(k4.x * k4.x + k4.y * k4.y + k4.z * k4.z + k4.w * k4.w);
-    const float rq = scale / sqrtf(sq + 1e-6f), rk = 1.0f / sqrtf(sk + 1e-6f);
-    q4.x *= rq; q4.y *= rq; q4.z *= rq; q4.w *= rq;
-    k4.x *= rk; k4.y *= rk; k4.z *= rk; k4.w *= rk;
-    reinterpret_cast<float4*>(qs + t * GDN_D)[lane] = q4;
-    reinterpret_cast<float4*>(ks + t * GDN_D)[lane] = k4;
-    const float d = warp_sum(q4.x * k4.x + q4.y * k4.y + q4.z * k4.z + q4.w * k4.w);
-    if (lane == 0) qk[t] = d;
-  }
-  // ---- recurrence ----
-  const bool have = __syncthreads_and(mbar_wait(bar, 0, args.err, ERR_TIMEOUT_TMA));
-  if (!have) {  // the bulk copy never landed: error recorded, state left untouched; one more bounded wait, then leave
-    mbar_wait(bar, 0, nullptr, 0);
-    return;
-  }
-  const int c4 = lane, rg = warp;      // columns 4*c4..4*c4+3, rows 32*rg..32*rg+31
-  float4 s[32];
-#pragma unroll
-  for (int i = 0; i < 32; ++i) s[i] = reinterpret_cast<const float4*>(st + (rg * 32 + i) * GDN_D)[c4];
-  for (int t = 0; t < len; ++t) {
-    const float* kt = ks + t * GDN_D + rg * 32;
-    const float* qt = qs + t * GDN_D + rg * 32;
-    float4 pk = make_float4(0.f, 0.f, 0.f, 0.f), pq = pk;
-#pragma unroll
-    for (int i = 0; i < 32; ++i) {
-      const float kv = kt[i], qv = qt[i];
-      pk.x = fmaf(s[i].x, kv, pk.x); pk.y = fmaf(s[i].y, kv, pk.y);
-      pk.z = fmaf(s[i].z, kv, pk.z); pk.w = fmaf(s[i].w, kv, pk.w);
-      pq.x = fmaf(s[i].x, qv, pq.x); pq.y = fmaf(s[i].y, qv, pq.y);
-      pq.z = fmaf(s[i].z, qv, pq.z); pq.w = fmaf(s[i].w, qv, pq.w);
-    }
-    float2* rb = red + (t & 1) * 4 * GDN_D;
-    float4* rbv = reinterpret_cast<float4*>(rb + rg * GDN_D + c4 * 4);
-    rbv[0] = make_float4(pk.x, pq.x, pk.y, pq.y);
-    rbv[1] = make_float4(pk.z, pq.z, pk.w, pq.w);
-    __syncthreads();
-    float kvs[4] = {0.f, 0.f, 0.f, 0.f}, qss[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-    for (int r = 0; r < 4; ++r) {
-      const float4* p = reinterpret_cast<const float4*>(rb + r * GDN_D + c4 * 4);
-      const float4 a0 = p[0], a1 = p[1];
-      kvs[0] += a0.x; qss[0] += a0.y; kvs[1] += a0.z; qss[1] += a0.w;
-      kvs[2] += a1.x; qss[2] += a1.y; kvs[3] += a1.z; qss[3] += a1.w;
-    }
-    const float eg = gv[t], beta = bv[t], dqk = qk[t];
-    const float4 v4 = reinterpret_cast<const float4*>(vs + t * GDN_D)[c4];
-    const float vv[4] = {v4.x, v4.y, v4.z, v4.w};
-    float dl[4], ov[4];
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      dl[j] = beta * (vv[j] - eg * kvs[j]);
-      ov[j] = fmaf(eg, qss[j], dqk * dl[j]);
-    }
-    if (rg == 0) reinterpret_cast<float4*>(os + t * GDN_D)[c4] = make_float4(ov[0], ov[1], ov[2], ov[3]);
-    const float* kr = ks + t * GDN_D + rg * 32;
-#pragma unroll
-    for (int i = 0; i < 32; ++i) {
-      const float kv = kr[i];
-      s[i].x = fmaf(eg, s[i].x, kv * dl[0]);
-      s[i].y = fmaf(eg, s[i].y, kv * dl[1]);
-      s[i].z = fmaf(eg, s[i].z, kv * dl[2]);
-      s[i].w = fmaf(eg, s[i].w, kv * dl[3]);
-    }
-  }
-#pragma unroll
-  for (int i = 0; i < 32; ++i) reinterpret_cast<float4*>(gstate + (rg * 32 + i) * GDN_D)[c4] = s[i];
-  __syncthreads();
+  };
+  float cur_a, cur_b;
+  load_ab(0, cur_a, cur_b);
+  bool broken = false;
 
-  // ---- epilogue ----
-  if (FUSED) {
-    // gated RMSNorm over dv: w * (o * rsqrt(mean(o^2) + eps)) * silu(z); warp w takes tokens w, w+4, ...
-    const float4 gw = reinterpret_cast<const float4*>(args.gnorm_w)[lane];
-    for (int t = warp; t < lb; t += 4) {
-      const size_t row = (size_t)n * lb + t;
-      __nv_bfloat16* oh = args.out_hi + row * KEY_DIM + h * GDN_D + lane * 4;
-      __nv_bfloat16* ol = args.out_lo + row * KEY_DIM + h * GDN_D + lane * 4;
-      if (t >= len) {
-        for (int j = 0; j < 4; ++j) { oh[j] = __float2bfloat16_rn(0.f); ol[j] = __float2bfloat16_rn(0.f); }
-        continue;
+  for (int i = 0; i < n_items && !broken; ++i) {
+    float nxt_a, nxt_b;
+    load_ab(i + 1, nxt_a, nxt_b);
+    const int s = i % S, n = row_of(i);
+    uint8_t* st = stage_ptr(s);
+    float* stile = reinterpret_cast<float*>(st);
+    float* x = reinterpret_cast<float*>(st + GDN_TILE_BYTES);
+    float* hist = x + lb * 4 * GDN_D;
+    if (!named_sync_and<GDN_CONSUMERS>(mbar_wait(&full[s], (i / S) & 1, args.err, ERR_TIMEOUT_TMA))) {
+      broken = true;
+      break;
+    }
+    const int len = meta[s].len;
+    const int64_t slot = meta[s].slot;
+    if (len == 0) {
+      for (int e = tid; e < lb * GDN_D; e += GDN_CONSUMERS) {
+        const size_t row = (size_t)n * lb + e / GDN_D;
+        if (FUSED) {
+          args.out_hi[row * KEY_DIM + h * GDN_D + (e & 127)] = __float2bfloat16_rn(0.f);
+          args.out_lo[row * KEY_DIM + h * GDN_D + (e & 127)] = __float2bfloat16_rn(0.f);
+        } else {
+          args.o_raw[(row * GDN_H + h) * GDN_D + (e & 127)] = 0.f;
+        }
       }
-      const float4 o4 = reinterpret_cast<const float4*>(os + t * GDN_D)[lane];
-      const float var = warp_sum(o4.x * o4.x + o4.y * o4.y + o4.z * o4.z + o4.w * o4.w) * (1.0f / GDN_D);
-      const float r = 1.0f / sqrtf(var + args.eps);
-      const float4 z4 = *reinterpret_cast<const float4*>(args.proj + row * GDN_IN + GDN_Z_OFF + h * GDN_D + lane * 4);
-      const float y[4] = {gw.x * (o4.x * r) * silu(z4.x), gw.y * (o4.y * r) * silu(z4.y),
-                          gw.z * (o4.z * r) * silu(z4.z), gw.w * (o4.w * r) * silu(z4.w)};
+    } else {
+      // ---- prologue: q, k, v of the tokens, in place at x[t][0..2] ----
+      if (FUSED) {
+        if (tid < 3 * GDN_D) {
+          const int c3 = tid >> 7;
+          float e0 = hist[(0 * 3 + c3) * GDN_D + col], e1 = hist[(1 * 3 + c3) * GDN_D + col],
+                e2 = hist[(2 * 3 + c3) * GDN_D + col];
+          for (int t = 0; t < len; ++t) {
+            float* xp = x + (t * 4 + c3) * GDN_D + col;
+            const float xv = *xp;
+            float acc = cw.x * e0;
+            acc = fmaf(cw.y, e1, acc);
+            acc = fmaf(cw.z, e2, acc);
+            acc = fmaf(cw.w, xv, acc);
+            *xp = silu(acc);
+            e0 = e1; e1 = e2; e2 = xv;
+          }
+          float* g = args.conv_pool + (size_t)slot * CONV_KEEP * CONV_DIM + c3 * KEY_DIM + h * GDN_D + col;
+          g[0] = e0;
+          g[CONV_DIM] = e1;
+          g[2 * CONV_DIM] = e2;
+        }
+      } else {
+        // bf16 q, k, v occupy the first half of the x area: widen from the last token down
+        const __nv_bfloat16* xb = reinterpret_cast<const __nv_bfloat16*>(x);
+        for (int t = len - 1; t >= 0; --t) {
+          float v = 0.f;
+          if (tid < 3 * GDN_D) v = __bfloat162float(xb[(t * 3 + (tid >> 7)) * GDN_D + col]);
+          named_sync<GDN_CONSUMERS>();
+          if (tid < 3 * GDN_D) x[(t * 4 + (tid >> 7)) * GDN_D + col] = v;
+          named_sync<GDN_CONSUMERS>();
+        }
+      }
+      if (tid < len) {
+        const float xg = cur_a + dtb;
+        const float sp = xg > 20.f ? xg : log1pf(expf(xg));
+        gv[tid] = expf(negA * sp);
+        bv[tid] = sigmoidf_(cur_b);
+      }
+      named_sync<GDN_CONSUMERS>();
+      const float scale = 0.08838834764831845f;  // 128^-1/2, correctly rounded
+      for (int t = warp; t < len; t += GDN_CWARPS) {
+        float4* qp = reinterpret_cast<float4*>(x + (t * 4 + 0) * GDN_D) + lane;
+        float4* kp = reinterpret_cast<float4*>(x + (t * 4 + 1) * GDN_D) + lane;
+        float4 q4 = *qp, k4 = *kp;
+        const float sq = warp_sum(q4.x * q4.x + q4.y * q4.y + q4.z * q4.z + q4.w * q4.w);
+        const float sk = warp_sum(k4.x * k4.x + k4.y * k4.y + k4.z * k4.z + k4.w * k4.w);
+        const float rq = scale / sqrtf(sq + 1e-6f), rk = 1.0f / sqrtf(sk + 1e-6f);
+        q4.x *= rq; q4.y *= rq; q4.z *= rq; q4.w *= rq;
+        k4.x *= rk; k4.y *= rk; k4.z *= rk; k4.w *= rk;
+        *qp = q4;
+        *kp = k4;
+        const float d = warp_sum(q4.x * k4.x + q4.y * k4.y + q4.z * k4.z + q4.w * k4.w);
+        if (lane == 0) qk[t] = d;
+      }
+      named_sync<GDN_CONSUMERS>();
+      // ---- recurrence ----
+      float sv[32];
 #pragma unroll
-      for (int j = 0; j < 4; ++j) split_bf16(y[j], oh[j], ol[j]);
+      for (int r = 0; r < 32; ++r) sv[r] = stile[(rg * 32 + r) * GDN_D + col];
+      for (int t = 0; t < len; ++t) {
+        const float4* q4 = reinterpret_cast<const float4*>(x + (t * 4 + 0) * GDN_D + rg * 32);
+        const float4* k4 = reinterpret_cast<const float4*>(x + (t * 4 + 1) * GDN_D + rg * 32);
+        float pk0 = 0.f, pk1 = 0.f, pq0 = 0.f, pq1 = 0.f;
+#pragma unroll
+        for (int r4 = 0; r4 < 8; ++r4) {
+          const float4 kk = k4[r4], qq = q4[r4];
+          pk0 = fmaf(sv[4 * r4 + 0], kk.x, pk0); pk1 = fmaf(sv[4 * r4 + 1], kk.y, pk1);
+          pk0 = fmaf(sv[4 * r4 + 2], kk.z, pk0); pk1 = fmaf(sv[4 * r4 + 3], kk.w, pk1);
+          pq0 = fmaf(sv[4 * r4 + 0], qq.x, pq0); pq1 = fmaf(sv[4 * r4 + 1], qq.y, pq1);
+          pq0 = fmaf(sv[4 * r4 + 2], qq.z, pq0); pq1 = fmaf(sv[4 * r4 + 3], qq.w, pq1);
+        }
+        float2* rb = red + (t & 1) * GDN_RG * GDN_D;
+        rb[rg * GDN_D + col] = make_float2(pk0 + pk1, pq0 + pq1);
+        named_sync<GDN_CONSUMERS>();
+        float kvs = 0.f, qss = 0.f;
+#pragma unroll
+        for (int r = 0; r < GDN_RG; ++r) {
+          const float2 a = rb[r * GDN_D + col];
+          kvs += a.x;
+          qss += a.y;
+        }
+        const float eg = gv[t];
+        const float dl = bv[t] * (x[(t * 4 + 2) * GDN_D + col] - eg * kvs);
+        // q[t] was consumed before the barrier above: its slot now holds o[t]
+        if (rg == 0) x[(t * 4 + 0) * GDN_D + col] = fmaf(eg, qss, qk[t] * dl);
+#pragma unroll
+        for (int r4 = 0; r4 < 8; ++r4) {
+          const float4 kk = k4[r4];
+          sv[4 * r4 + 0] = fmaf(eg, sv[4 * r4 + 0], kk.x * dl);
+          sv[4 * r4 + 1] = fmaf(eg, sv[4 * r4 + 1], kk.y * dl);
+          sv[4 * r4 + 2] = fmaf(eg, sv[4 * r4 + 2], kk.z * dl);
+          sv[4 * r4 + 3] = fmaf(eg, sv[4 * r4 + 3], kk.w * dl);
+        }
+      }
+#pragma unroll
+      for (int r = 0; r < 32; ++r) stile[(rg * 32 + r) * GDN_D + col] = sv[r];
+      named_sync<GDN_CONSUMERS>();  // o[t] complete for the epilogue
+      // ---- epilogue ----
+      if (FUSED) {
+        for (int t = warp; t < lb; t += GDN_CWARPS) {
+          const size_t row = (size_t)n * lb + t;
+          __nv_bfloat16* oh = args.out_hi + row * KEY_DIM + h * GDN_D + lane * 4;
+          __nv_bfloat16* ol = args.out_lo + row * KEY_DIM + h * GDN_D + lane * 4;
+          __nv_bfloat16 hv[4], lv[4];
+          if (t >= len) {
+#pragma unroll
+            for (int j = 0; j < 4; ++j) hv[j] = lv[j] = __float2bfloat16_rn(0.f);
+          } else {
+            const float4 o4 = reinterpret_cast<const float4*>(x + (t * 4 + 0) * GDN_D)[lane];
+            const float4 z4 = reinterpret_cast<const float4*>(x + (t * 4 + 3) * GDN_D)[lane];
+            const float var = warp_sum(o4.x * o4.x + o4.y * o4.y + o4.z * o4.z + o4.w * o4.w) * (1.0f / GDN_D);
+            const float r = 1.0f / sqrtf(var + args.eps);
+            const float y[4] = {gw.x * (o4.x * r) * silu(z4.x), gw.y * (o4.y * r) * silu(z4.y),
+                                gw.z * (o4.z * r) * silu(z4.z), gw.w * (o4.w * r) * silu(z4.w)};
+#pragma unroll
+            for (int j = 0; j < 4; ++j) split_bf16(y[j], hv[j], lv[j]);
+          }
+          *reinterpret_cast<uint2*>(oh) = *reinterpret_cast<uint2*>(hv);
+          *reinterpret_cast<uint2*>(ol) = *reinterpret_cast<uint2*>(lv);
+        }
+      } else {
+        for (int e = tid; e < lb * GDN_D; e += GDN_CONSUMERS) {
+          const int t = e >> 7;
+          const size_t row = (size_t)n * lb + t;
+          args.o_raw[(row * GDN_H + h) * GDN_D + (e & 127)] = t < len ? x[(t * 4 + 0) * GDN_D + (e & 127)] : 0.f;
+        }
+      }
     }
-  } else {
-    for (int t = 0; t < lb; ++t) {
-      const size_t row = (size_t)n * lb + t;
-      args.o_raw[(row * GDN_H + h) * GDN_D + tid] = t < len ? os[t * GDN_D + tid] : 0.f;
-    }
+    fence_proxy_async();   // this thread's writes to the stage are visible to the bulk store
+    mbar_arrive(&empty[s]);
+    cur_a = nxt_a;
+    cur_b = nxt_b;
   }
 }
 

@@ -95,8 +95,17 @@ static int gemm_smem(int tn, int use_lo, int stages) {
   return stages * gemm_stage_bytes(tn, use_lo) + (2 * stages + 1) * 8 + 16 + 64 * 16 * 4 + 1024;
 }
 
-// Choose token blocking (tb blocks of tn tokens), K splits (atomic mode only) and pipeline depth so that the grid
-// fills the 148 SMs in as few waves as possible; cost ~ waves x tokens per CTA x K blocks per CTA.
+// Choose token blocking (tb blocks of tn tokens), K splits (atomic mode only) and pipeline depth. Modelled CTA time
+// in SM cycles: a fixed cost (barrier/TMEM set-up, first TMA latency) + per 64-wide K block the weight-tile load and
+// the MMAs over tn tokens (x2 with the lo operand) + the epilogue; the grid runs in ceil(CTAs / 148) waves.
+static long gemm_cost(int tiles, int KB, int tb, int tn, int splits, int kps, int mode, int use_lo) {
+  const long ctas = (long)tiles * tb * splits;
+  const long waves = (ctas + SM_COUNT - 1) / SM_COUNT;
+  const long per_kb = 256 + 2L * tn * (1 + use_lo);
+  const long epi = (long)tn * (mode == GEMM_ATOMIC ? 8 : 4);
+  return waves * (3000 + kps * per_kb + epi);
+}
+
 static GemmPlan plan_gemm(int n_w, int K, int M, int mode, int use_lo) {
   const int tiles = n_w / 128, KB = K / 64;
   GemmPlan best{0, 0, 0, 0, 0, 0};
@@ -105,16 +114,16 @@ static GemmPlan plan_gemm(int n_w, int K, int M, int mode, int use_lo) {
   for (int tb = 1; tb <= max_tb; ++tb) {
     const int tn = ((M + tb - 1) / tb + 15) / 16 * 16;
     if (tn > 256) continue;
-    int splits = 1;
-    if (mode == GEMM_ATOMIC) splits = std::max(1, std::min(KB / 2, SM_COUNT / (tiles * tb)));
-    const int kps = (KB + splits - 1) / splits;
-    splits = (KB + kps - 1) / kps;
-    const long ctas = (long)tiles * tb * splits;
-    const long waves = (ctas + SM_COUNT - 1) / SM_COUNT;
-    const long cost = waves * tn * kps;
-    if (best_cost < 0 || cost < best_cost) {
-      best_cost = cost;
-      best = {tb, tn, splits, kps, 0, 0};
+    const int max_splits = mode == GEMM_ATOMIC ? std::max(1, KB / 2) : 1;
+    for (int sp = 1; sp <= max_splits; ++sp) {
+      const int kps = (KB + sp - 1) / sp;
+      const int splits = (KB + kps - 1) / kps;
+      if (splits != sp) continue;
+      const long cost = gemm_cost(tiles, KB, tb, tn, splits, kps, mode, use_lo);
+      if (best_cost < 0 || cost < best_cost) {
+        best_cost = cost;
+        best = {tb, tn, splits, kps, 0, 0};
+      }
     }
   }
   int stages = 4;
@@ -124,9 +133,12 @@ static GemmPlan plan_gemm(int n_w, int K, int M, int mode, int use_lo) {
   return best;
 }
 
+struct hsg_engine;
+static void prof_mark(hsg_engine* e, int cls);
+
 static int launch_gemm(cudaStream_t st, const void* w, int n_w, int K, const void* xhi, const void* xlo, int m_alloc,
                        int M, int mode, float* y, int ldy, __nv_bfloat16* ahi, __nv_bfloat16* alo, int ld_act,
-                       int* err, int force_splits = 0) {
+                       int* err, int force_splits = 0, hsg_engine* prof = nullptr, int prof_cls = -1) {
   const int use_lo = xlo != nullptr;
   GemmPlan p = plan_gemm(n_w, K, M, mode, use_lo);
   if (force_splits > 0 && mode == GEMM_ATOMIC) {
@@ -154,16 +166,17 @@ static int launch_gemm(cudaStream_t st, const void* w, int n_w, int K, const voi
   a.ld_act = ld_act;
   a.err = err;
   dim3 grid(p.tb, n_w / 128, p.splits);
+  if (prof) prof_mark(prof, prof_cls);
   gemm_tc_kernel<<<grid, GEMM_THREADS, p.smem, st>>>(tw, th, tl, a);
+  if (prof) prof_mark(prof, -1);
   CU(cudaGetLastError());
   return HSG_OK;
 }
 
 static int set_kernel_attributes() {
   CU(cudaFuncSetAttribute(gemm_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_MAX));
-  CU(cudaFuncSetAttribute(gdn_step_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, gdn_smem_bytes(MAX_LB)));
-  CU(cudaFuncSetAttribute(gdn_step_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                          gdn_smem_bytes(MAX_LB)));
+  CU(cudaFuncSetAttribute(gdn_step_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, GDN_SMEM_LIMIT));
+  CU(cudaFuncSetAttribute(gdn_step_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, GDN_SMEM_LIMIT));
   CU(cudaFuncSetAttribute(ring_attn_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, attn_smem_bytes(4)));
   CU(cudaFuncSetAttribute(ring_attn_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, attn_smem_bytes(8)));
   return HSG_OK;
@@ -233,29 +246,21 @@ static int check_config(const hsg_config* c) {
 
 static bool is_attn_layer(int i) { return (i + 1) % 4 == 0; }
 
-// Record timing events around one launch when profiling; always count launches.
+// Profiling: a timing event right before (class >= 0) and right after (class -1) each kernel launch.
+static void prof_mark(hsg_engine* e, int cls) {
+  if (cls >= 0) e->launch_count++;
+  if (!e->profiling) return;
+  cudaEvent_t ev;
+  cudaEventCreate(&ev);
+  cudaEventRecord(ev, e->stream);
+  e->events.push_back(ev);
+  e->event_class.push_back(cls);
+}
+
 struct ProfScope {
   hsg_engine* e;
-  int cls;
-  ProfScope(hsg_engine* e_, int c) : e(e_), cls(c) {
-    e->launch_count++;
-    if (e->profiling) {
-      cudaEvent_t ev;
-      cudaEventCreate(&ev);
-      cudaEventRecord(ev, e->stream);
-      e->events.push_back(ev);
-      e->event_class.push_back(cls);
-    }
-  }
-  ~ProfScope() {
-    if (e->profiling) {
-      cudaEvent_t ev;
-      cudaEventCreate(&ev);
-      cudaEventRecord(ev, e->stream);
-      e->events.push_back(ev);
-      e->event_class.push_back(-1);
-    }
-  }
+  ProfScope(hsg_engine* e_, int c) : e(e_) { prof_mark(e, c); }
+  ~ProfScope() { prof_mark(e, -1); }
 };
 
 // The whole tick as a sequence of kernels on e->stream (captured into a graph, or run eagerly when profiling).
@@ -281,9 +286,8 @@ static int enqueue_step(hsg_engine* e, int nb, int lb) {
     const hsg_layer_weights& L = e->w.layers[i];
     if (!is_attn_layer(i)) {
       {
-        ProfScope ps(e, HSG_PROF_GEMM_IN);
         if ((rc = launch_gemm(st, L.w_in, GDN_IN, HIDDEN, e->xhi, lo(e->xlo), e->m_alloc, M, GEMM_STORE, e->proj,
-                              GDN_IN, nullptr, nullptr, 0, e->err)) != HSG_OK)
+                              GDN_IN, nullptr, nullptr, 0, e->err, 0, e, HSG_PROF_GEMM_IN)) != HSG_OK)
           return rc;
       }
       GdnArgs g{};
@@ -295,17 +299,17 @@ static int enqueue_step(hsg_engine* e, int nb, int lb) {
       g.A_log = L.A_log; g.dt_bias = L.dt_bias;
       g.state = e->rec + (size_t)gi * (e->S + 1) * e->rec_slot();
       g.err = e->err;
+      g.stages = gdn_stages(lb);
       {
         ProfScope ps(e, HSG_PROF_GDN);
-        gdn_step_kernel<true><<<dim3(GDN_H, nb), GDN_THREADS, gdn_smem_bytes(lb), st>>>(g);
+        gdn_step_kernel<true><<<dim3(GDN_H, std::min(nb, GDN_CTAS_PER_HEAD)), GDN_THREADS, gdn_smem_bytes(lb), st>>>(g);
         CU(cudaGetLastError());
       }
       ++gi;
     } else {
       {
-        ProfScope ps(e, HSG_PROF_GEMM_IN);
         if ((rc = launch_gemm(st, L.w_in, ATT_IN, HIDDEN, e->xhi, lo(e->xlo), e->m_alloc, M, GEMM_STORE, e->proj,
-                              ATT_IN, nullptr, nullptr, 0, e->err)) != HSG_OK)
+                              ATT_IN, nullptr, nullptr, 0, e->err, 0, e, HSG_PROF_GEMM_IN)) != HSG_OK)
           return rc;
       }
       AttnArgs a{};
@@ -341,9 +345,8 @@ static int enqueue_step(hsg_engine* e, int nb, int lb) {
       ++ai;
     }
     {
-      ProfScope ps(e, HSG_PROF_GEMM_OUT);
       if ((rc = launch_gemm(st, L.w_out, HIDDEN, KEY_DIM, e->ohi, lo(e->olo), e->m_alloc, M, GEMM_ATOMIC, e->hidden,
-                            HIDDEN, nullptr, nullptr, 0, e->err)) != HSG_OK)
+                            HIDDEN, nullptr, nullptr, 0, e->err, 0, e, HSG_PROF_GEMM_OUT)) != HSG_OK)
         return rc;
     }
     {
@@ -352,15 +355,13 @@ static int enqueue_step(hsg_engine* e, int nb, int lb) {
       CU(cudaGetLastError());
     }
     {
-      ProfScope ps(e, HSG_PROF_GEMM_GU);
       if ((rc = launch_gemm(st, L.w_gu, 2 * INTER, HIDDEN, e->xhi, lo(e->xlo), e->m_alloc, M, GEMM_SILU_MUL, nullptr,
-                            0, e->ahi, e->alo, INTER, e->err)) != HSG_OK)
+                            0, e->ahi, e->alo, INTER, e->err, 0, e, HSG_PROF_GEMM_GU)) != HSG_OK)
         return rc;
     }
     {
-      ProfScope ps(e, HSG_PROF_GEMM_DOWN);
       if ((rc = launch_gemm(st, L.w_down, HIDDEN, INTER, e->ahi, lo(e->alo), e->m_alloc, M, GEMM_ATOMIC, e->hidden,
-                            HIDDEN, nullptr, nullptr, 0, e->err)) != HSG_OK)
+                            HIDDEN, nullptr, nullptr, 0, e->err, 0, e, HSG_PROF_GEMM_DOWN)) != HSG_OK)
         return rc;
     }
     {
@@ -371,9 +372,8 @@ static int enqueue_step(hsg_engine* e, int nb, int lb) {
     }
   }
   {
-    ProfScope ps(e, HSG_PROF_HEAD_GEMM);
     if ((rc = launch_gemm(st, e->w.head_w1, N_ROLES * HEAD_E, HIDDEN, e->xhi, lo(e->xlo), e->m_alloc, M, GEMM_STORE,
-                          e->hbuf, N_ROLES * HEAD_E, nullptr, nullptr, 0, e->err)) != HSG_OK)
+                          e->hbuf, N_ROLES * HEAD_E, nullptr, nullptr, 0, e->err, 0, e, HSG_PROF_HEAD_GEMM)) != HSG_OK)
       return rc;
   }
   {
@@ -737,7 +737,9 @@ int hsg_gdn_step(const void* packed, const float* a, const float* b, const float
   g.packed = static_cast<const __nv_bfloat16*>(packed);
   g.a_raw = a; g.b_raw = b; g.o_raw = o;
   g.A_log = A_log; g.dt_bias = dt_bias; g.state = state; g.err = err;
-  gdn_step_kernel<false><<<dim3(GDN_H, n), GDN_THREADS, gdn_smem_bytes(lb), (cudaStream_t)stream>>>(g);
+  g.stages = gdn_stages(lb);
+  gdn_step_kernel<false><<<dim3(GDN_H, std::min(n, GDN_CTAS_PER_HEAD)), GDN_THREADS, gdn_smem_bytes(lb),
+                           (cudaStream_t)stream>>>(g);
   CU(cudaGetLastError());
   return HSG_OK;
 }
