@@ -50,6 +50,8 @@ constexpr int RING_COLS = WIN + 1;
 
 // ---------------------------------------------------------------------------------------------------------------
 __global__ void __launch_bounds__(256) attn_prep_kernel(const AttnArgs args) {
+  pdl_wait();
+  pdl_trigger();
   const int m = blockIdx.x;
   const int n = m / args.lb, t = m % args.lb;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -145,6 +147,8 @@ __device__ __forceinline__ float reduce_scatter(float (&v)[N], int lane) {
 // two 128-thread groups split the rows (4 each), with RB = 4 they split the keys (even / odd) and are summed at the end.
 template <int RB>
 __global__ void __launch_bounds__(ATT_THREADS, 2) ring_attn_kernel(const AttnArgs args) {
+  pdl_wait();
+  pdl_trigger();
   extern __shared__ __align__(128) uint8_t attn_smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(attn_smem_raw) + 127) & ~uintptr_t(127));
   __half* kbuf = reinterpret_cast<__half*>(smem);                 // [2][32][256]
@@ -406,6 +410,8 @@ __global__ void __launch_bounds__(ATT_THREADS, 2) ring_attn_kernel(const AttnArg
 
 // ---------------------------------------------------------------------------------------------------------------
 __global__ void __launch_bounds__(256) ring_append_kernel(const AttnArgs args) {
+  pdl_wait();
+  pdl_trigger();
   const int n = blockIdx.x, kvh = blockIdx.y;
   const int len = (int)args.lens[n];
   const int64_t slot = args.slots[n], start = args.starts[n];
@@ -422,6 +428,8 @@ __global__ void __launch_bounds__(256) ring_append_kernel(const AttnArgs args) {
 
 __global__ void ring_commit_kernel(const int64_t* slots, const int64_t* lens, const int64_t* starts, int nb, int lb,
                                    int max_slots, int64_t* ring_pos) {
+  pdl_wait();
+  pdl_trigger();
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= nb * lb) return;
   const int n = i / lb, t = i % lb;

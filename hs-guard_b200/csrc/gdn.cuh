@@ -108,20 +108,11 @@ __global__ void __launch_bounds__(GDN_THREADS, 1) gdn_step_kernel(const GdnArgs 
     // ===================================== producer =====================================
     int64_t held_slot[3] = {0, 0, 0};
     int held_len[3] = {0, 0, 0};
-    for (int i = 0; i < n_items + S; ++i) {
-      const int s = i % S, r = i / S;
-      if (r > 0 && i - S < n_items) {
-        // the consumers are done with item i - S in stage s: write its state back
-        if (!mbar_wait(&empty[s], (r - 1) & 1, args.err, ERR_TIMEOUT_TMA)) break;
-        if (lane == 0 && held_len[s] > 0) {
-          bulk_s2g(args.state + ((size_t)held_slot[s] * GDN_H + h) * (GDN_D * GDN_D), stage_ptr(s), GDN_TILE_BYTES);
-          bulk_commit();
-        }
-      }
-      if (i >= n_items) continue;
-      if (lane == 0 && r > 0) bulk_wait_read_all();  // the store has read the stage
-      __syncwarp();
-      const int n = row_of(i);
+    // Part 1 of an item's loads: metadata, expected bytes, the state tile and the conv history. These belong to this
+    // layer alone (no earlier kernel of the tick touches them), so for the first stages they are issued before the
+    // dependency wait. Part 2: the projection slices written by the preceding GEMM.
+    auto issue_state = [&](int i) {
+      const int s = i % S, n = row_of(i);
       int len = (int)args.lens[n];
       const int64_t slot = args.slots[n];
       if (len < 0 || len > lb) {
@@ -135,12 +126,10 @@ __global__ void __launch_bounds__(GDN_THREADS, 1) gdn_step_kernel(const GdnArgs 
       held_slot[s] = slot;
       held_len[s] = len;
       uint8_t* st = stage_ptr(s);
-      float* x = reinterpret_cast<float*>(st + GDN_TILE_BYTES);
-      float* hist = x + lb * 4 * GDN_D;
+      float* hist = reinterpret_cast<float*>(st + GDN_TILE_BYTES) + lb * 4 * GDN_D;
       if (lane == 0) {
         meta[s].slot = slot;
         meta[s].len = len;
-        fence_proxy_async();
         if (len > 0)
           mbar_arrive_expect_tx(&full[s], GDN_TILE_BYTES +
                                               (FUSED ? len * 4 * GDN_D * 4 + 9 * GDN_D * 4 : len * 3 * GDN_D * 2));
@@ -148,18 +137,23 @@ __global__ void __launch_bounds__(GDN_THREADS, 1) gdn_step_kernel(const GdnArgs 
           mbar_arrive(&full[s]);
       }
       __syncwarp();
-      if (len == 0) continue;
+      if (len == 0) return;
       if (lane == 0) bulk_g2s(st, args.state + ((size_t)slot * GDN_H + h) * (GDN_D * GDN_D), GDN_TILE_BYTES, &full[s]);
+      if (FUSED && lane < 9) {  // conv history: 3 rows x (q, k, v) channel blocks
+        const int rr = lane / 3, part = lane % 3;
+        const float* src = args.conv_pool + ((size_t)slot * CONV_KEEP + rr) * CONV_DIM + part * KEY_DIM + h * GDN_D;
+        bulk_g2s(hist + (rr * 3 + part) * GDN_D, src, GDN_D * 4, &full[s]);
+      }
+    };
+    auto issue_inputs = [&](int i) {
+      const int s = i % S, n = row_of(i), len = held_len[s];
+      if (len == 0) return;
+      float* x = reinterpret_cast<float*>(stage_ptr(s) + GDN_TILE_BYTES);
       if (FUSED) {
         for (int j = lane; j < len * 4; j += 32) {  // q, k, v, z slices of each token: 4 x 512 B
           const int t = j >> 2, part = j & 3;
           const float* src = args.proj + ((size_t)n * lb + t) * GDN_IN + part * KEY_DIM + h * GDN_D;
           bulk_g2s(x + (t * 4 + part) * GDN_D, src, GDN_D * 4, &full[s]);
-        }
-        if (lane < 9) {  // conv history: 3 rows x (q, k, v) channel blocks
-          const int rr = lane / 3, part = lane % 3;
-          const float* src = args.conv_pool + ((size_t)slot * CONV_KEEP + rr) * CONV_DIM + part * KEY_DIM + h * GDN_D;
-          bulk_g2s(hist + (rr * 3 + part) * GDN_D, src, GDN_D * 4, &full[s]);
         }
       } else {
         __nv_bfloat16* xb = reinterpret_cast<__nv_bfloat16*>(x);
@@ -169,6 +163,26 @@ __global__ void __launch_bounds__(GDN_THREADS, 1) gdn_step_kernel(const GdnArgs 
           bulk_g2s(xb + (t * 3 + part) * GDN_D, src, GDN_D * 2, &full[s]);
         }
       }
+    };
+    const int pre = n_items < S ? n_items : S;
+    for (int i = 0; i < pre; ++i) issue_state(i);
+    pdl_wait();
+    for (int i = 0; i < pre; ++i) issue_inputs(i);
+    for (int i = S; i < n_items + S; ++i) {
+      const int s = i % S, r = i / S;
+      if (i - S < n_items) {
+        // the consumers are done with item i - S in stage s: write its state back
+        if (!mbar_wait(&empty[s], (r - 1) & 1, args.err, ERR_TIMEOUT_TMA)) break;
+        if (lane == 0 && held_len[s] > 0) {
+          bulk_s2g(args.state + ((size_t)held_slot[s] * GDN_H + h) * (GDN_D * GDN_D), stage_ptr(s), GDN_TILE_BYTES);
+          bulk_commit();
+        }
+      }
+      if (i >= n_items) continue;
+      if (lane == 0) bulk_wait_read_all();  // the store has read the stage
+      __syncwarp();
+      issue_state(i);
+      issue_inputs(i);
     }
     if (lane == 0) bulk_wait_all();
     return;
@@ -198,6 +212,8 @@ __global__ void __launch_bounds__(GDN_THREADS, 1) gdn_step_kernel(const GdnArgs 
       b = args.b_raw[((size_t)n * lb + tid) * GDN_H + h];
     }
   };
+  pdl_wait();
+  if (tid == 0) pdl_trigger();
   float cur_a, cur_b;
   load_ab(0, cur_a, cur_b);
   bool broken = false;

@@ -8,8 +8,11 @@
 // accumulated into the same TMEM accumulator, which makes the product accurate to near fp32 against bf16 weights.
 //
 // Roles in a 128-thread CTA: thread 0 issues the TMA loads (a STAGES-deep ring of shared-memory buffers), thread 32
-// issues tcgen05.mma and commits each stage back to the producer, then all four warps drain TMEM in the epilogue
-// (warp w owns accumulator lanes 32w..32w+31 = weight rows). Every wait is bounded and reports through `err`.
+// issues tcgen05.mma and commits each stage back to the producer, then all four warps drain TMEM (warp w owns
+// accumulator lanes 32w..32w+31 = weight rows) into a shared-memory tile that one TMA bulk store (or bulk
+// reduce-add, for split-K partial sums accumulated into the fp32 residual stream) writes out. Before the dependency
+// wait of programmatic dependent launch the CTA sets up its barriers and TMEM, requests its first weight tiles and
+// asks L2 to prefetch the rest of its weight slab. Every wait is bounded and reports through `err`.
 #pragma once
 #include "common.cuh"
 
@@ -17,8 +20,8 @@ namespace hsg {
 
 enum GemmMode : int {
   GEMM_STORE = 0,     // Y[t, n] = acc                      (fp32)
-  GEMM_ATOMIC = 1,    // Y[t, n] += acc  (split-K partial sums and residual accumulation, fp32 red.add)
-  GEMM_SILU_MUL = 2,  // W rows interleaved [64 gate | 64 up] per tile: act[t, f] = silu(g) * u as a bf16 hi/lo pair
+  GEMM_ATOMIC = 1,    // Y[t, n] += acc  (TMA bulk reduce-add in L2; split-K partial sums, residual accumulation)
+  GEMM_SILU_MUL = 2,  // W rows in (gate, up) pairs: act[t, f] = silu(gate_f) * up_f as a bf16 hi/lo pair
 };
 
 struct GemmArgs {
@@ -26,14 +29,8 @@ struct GemmArgs {
   int k_blocks_total;
   int tn;                  // tokens per CTA (multiple of 16, <= 256)
   int use_lo;              // accumulate the lo half of the activation split
-  int m_store;             // token rows written by the epilogue (rows >= m_store are skipped)
   int stages;
   int mode;
-  float* y;                // GEMM_STORE / GEMM_ATOMIC output, row stride ldy
-  int ldy;
-  __nv_bfloat16* act_hi;   // GEMM_SILU_MUL output pair, row stride ld_act
-  __nv_bfloat16* act_lo;
-  int ld_act;
   int* err;
 };
 
@@ -46,9 +43,13 @@ __host__ __device__ inline int gemm_stage_bytes(int tn, int use_lo) {
 }
 
 // grid: x = token block, y = weight tile (128 rows), z = K split.
+// Output maps: STORE / ATOMIC: tm_o0 = fp32 Y [tokens][N] with a [128 x tn] box; SILU_MUL: tm_o0 / tm_o1 = bf16
+// act_hi / act_lo [tokens][N/2] with [64 x tn] boxes. The maps' row extent is the number of valid tokens, so rows
+// past it are never written.
 __global__ void __launch_bounds__(GEMM_THREADS, 1)
 gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_xhi,
-               const __grid_constant__ CUtensorMap tm_xlo, const GemmArgs args) {
+               const __grid_constant__ CUtensorMap tm_xlo, const __grid_constant__ CUtensorMap tm_o0,
+               const __grid_constant__ CUtensorMap tm_o1, const GemmArgs args) {
   extern __shared__ __align__(1024) uint8_t gemm_smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(gemm_smem_raw) + 1023) & ~uintptr_t(1023));
   const int S = args.stages;
@@ -58,16 +59,16 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__
   uint64_t* done = empty + S;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
   int* progress = reinterpret_cast<int*>(tmem_slot + 1);   // [0] loads issued, [1] stages consumed by the MMA
-  float* xchg = reinterpret_cast<float*>(tmem_slot + 4);  // 64 x 16 fp32 exchange buffer (SILU_MUL epilogue)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int tok0 = blockIdx.x * args.tn;
+  const int tn = args.tn;
+  const int tok0 = blockIdx.x * tn;
   const int wrow0 = blockIdx.y * 128;
   const int kb0 = blockIdx.z * args.k_blocks_per_split;
   const int kb1 = min(kb0 + args.k_blocks_per_split, args.k_blocks_total);
   const int nk = kb1 - kb0;
   uint32_t ncols = 32;
-  while (ncols < (uint32_t)args.tn) ncols <<= 1;
+  while (ncols < (uint32_t)tn) ncols <<= 1;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
@@ -80,6 +81,8 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__
     prefetch_tmap(&tm_w);
     prefetch_tmap(&tm_xhi);
     if (args.use_lo) prefetch_tmap(&tm_xlo);
+    prefetch_tmap(&tm_o0);
+    if (args.mode == GEMM_SILU_MUL) prefetch_tmap(&tm_o1);
   }
   if (warp == 0) tmem_alloc(tmem_slot, ncols);
   tc_fence_before();
@@ -90,31 +93,42 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__
 
   if (threadIdx.x == 0) {
     // ---- TMA producer ----
+    // Weights do not depend on the previous kernel: the first stages' weight tiles are requested and the rest of the
+    // slab is prefetched into L2 before the dependency wait, overlapping the previous kernel's tail.
     const uint32_t bytes = stage_bytes;
+    const int pre = nk < S ? nk : S;
+    for (int i = 0; i < pre; ++i) {
+      mbar_arrive_expect_tx(&full[i], bytes);
+      tma_load_2d(smem + i * stage_bytes, &tm_w, (kb0 + i) * GEMM_BK, wrow0, &full[i]);
+    }
+    for (int i = pre; i < nk; ++i) tma_prefetch_l2_2d(&tm_w, (kb0 + i) * GEMM_BK, wrow0);
+    pdl_wait();
     for (int i = 0; i < nk && ok; ++i) {
       const int s = i % S, r = i / S;
       if (r > 0) ok = mbar_wait(&empty[s], (r - 1) & 1, args.err, ERR_TIMEOUT_MMA);
       if (!ok) break;
       uint8_t* a = smem + s * stage_bytes;
       uint8_t* bh = a + GEMM_A_BYTES;
-      uint8_t* bl = bh + args.tn * GEMM_BK * 2;
+      uint8_t* bl = bh + tn * GEMM_BK * 2;
       const int kx = (kb0 + i) * GEMM_BK;
-      mbar_arrive_expect_tx(&full[s], bytes);
-      tma_load_2d(a, &tm_w, kx, wrow0, &full[s]);
+      if (i >= pre) {
+        mbar_arrive_expect_tx(&full[s], bytes);
+        tma_load_2d(a, &tm_w, kx, wrow0, &full[s]);
+      }
       tma_load_2d(bh, &tm_xhi, kx, tok0, &full[s]);
       if (args.use_lo) tma_load_2d(bl, &tm_xlo, kx, tok0, &full[s]);
       progress[0] = i + 1;
     }
   } else if (threadIdx.x == 32) {
     // ---- MMA issuer ----
-    const uint32_t idesc = idesc_bf16(128, args.tn);
+    const uint32_t idesc = idesc_bf16(128, tn);
     for (int i = 0; i < nk; ++i) {
       const int s = i % S, r = i / S;
       if (!mbar_wait(&full[s], r & 1, args.err, ERR_TIMEOUT_TMA)) { ok = false; break; }
       tc_fence_after();
       const uint32_t a = smem_u32(smem + s * stage_bytes);
       const uint32_t bh = a + GEMM_A_BYTES;
-      const uint32_t bl = bh + args.tn * GEMM_BK * 2;
+      const uint32_t bl = bh + tn * GEMM_BK * 2;
 #pragma unroll
       for (int kk = 0; kk < GEMM_BK / 16; ++kk) {
         const uint64_t da = sw128_desc(a + kk * 32);
@@ -127,59 +141,65 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__
     mma_commit(done);
   }
   __syncwarp();
-  // ---- epilogue: every warp waits for the accumulator ----
+  pdl_wait();     // the epilogue writes memory the previous kernel may still read
+  pdl_trigger();  // the next kernel may start its own set-up now
+  // ---- epilogue: TMEM -> shared-memory tile (the drained stage buffers) -> one TMA bulk store ----
   const bool have = __syncthreads_and(mbar_wait(done, 0, args.err, ERR_TIMEOUT_MMA));
   tc_fence_after();
   if (have && nk > 0) {
     const int row = warp * 32 + lane;  // accumulator lane == weight row within the tile
     const uint32_t lane_base = tmem + ((uint32_t)(warp * 32) << 16);
-    for (int c = 0; c < args.tn; c += 16) {
-      float v[16];
-      tmem_ld16(lane_base + c, v);
-      if (args.mode == GEMM_SILU_MUL) {
-        // rows 0..63 hold gate features, rows 64..127 the matching up features
-        __syncthreads();
-        if (warp >= 2) {
+    if (args.mode == GEMM_SILU_MUL) {
+      // rows (2f, 2f+1) hold (gate, up) of feature f: the pair sits in adjacent lanes
+      __nv_bfloat16* sh = reinterpret_cast<__nv_bfloat16*>(smem);  // [tn][64]
+      __nv_bfloat16* sl = sh + tn * 64;                              // [tn][64]
+      // after the exchange the even lane holds (gate, up) of even tokens, the odd lane of odd tokens
+      const int f = row >> 1, odd = lane & 1;
+      for (int c = 0; c < tn; c += 32) {
+        float v[32];
+        tmem_ld32(lane_base + c, v);
 #pragma unroll
-          for (int j = 0; j < 16; ++j) xchg[(row - 64) * 16 + j] = v[j];
-        }
-        __syncthreads();
-        if (warp < 2) {
-          const int f = blockIdx.y * 64 + row;
-#pragma unroll
-          for (int j = 0; j < 16; ++j) {
-            const int t = tok0 + c + j;
-            if (t < args.m_store) {
-              const float a = silu(v[j]) * xchg[row * 16 + j];
-              __nv_bfloat16 hi, lo;
-              split_bf16(a, hi, lo);
-              args.act_hi[(size_t)t * args.ld_act + f] = hi;
-              args.act_lo[(size_t)t * args.ld_act + f] = lo;
-            }
-          }
-        }
-      } else {
-        const int n = wrow0 + row;
-#pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          const int t = tok0 + c + j;
-          if (t < args.m_store) {
-            float* p = args.y + (size_t)t * args.ldy + n;
-            if (args.mode == GEMM_ATOMIC) atomicAdd(p, v[j]);
-            else *p = v[j];
-          }
+        for (int j = 0; j < 32; j += 2) {
+          // even lane sends v[j+1] (gate of token j+1), odd lane sends v[j] (up of token j)
+          const float other = __shfl_xor_sync(0xffffffffu, odd ? v[j] : v[j + 1], 1);
+          const float gate = odd ? other : v[j];
+          const float up = odd ? v[j + 1] : other;
+          const int tok = c + j + odd;
+          if (tok < tn) split_bf16(silu_fast(gate) * up, sh[tok * 64 + f], sl[tok * 64 + f]);
         }
       }
+    } else {
+      float* tile = reinterpret_cast<float*>(smem);  // [tn][128]
+      for (int c = 0; c < tn; c += 32) {
+        float v[32];
+        tmem_ld32(lane_base + c, v);
+#pragma unroll
+        for (int j = 0; j < 32; ++j)
+          if (c + j < tn) tile[(c + j) * 128 + row] = v[j];
+      }
     }
+    fence_proxy_async();
   }
   tc_fence_before();
   __syncthreads();
+  if (warp == 0) tmem_dealloc(tmem, ncols);
   if (threadIdx.x == 0) {
+    if (have && nk > 0) {
+      if (args.mode == GEMM_SILU_MUL) {
+        const __nv_bfloat16* sh = reinterpret_cast<const __nv_bfloat16*>(smem);
+        tma_store_2d(&tm_o0, sh, blockIdx.y * 64, tok0);
+        tma_store_2d(&tm_o1, sh + tn * 64, blockIdx.y * 64, tok0);
+      } else if (args.mode == GEMM_STORE) {
+        tma_store_2d(&tm_o0, smem, wrow0, tok0);
+      } else {
+        tma_reduce_add_2d(&tm_o0, smem, wrow0, tok0);
+      }
+      bulk_commit();
+      bulk_wait_all();
+    }
     // Error path only: loads the MMA never consumed may still be in flight; wait for them (bounded) before exit.
     for (int i = progress[1]; i < progress[0]; ++i) mbar_wait(&full[i % S], (i / S) & 1, args.err, ERR_TIMEOUT_TMA);
   }
-  __syncwarp();
-  if (warp == 0) tmem_dealloc(tmem, ncols);
 }
 
 }  // namespace hsg

@@ -16,6 +16,7 @@
 #include "gdn.cuh"
 #include "gemm.cuh"
 #include "norm.cuh"
+#include "ring_decode.cuh"
 
 using namespace hsg;
 
@@ -67,20 +68,29 @@ static int get_encoder() {
   return g_encode ? HSG_OK : HSG_ERR_CUDA;
 }
 
-// 2-D bf16 [rows][k] row-major, box [64 k][box_rows], 128-byte swizzle.
-static int make_map(CUtensorMap* map, const void* base, int rows, int k, int box_rows) {
+// 2-D row-major tensor map: `rows` x `cols` elements of `dtype`, rows `row_bytes` apart, box `box_cols` x `box_rows`.
+static int make_map_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dtype, int elem_bytes, uint64_t rows,
+                       uint64_t cols, uint64_t row_bytes, int box_cols, int box_rows, CUtensorMapSwizzle swizzle) {
   if (get_encoder() != HSG_OK) return HSG_ERR_CUDA;
-  if ((reinterpret_cast<uintptr_t>(base) & 15) || (k % 64) || box_rows < 16 || box_rows > 256)
-    return fail(HSG_ERR_INVALID, "bad tensor map (base %p, k %d, box %d)", base, k, box_rows);
-  cuuint64_t dims[2] = {(cuuint64_t)k, (cuuint64_t)rows};
-  cuuint64_t strides[1] = {(cuuint64_t)k * 2};
-  cuuint32_t box[2] = {64, (cuuint32_t)box_rows};
+  if ((reinterpret_cast<uintptr_t>(base) & 15) || (row_bytes & 15) || ((uint64_t)box_cols * elem_bytes) % 16 ||
+      box_rows < 1 || box_rows > 256 || box_cols > 256 || rows < 1)
+    return fail(HSG_ERR_INVALID, "bad tensor map (base %p, row bytes %llu, box %d x %d)", base,
+                (unsigned long long)row_bytes, box_cols, box_rows);
+  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)row_bytes};
+  cuuint32_t box[2] = {(cuuint32_t)box_cols, (cuuint32_t)box_rows};
   cuuint32_t estr[2] = {1, 1};
-  CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
-                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  CUresult r = g_encode(map, dtype, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return fail(HSG_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
   return HSG_OK;
+}
+
+// GEMM operand: bf16 [rows][k], box [64 k][box_rows], 128-byte swizzle (the tcgen05 K-major SW128 layout).
+static int make_map(CUtensorMap* map, const void* base, int rows, int k, int box_rows) {
+  if (k % 64 || box_rows < 16) return fail(HSG_ERR_INVALID, "bad operand map (k %d, box %d)", k, box_rows);
+  return make_map_2d(map, base, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, rows, k, (uint64_t)k * 2, 64, box_rows,
+                     CU_TENSOR_MAP_SWIZZLE_128B);
 }
 
 // ---- GEMM planning ----------------------------------------------------------------------------------------------
@@ -92,7 +102,7 @@ static constexpr int SM_COUNT = 148;
 static constexpr int SMEM_MAX = 227 * 1024;
 
 static int gemm_smem(int tn, int use_lo, int stages) {
-  return stages * gemm_stage_bytes(tn, use_lo) + (2 * stages + 1) * 8 + 16 + 64 * 16 * 4 + 1024;
+  return stages * gemm_stage_bytes(tn, use_lo) + (2 * stages + 1) * 8 + 16 + 1024;
 }
 
 // Choose token blocking (tb blocks of tn tokens), K splits (atomic mode only) and pipeline depth. Modelled CTA time
@@ -133,12 +143,31 @@ static GemmPlan plan_gemm(int n_w, int K, int M, int mode, int use_lo) {
   return best;
 }
 
+// Kernel launch with the programmatic-stream-serialization attribute (programmatic dependent launch): the kernel may
+// begin while its predecessor drains; every kernel calls pdl_wait() before touching memory its predecessor uses.
+template <typename... KArgs, typename... Args>
+static cudaError_t launch_k(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, bool pdl,
+                            Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kernel, args...);
+}
+
 struct hsg_engine;
 static void prof_mark(hsg_engine* e, int cls);
 
 static int launch_gemm(cudaStream_t st, const void* w, int n_w, int K, const void* xhi, const void* xlo, int m_alloc,
                        int M, int mode, float* y, int ldy, __nv_bfloat16* ahi, __nv_bfloat16* alo, int ld_act,
-                       int* err, int force_splits = 0, hsg_engine* prof = nullptr, int prof_cls = -1) {
+                       int* err, int force_splits = 0, hsg_engine* prof = nullptr, int prof_cls = -1,
+                       bool pdl = false) {
   const int use_lo = xlo != nullptr;
   GemmPlan p = plan_gemm(n_w, K, M, mode, use_lo);
   if (force_splits > 0 && mode == GEMM_ATOMIC) {
@@ -146,30 +175,36 @@ static int launch_gemm(cudaStream_t st, const void* w, int n_w, int K, const voi
     p.kps = (KB + force_splits - 1) / force_splits;
     p.splits = (KB + p.kps - 1) / p.kps;
   }
-  CUtensorMap tw, th, tl;
+  CUtensorMap tw, th, tl, t0, t1;
   int rc;
   if ((rc = make_map(&tw, w, n_w, K, 128)) != HSG_OK) return rc;
   if ((rc = make_map(&th, xhi, m_alloc, K, p.tn)) != HSG_OK) return rc;
   if ((rc = make_map(&tl, use_lo ? xlo : xhi, m_alloc, K, p.tn)) != HSG_OK) return rc;
+  if (mode == GEMM_SILU_MUL) {
+    if ((rc = make_map_2d(&t0, ahi, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, M, n_w / 2, (uint64_t)ld_act * 2, 64, p.tn,
+                          CU_TENSOR_MAP_SWIZZLE_NONE)) != HSG_OK)
+      return rc;
+    if ((rc = make_map_2d(&t1, alo, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, M, n_w / 2, (uint64_t)ld_act * 2, 64, p.tn,
+                          CU_TENSOR_MAP_SWIZZLE_NONE)) != HSG_OK)
+      return rc;
+  } else {
+    if ((rc = make_map_2d(&t0, y, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, M, n_w, (uint64_t)ldy * 4, 128, p.tn,
+                          CU_TENSOR_MAP_SWIZZLE_NONE)) != HSG_OK)
+      return rc;
+    t1 = t0;
+  }
   GemmArgs a;
   a.k_blocks_per_split = p.kps;
   a.k_blocks_total = K / 64;
   a.tn = p.tn;
   a.use_lo = use_lo;
-  a.m_store = M;
   a.stages = p.stages;
   a.mode = mode;
-  a.y = y;
-  a.ldy = ldy;
-  a.act_hi = ahi;
-  a.act_lo = alo;
-  a.ld_act = ld_act;
   a.err = err;
   dim3 grid(p.tb, n_w / 128, p.splits);
   if (prof) prof_mark(prof, prof_cls);
-  gemm_tc_kernel<<<grid, GEMM_THREADS, p.smem, st>>>(tw, th, tl, a);
+  CU(launch_k(gemm_tc_kernel, grid, dim3(GEMM_THREADS), p.smem, st, pdl, tw, th, tl, t0, t1, a));
   if (prof) prof_mark(prof, -1);
-  CU(cudaGetLastError());
   return HSG_OK;
 }
 
@@ -179,6 +214,7 @@ static int set_kernel_attributes() {
   CU(cudaFuncSetAttribute(gdn_step_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, GDN_SMEM_LIMIT));
   CU(cudaFuncSetAttribute(ring_attn_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, attn_smem_bytes(4)));
   CU(cudaFuncSetAttribute(ring_attn_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, attn_smem_bytes(8)));
+  CU(cudaFuncSetAttribute(ring_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, rd_smem_bytes()));
   return HSG_OK;
 }
 
@@ -218,6 +254,7 @@ struct hsg_engine {
   std::vector<cudaEvent_t> events;
   std::vector<int> event_class;
   bool profiling = false;
+  bool pdl = true;
   int launch_count = 0;
 
   size_t rec_slot() const { return (size_t)GDN_H * GDN_D * GDN_D; }
@@ -287,7 +324,7 @@ static int enqueue_step(hsg_engine* e, int nb, int lb) {
     if (!is_attn_layer(i)) {
       {
         if ((rc = launch_gemm(st, L.w_in, GDN_IN, HIDDEN, e->xhi, lo(e->xlo), e->m_alloc, M, GEMM_STORE, e->proj,
-                              GDN_IN, nullptr, nullptr, 0, e->err, 0, e, HSG_PROF_GEMM_IN)) != HSG_OK)
+                              GDN_IN, nullptr, nullptr, 0, e->err, 0, e, HSG_PROF_GEMM_IN, e->pdl)) != HSG_OK)
           return rc;
       }
       GdnArgs g{};
@@ -302,14 +339,14 @@ static int enqueue_step(hsg_engine* e, int nb, int lb) {
       g.stages = gdn_stages(lb);
       {
         ProfScope ps(e, HSG_PROF_GDN);
-        gdn_step_kernel<true><<<dim3(GDN_H, std::min(nb, GDN_CTAS_PER_HEAD)), GDN_THREADS, gdn_smem_bytes(lb), st>>>(g);
-        CU(cudaGetLastError());
+        CU(launch_k(gdn_step_kernel<true>, dim3(GDN_H, std::min(nb, GDN_CTAS_PER_HEAD)), dim3(GDN_THREADS),
+                    gdn_smem_bytes(lb), st, e->pdl, g));
       }
       ++gi;
     } else {
       {
         if ((rc = launch_gemm(st, L.w_in, ATT_IN, HIDDEN, e->xhi, lo(e->xlo), e->m_alloc, M, GEMM_STORE, e->proj,
-                              ATT_IN, nullptr, nullptr, 0, e->err, 0, e, HSG_PROF_GEMM_IN)) != HSG_OK)
+                              ATT_IN, nullptr, nullptr, 0, e->err, 0, e, HSG_PROF_GEMM_IN, e->pdl)) != HSG_OK)
           return rc;
       }
       AttnArgs a{};
@@ -325,67 +362,64 @@ static int enqueue_step(hsg_engine* e, int nb, int lb) {
       a.err = e->err;
       {
         ProfScope ps(e, HSG_PROF_ATTN_PREP);
-        attn_prep_kernel<<<M, 256, 0, st>>>(a);
-        CU(cudaGetLastError());
+        CU(launch_k(attn_prep_kernel, dim3(M), dim3(256), 0, st, e->pdl, a));
       }
       {
         ProfScope ps(e, HSG_PROF_RING_ATTN);
-        if (lb == 1) {
-          ring_attn_kernel<4><<<dim3(nb, ATT_HKV, 1), ATT_THREADS, attn_smem_bytes(4), st>>>(a);
-        } else {
-          ring_attn_kernel<8><<<dim3(nb, ATT_HKV, (ATT_G * lb + 7) / 8), ATT_THREADS, attn_smem_bytes(8), st>>>(a);
-        }
-        CU(cudaGetLastError());
+        if (lb == 1)
+          CU(launch_k(ring_decode_kernel, dim3(std::min(SM_COUNT, nb * ATT_HKV)), dim3(RD_THREADS), rd_smem_bytes(),
+                      st, e->pdl, a));
+        else
+          CU(launch_k(ring_attn_kernel<8>, dim3(nb, ATT_HKV, (ATT_G * lb + 7) / 8), dim3(ATT_THREADS),
+                      attn_smem_bytes(8), st, e->pdl, a));
       }
       if (lb > 1) {
         ProfScope ps(e, HSG_PROF_RING_APPEND);
-        ring_append_kernel<<<dim3(nb, ATT_HKV), ATT_D, 0, st>>>(a);
-        CU(cudaGetLastError());
+        CU(launch_k(ring_append_kernel, dim3(nb, ATT_HKV), dim3(ATT_D), 0, st, e->pdl, a));
       }
       ++ai;
     }
     {
       if ((rc = launch_gemm(st, L.w_out, HIDDEN, KEY_DIM, e->ohi, lo(e->olo), e->m_alloc, M, GEMM_ATOMIC, e->hidden,
-                            HIDDEN, nullptr, nullptr, 0, e->err, 0, e, HSG_PROF_GEMM_OUT)) != HSG_OK)
+                            HIDDEN, nullptr, nullptr, 0, e->err, 0, e, HSG_PROF_GEMM_OUT, e->pdl)) != HSG_OK)
         return rc;
     }
     {
       ProfScope ps(e, HSG_PROF_NORM);
-      resid_norm_kernel<<<M, NORM_THREADS, 0, st>>>(e->hidden, L.norm_post, eps, e->xhi, e->xlo, M);
-      CU(cudaGetLastError());
+      CU(launch_k(resid_norm_kernel, dim3(M), dim3(NORM_THREADS), 0, st, e->pdl, (const float*)e->hidden,
+                  L.norm_post, eps, e->xhi, e->xlo, M));
     }
     {
       if ((rc = launch_gemm(st, L.w_gu, 2 * INTER, HIDDEN, e->xhi, lo(e->xlo), e->m_alloc, M, GEMM_SILU_MUL, nullptr,
-                            0, e->ahi, e->alo, INTER, e->err, 0, e, HSG_PROF_GEMM_GU)) != HSG_OK)
+                            0, e->ahi, e->alo, INTER, e->err, 0, e, HSG_PROF_GEMM_GU, e->pdl)) != HSG_OK)
         return rc;
     }
     {
       if ((rc = launch_gemm(st, L.w_down, HIDDEN, INTER, e->ahi, lo(e->alo), e->m_alloc, M, GEMM_ATOMIC, e->hidden,
-                            HIDDEN, nullptr, nullptr, 0, e->err, 0, e, HSG_PROF_GEMM_DOWN)) != HSG_OK)
+                            HIDDEN, nullptr, nullptr, 0, e->err, 0, e, HSG_PROF_GEMM_DOWN, e->pdl)) != HSG_OK)
         return rc;
     }
     {
       ProfScope ps(e, HSG_PROF_NORM);
       const float* nxt = i + 1 < HSG_N_LAYERS ? e->w.layers[i + 1].norm_in : e->w.final_norm;
-      resid_norm_kernel<<<M, NORM_THREADS, 0, st>>>(e->hidden, nxt, eps, e->xhi, e->xlo, M);
-      CU(cudaGetLastError());
+      CU(launch_k(resid_norm_kernel, dim3(M), dim3(NORM_THREADS), 0, st, e->pdl, (const float*)e->hidden, nxt, eps,
+                  e->xhi, e->xlo, M));
     }
   }
   {
     if ((rc = launch_gemm(st, e->w.head_w1, N_ROLES * HEAD_E, HIDDEN, e->xhi, lo(e->xlo), e->m_alloc, M, GEMM_STORE,
-                          e->hbuf, N_ROLES * HEAD_E, nullptr, nullptr, 0, e->err, 0, e, HSG_PROF_HEAD_GEMM)) != HSG_OK)
+                          e->hbuf, N_ROLES * HEAD_E, nullptr, nullptr, 0, e->err, 0, e, HSG_PROF_HEAD_GEMM, e->pdl)) != HSG_OK)
       return rc;
   }
   {
     ProfScope ps(e, HSG_PROF_HEAD);
-    head_finish_kernel<<<M, 256, 0, st>>>(e->hbuf, e->w.head_b1, e->w.head_ln_w, e->w.head_ln_b, e->w.head_w2,
-                                          e->w.head_b2, e->cfg.head_ln_eps, e->probs, M);
-    CU(cudaGetLastError());
+    CU(launch_k(head_finish_kernel, dim3(M), dim3(256), 0, st, e->pdl, (const float*)e->hbuf, e->w.head_b1,
+                e->w.head_ln_w, e->w.head_ln_b, e->w.head_w2, e->w.head_b2, e->cfg.head_ln_eps, e->probs, M));
   }
   {
     ProfScope ps(e, HSG_PROF_COMMIT);
-    ring_commit_kernel<<<(M + 255) / 256, 256, 0, st>>>(slots, lens, starts, nb, lb, e->S, e->ring_pos);
-    CU(cudaGetLastError());
+    CU(launch_k(ring_commit_kernel, dim3((M + 255) / 256), dim3(256), 0, st, e->pdl, slots, lens, starts, nb, lb, e->S,
+                e->ring_pos));
   }
   return HSG_OK;
 }
@@ -768,7 +802,8 @@ int hsg_ring_attention(const float* q, void* ring_k, void* ring_v, const void* n
   a.scale = scale;
   a.err = err;
   cudaStream_t st = (cudaStream_t)stream;
-  if (lb == 1) ring_attn_kernel<4><<<dim3(n, ATT_HKV, 1), ATT_THREADS, attn_smem_bytes(4), st>>>(a);
+  if (lb == 1)
+    ring_decode_kernel<<<dim3(std::min(SM_COUNT, n * ATT_HKV)), RD_THREADS, rd_smem_bytes(), st>>>(a);
   else ring_attn_kernel<8><<<dim3(n, ATT_HKV, (ATT_G * lb + 7) / 8), ATT_THREADS, attn_smem_bytes(8), st>>>(a);
   CU(cudaGetLastError());
   return HSG_OK;

@@ -16,6 +16,8 @@ __global__ void __launch_bounds__(NORM_THREADS) embed_norm_kernel(const int64_t*
                                                                   int vocab, const float* w1, float eps,
                                                                   float* hidden, __nv_bfloat16* x_hi,
                                                                   __nv_bfloat16* x_lo, int m_valid, int* err) {
+  pdl_wait();
+  pdl_trigger();
   __shared__ float scratch[NORM_THREADS / 32];
   const int m = blockIdx.x, d = threadIdx.x * 4;
   float x[4] = {0.f, 0.f, 0.f, 0.f};
@@ -46,6 +48,8 @@ __global__ void __launch_bounds__(NORM_THREADS) embed_norm_kernel(const int64_t*
 __global__ void __launch_bounds__(NORM_THREADS) resid_norm_kernel(const float* hidden, const float* w1, float eps,
                                                                   __nv_bfloat16* x_hi, __nv_bfloat16* x_lo,
                                                                   int m_valid) {
+  pdl_wait();
+  pdl_trigger();
   __shared__ float scratch[NORM_THREADS / 32];
   const int m = blockIdx.x, d = threadIdx.x * 4;
   float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
@@ -68,6 +72,8 @@ __global__ void __launch_bounds__(NORM_THREADS) resid_norm_kernel(const float* h
 __global__ void __launch_bounds__(256) head_finish_kernel(const float* hbuf, const float* b1, const float* ln_w,
                                                           const float* ln_b, const float* w2, const float* b2,
                                                           float eps, float* probs, int m_valid) {
+  pdl_wait();
+  pdl_trigger();
   __shared__ float red[8][4];
   const int m = blockIdx.x, role = threadIdx.x >> 7, t = threadIdx.x & 127;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, wr = warp & 3;

@@ -171,8 +171,8 @@ def engine_layout(sd, cfg: HsgConfig = DEFAULT, device="cuda"):
     - GDN layer ``w_in``: rows [in_proj_qkv | in_proj_z | in_proj_b | in_proj_a | zero pad] (bf16, K-major),
       one GEMM per layer for the four projections of reference engine/slot_engine_v8.py:230-232.
     - attention layer ``w_in``: rows [q_proj (query|gate per head) | k_proj | v_proj].
-    - ``w_gu``: gate_proj and up_proj interleaved in 64-row groups (rows 128g..128g+63 = gate 64g..64g+63,
-      rows 128g+64.. = the matching up rows), so one 128-row GEMM tile holds both halves of silu(g)*u.
+    - ``w_gu``: gate_proj and up_proj interleaved row by row (row 2f = gate f, row 2f+1 = up f), so one 128-row
+      GEMM tile holds both halves of silu(g)*u for 64 features, each pair in adjacent accumulator lanes.
     - RMSNorm weights are stored as ``1 + w`` in fp32 (Qwen3_5RMSNorm), the gated norm as ``w``.
     - heads: ``head_w1`` [roles*512, 1024] bf16, LayerNorm and the 512->3 readout in fp32.
     """
@@ -185,7 +185,6 @@ def engine_layout(sd, cfg: HsgConfig = DEFAULT, device="cuda"):
     out = {"embed": g("backbone.embed_tokens.weight", bf),
            "final_norm": (1.0 + g("backbone.norm.weight", f32)).contiguous(),
            "inv_freq": rope_inv_freq(cfg).to(device), "layers": []}
-    half = 64
     for i, kind in enumerate(cfg.layer_types):
         p = f"backbone.layers.{i}."
         lay = {"kind": kind}
@@ -208,9 +207,7 @@ def engine_layout(sd, cfg: HsgConfig = DEFAULT, device="cuda"):
             lay["q_norm"] = (1.0 + g(a + "q_norm.weight", f32)).contiguous()
             lay["k_norm"] = (1.0 + g(a + "k_norm.weight", f32)).contiguous()
         gate, up = g(p + "mlp.gate_proj.weight", bf), g(p + "mlp.up_proj.weight", bf)
-        groups = cfg.intermediate // half
-        lay["w_gu"] = torch.stack([gate.view(groups, half, -1), up.view(groups, half, -1)], 1) \
-            .reshape(2 * cfg.intermediate, cfg.hidden).contiguous()
+        lay["w_gu"] = torch.stack([gate, up], 1).reshape(2 * cfg.intermediate, cfg.hidden).contiguous()
         lay["w_down"] = g(p + "mlp.down_proj.weight", bf)
         lay["norm_in"] = (1.0 + g(p + "input_layernorm.weight", f32)).contiguous()
         lay["norm_post"] = (1.0 + g(p + "post_attention_layernorm.weight", f32)).contiguous()

@@ -47,7 +47,8 @@ typedef struct hsg_config {
 /* Per-layer weights in the engine layout (device pointers, borrowed: they must outlive the engine).
  * GDN layers use w_in = [in_proj_qkv | in_proj_z | in_proj_b | in_proj_a | zero pad] (8320 x 1024 bf16) and
  * conv_w / A_log / dt_bias / gnorm_w; attention layers use w_in = [q_proj | k_proj | v_proj] (5120 x 1024 bf16)
- * and q_norm / k_norm. w_gu interleaves gate_proj and up_proj in 64-row groups (7168 x 1024 bf16). All RMSNorm
+ * and q_norm / k_norm. w_gu interleaves gate_proj and up_proj row by row (row 2f = gate f, row 2f+1 = up f;
+ * 7168 x 1024 bf16). All RMSNorm
  * weights are passed as fp32 (1 + w); gnorm_w is the gated norm's plain w. */
 typedef struct hsg_layer_weights {
   const void* w_in;
@@ -156,8 +157,9 @@ int hsg_ring_attention(const float* q, void* ring_k, void* ring_v, const void* n
                        int n, int lb, int max_slots, float scale, float* out, int write_ring, int* err, void* stream);
 
 /* The engine's tensor-core GEMM on its own: y[m][n] (+)= sum_k x[m][k] w[n][k] with x given as bf16 hi (and
- * optional lo) [m_alloc][k], w bf16 [n][k]; mode 0 store, 1 atomic add (with `splits` K splits), 2 SiLU-mul of
- * interleaved gate/up rows into act_hi/act_lo [m][n/2]. n % 128 == 0, k % 64 == 0, 16-byte aligned pointers. */
+ * optional lo) [m_alloc][k], w bf16 [n][k]; mode 0 store, 1 add into y (TMA bulk reduce-add, with `splits` K
+ * splits), 2 SiLU-mul of row-interleaved (gate, up) pairs into act_hi/act_lo [m][n/2]. n % 128 == 0, k % 64 == 0,
+ * 16-byte aligned pointers; y has row stride n. */
 int hsg_gemm(const void* w, int n, int k, const void* x_hi, const void* x_lo, int m, int m_alloc, float* y,
              void* act_hi, void* act_lo, int mode, int splits, int* err, void* stream);
 
