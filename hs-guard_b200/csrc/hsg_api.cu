@@ -208,6 +208,12 @@ static int launch_gemm(cudaStream_t st, const void* w, int n_w, int K, const voi
   return HSG_OK;
 }
 
+// Tensor maps of the single-token decode kernel: a [rows][256] fp16 tensor read in [64 dims x 32 rows] boxes.
+static int make_decode_map(CUtensorMap* map, const void* base, uint64_t rows) {
+  return make_map_2d(map, base, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, rows, ATT_D, ATT_D * 2, 64, RD_TILE,
+                     CU_TENSOR_MAP_SWIZZLE_128B);
+}
+
 static int set_kernel_attributes() {
   CU(cudaFuncSetAttribute(gemm_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_MAX));
   CU(cudaFuncSetAttribute(gdn_step_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, GDN_SMEM_LIMIT));
@@ -249,6 +255,8 @@ struct hsg_engine {
   int* err = nullptr;
   int* err_host = nullptr;
   std::map<std::pair<int, int>, Bucket> graphs;
+  CUtensorMap ring_maps[6][2];  // per attention layer: ring K, ring V as 2-D [rows][256] fp16, [64 x 32] SW128 boxes
+  CUtensorMap new_maps[2];      // the tick's new K, V ([rows = row*2 + head][256], 1-token ticks)
   std::vector<void*> allocations;
   // profiling
   std::vector<cudaEvent_t> events;
@@ -368,7 +376,7 @@ static int enqueue_step(hsg_engine* e, int nb, int lb) {
         ProfScope ps(e, HSG_PROF_RING_ATTN);
         if (lb == 1)
           CU(launch_k(ring_decode_kernel, dim3(std::min(SM_COUNT, nb * ATT_HKV)), dim3(RD_THREADS), rd_smem_bytes(),
-                      st, e->pdl, a));
+                      st, e->pdl, e->ring_maps[ai][0], e->ring_maps[ai][1], e->new_maps[0], e->new_maps[1], a));
         else
           CU(launch_k(ring_attn_kernel<8>, dim3(nb, ATT_HKV, (ATT_G * lb + 7) / 8), dim3(ATT_THREADS),
                       attn_smem_bytes(8), st, e->pdl, a));
@@ -540,6 +548,13 @@ int hsg_create(const hsg_config* cfg, const hsg_weights* w, int max_slots, int d
   TRY(dalloc(e, &e->hbuf, M * N_ROLES * HEAD_E));
   TRY(dalloc(e, &e->probs, (size_t)N_ROLES * M * N_CLS));
   TRY(dalloc(e, &e->err, 1));
+  for (int a = 0; a < e->n_attn; ++a) {
+    const uint64_t rows = S1 * ATT_HKV * RING_COLS;
+    TRY(make_decode_map(&e->ring_maps[a][0], e->ring_k + (size_t)a * S1 * e->ring_slot(), rows));
+    TRY(make_decode_map(&e->ring_maps[a][1], e->ring_v + (size_t)a * S1 * e->ring_slot(), rows));
+  }
+  TRY(make_decode_map(&e->new_maps[0], e->knew, M * ATT_HKV));
+  TRY(make_decode_map(&e->new_maps[1], e->vnew, M * ATT_HKV));
 #undef TRY
   if (cudaMallocHost(&e->err_host, sizeof(int)) != cudaSuccess) {
     hsg_destroy(e);
@@ -802,8 +817,15 @@ int hsg_ring_attention(const float* q, void* ring_k, void* ring_v, const void* n
   a.scale = scale;
   a.err = err;
   cudaStream_t st = (cudaStream_t)stream;
-  if (lb == 1)
-    ring_decode_kernel<<<dim3(std::min(SM_COUNT, n * ATT_HKV)), RD_THREADS, rd_smem_bytes(), st>>>(a);
+  if (lb == 1) {
+    CUtensorMap rk, rv, nk, nv;
+    const uint64_t ring_rows = ((uint64_t)max_slots + 1) * ATT_HKV * RING_COLS;
+    if ((rc = make_decode_map(&rk, ring_k, ring_rows)) != HSG_OK || (rc = make_decode_map(&rv, ring_v, ring_rows)) ||
+        (rc = make_decode_map(&nk, new_k, (uint64_t)n * ATT_HKV)) ||
+        (rc = make_decode_map(&nv, new_v, (uint64_t)n * ATT_HKV)))
+      return rc;
+    ring_decode_kernel<<<dim3(std::min(SM_COUNT, n * ATT_HKV)), RD_THREADS, rd_smem_bytes(), st>>>(rk, rv, nk, nv, a);
+  }
   else ring_attn_kernel<8><<<dim3(n, ATT_HKV, (ATT_G * lb + 7) / 8), ATT_THREADS, attn_smem_bytes(8), st>>>(a);
   CU(cudaGetLastError());
   return HSG_OK;

@@ -1,18 +1,24 @@
-// Single-token ring-window attention decode (1-token ticks), a persistent warp-specialised TMA pipeline (sm_100a).
+// Single-token ring-window attention decode (1-token ticks): a persistent, warp-specialised TMA pipeline whose score
+// and P.V products run on the tensor cores (sm_100a).
 //
 // Work item = (session row n, kv head h): the 4 query heads of group h attend over the slot's ring (up to 512 keys)
 // plus the tick's own key. Grid = one CTA per SM; items are dealt round-robin.
 //
 // Producer warp: per item it reads the slot's ring positions, lists the 32-column tiles holding any filled column
 // plus the new-key tile, publishes the list (with every key's position) in a double-buffered metadata block, then
-// streams the K tiles and after them the V tiles (16 KB fp16 each, one TMA bulk copy) through an 8-stage ring.
-// Consumer warps (8): pass 1 scores every listed key (warp w takes keys 4w..4w+3 of a tile; lanes split the 256 dims,
-// a warp reduce-scatter finishes the 16 dot products), masked by the window rule 0 <= kpos <= qpos, kpos > qpos - 512;
-// one softmax per query row over all scores (fp32); pass 2 accumulates P.V (thread t: dims 2*(t%128), +1, keys of
-// parity t/128). Stages are released by mbarrier arrivals, so no block-wide barrier sits inside the tile loops.
-// Output: out * sigmoid(gate) as the o_proj operand (bf16 hi/lo). Then the new key/value are written into ring
-// column start % 512 (the position there, start - 512, is outside this query's window).
-// Same contract and results as ring_attn_kernel<4> (reference engine/fused_kernels.py:288-376 for Lb = 1).
+// streams the K tiles and after them the V tiles through an 8-stage ring. A tile is 32 keys x 256 dims fp16 (16 KB),
+// loaded as four [32 x 64] boxes by 2-D TMA with 128-byte swizzle, so the tensor-core fragment loads below are free
+// of shared-memory bank conflicts.
+// Consumer warps (8) -- warp-level MMA (mma.sync m16n8k16, fp16 in, fp32 accumulate); the 4 query rows sit in an
+// 8-row operand whose other rows are zero:
+//   pass 1: S^T[keys x rows] = K_tile[keys x dims] Q^T; warp w takes key half w & 1 and dims 64(w>>1)..+63, and adds
+//           its partial dot products into its own slice of a score buffer (no barrier per tile);
+//   softmax: per query row over all listed keys, masked by 0 <= kpos <= qpos, kpos > qpos - 512 (fp32);
+//   pass 2: O^T[dims x rows] += V_tile^T[dims x keys] P^T; warp w owns dims 32w..32w+31.
+// Stages are released by mbarrier arrivals. Output: out * sigmoid(gate) as the o_proj operand (bf16 hi/lo), or the
+// ungated fp32 output for the isolated kernel; then the new key/value are written into ring column start % 512 (the
+// position held there, start - 512, is outside this query's window).
+// Same contract as ring_attn_kernel (reference engine/fused_kernels.py:288-376 for Lb = 1).
 #pragma once
 #include "attn.cuh"
 
@@ -22,11 +28,13 @@ constexpr int RD_CONS = 256;                     // consumer threads
 constexpr int RD_THREADS = RD_CONS + 32;         // + producer warp
 constexpr int RD_TILE = 32;                      // keys per tile
 constexpr int RD_TILE_BYTES = RD_TILE * ATT_D * 2;
+constexpr int RD_SUB_BYTES = RD_TILE * 64 * 2;   // one [32 keys x 64 dims] swizzled box
 constexpr int RD_STAGES = 8;
 constexpr int RD_MAXT = WIN / RD_TILE + 1;       // 16 ring tiles + the new-key tile
 constexpr int RD_MAXK = RD_MAXT * RD_TILE;
+constexpr int RD_PSTRIDE = RD_MAXK + 8;          // fp16 probabilities row stride (bank-spread)
 
-struct alignas(16) RdMeta {  // 16-byte multiple: the score array after the two copies stays float4-aligned
+struct alignas(16) RdMeta {
   int64_t qpos;
   int len, ntile;
   int tile[RD_MAXT];      // ring tile index, or -1 for the new-key tile
@@ -34,23 +42,54 @@ struct alignas(16) RdMeta {  // 16-byte multiple: the score array after the two 
 };
 
 __host__ __device__ inline int rd_smem_bytes() {
-  // stages | meta x2 | scores [MAXK][4] | partial acc [4][256] | row sums [4] | barriers (8 full, 8 empty, 2+2 meta)
-  return RD_STAGES * RD_TILE_BYTES + 2 * (int)sizeof(RdMeta) + RD_MAXK * 4 * 4 + 4 * ATT_D * 4 + 16 +
-         (2 * RD_STAGES + 4) * 8 + 128;
+  // stages | meta x2 | partial scores [4][MAXK][4] f32 | probabilities [4][PSTRIDE] f16 | row sums [4] | barriers
+  return RD_STAGES * RD_TILE_BYTES + 2 * (int)sizeof(RdMeta) + 4 * RD_MAXK * 4 * 4 + 4 * RD_PSTRIDE * 2 + 16 +
+         (2 * RD_STAGES + 4) * 8 + 1024;
 }
 
-__global__ void __launch_bounds__(RD_THREADS, 1) ring_decode_kernel(const AttnArgs args) {
-  extern __shared__ __align__(128) uint8_t rd_smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(rd_smem_raw) + 127) & ~uintptr_t(127));
-  __half* stages = reinterpret_cast<__half*>(smem);
+// byte offset of (key r, 16-byte chunk c) inside a [32 x 64] fp16 box written with 128-byte swizzle
+__device__ __forceinline__ uint32_t sw128_off(int r, int c) { return r * 128 + ((c ^ (r & 7)) << 4); }
+
+__device__ __forceinline__ void ldmatrix_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+__device__ __forceinline__ void ldmatrix_x4_trans(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2,
+                                                  uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+// D[16x8] += A[16x16] B[16x8], fp16 inputs, fp32 accumulate
+__device__ __forceinline__ void mma_f16_16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                              uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ uint32_t pack_half2(float a, float b) {
+  __half2 h = __floats2half2_rn(a, b);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+
+// tm_rk / tm_rv: this layer's ring K / V as 2-D [rows = (slot*2 + head)*513 + column][256] fp16;
+// tm_nk / tm_nv: the tick's new keys / values as [rows = row*2 + head][256] fp16. All with [64 x 32] boxes, SW128.
+__global__ void __launch_bounds__(RD_THREADS, 1)
+ring_decode_kernel(const __grid_constant__ CUtensorMap tm_rk, const __grid_constant__ CUtensorMap tm_rv,
+                   const __grid_constant__ CUtensorMap tm_nk, const __grid_constant__ CUtensorMap tm_nv,
+                   const AttnArgs args) {
+  extern __shared__ __align__(1024) uint8_t rd_smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(rd_smem_raw) + 1023) & ~uintptr_t(1023));
   RdMeta* meta = reinterpret_cast<RdMeta*>(smem + RD_STAGES * RD_TILE_BYTES);
-  float* sc = reinterpret_cast<float*>(meta + 2);            // [MAXK][4]
-  float* xacc = sc + RD_MAXK * 4;                            // [4][256]
-  float* lsum = xacc + 4 * ATT_D;                            // [4]
-  uint64_t* full = reinterpret_cast<uint64_t*>(lsum + 4);    // [8]
-  uint64_t* empty = full + RD_STAGES;                        // [8]
-  uint64_t* meta_full = empty + RD_STAGES;                   // [2]
-  uint64_t* meta_free = meta_full + 2;                       // [2]
+  float* scp = reinterpret_cast<float*>(meta + 2);             // [4 dim ranges][MAXK][4 rows] partial scores
+  __half* pr = reinterpret_cast<__half*>(scp + 4 * RD_MAXK * 4);  // [4 rows][PSTRIDE] probabilities
+  float* lsum = reinterpret_cast<float*>(pr + 4 * RD_PSTRIDE);    // [4]
+  uint64_t* full = reinterpret_cast<uint64_t*>(lsum + 4);       // [8]
+  uint64_t* empty = full + RD_STAGES;                           // [8]
+  uint64_t* meta_full = empty + RD_STAGES;                      // [2]
+  uint64_t* meta_free = meta_full + 2;                          // [2]
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int n_items = args.nb * ATT_HKV;
@@ -64,6 +103,10 @@ __global__ void __launch_bounds__(RD_THREADS, 1) ring_decode_kernel(const AttnAr
       mbar_init(&meta_free[b], RD_CONS);
     }
     fence_barrier_init();
+    prefetch_tmap(&tm_rk);
+    prefetch_tmap(&tm_rv);
+    prefetch_tmap(&tm_nk);
+    prefetch_tmap(&tm_nv);
   }
   __syncthreads();
   pdl_wait();
@@ -107,8 +150,8 @@ __global__ void __launch_bounds__(RD_THREADS, 1) ring_decode_kernel(const AttnAr
           if (!(lane & 1)) m.tile[pos] = lane >> 1;
         }
         nt = __popc(even_on);
-        // the tick's own key(s): the new-key tile
-        if (lane < RD_TILE) m.kpos[nt * RD_TILE + lane] = lane < len ? (int)(start + lane) : -1;
+        // the tick's own key: the new-key tile (its other 31 columns are never visible)
+        m.kpos[nt * RD_TILE + lane] = lane < len ? (int)(start + lane) : -1;
         if (lane == 0) m.tile[nt] = -1;
         ++nt;
       }
@@ -121,21 +164,23 @@ __global__ void __launch_bounds__(RD_THREADS, 1) ring_decode_kernel(const AttnAr
       }
       __syncwarp();
       if (len == 0) continue;
-      const size_t head = ((size_t)slot * ATT_HKV + h) * RING_COLS * ATT_D;
-      const size_t nhead = ((size_t)n * ATT_HKV + h) * ATT_D;  // lb == 1: one new row per (row, head)
+      const int ring_row = (int)((slot * ATT_HKV + h) * RING_COLS);
+      const int new_row = n * ATT_HKV + h;
       for (int pass = 0; pass < 2; ++pass) {
-        const __half* ring = pass == 0 ? args.ring_k : args.ring_v;
-        const __half* fresh = pass == 0 ? args.knew : args.vnew;
+        const CUtensorMap* ring = pass == 0 ? &tm_rk : &tm_rv;
+        const CUtensorMap* fresh = pass == 0 ? &tm_nk : &tm_nv;
         for (int t = 0; t < nt; ++t, ++cnt) {
           const int s = cnt % RD_STAGES;
           if (cnt >= RD_STAGES && !mbar_wait(&empty[s], ((cnt / RD_STAGES) - 1) & 1, args.err, ERR_TIMEOUT_TMA))
             return;
           if (lane == 0) {
             const int tile = m.tile[t];
-            const uint32_t bytes = tile >= 0 ? RD_TILE_BYTES : ATT_D * 2;
-            const __half* src = tile >= 0 ? ring + head + (size_t)tile * RD_TILE * ATT_D : fresh + nhead;
-            mbar_arrive_expect_tx(&full[s], bytes);
-            bulk_g2s(stages + (size_t)s * RD_TILE * ATT_D, src, bytes, &full[s]);
+            const CUtensorMap* map = tile >= 0 ? ring : fresh;
+            const int y = tile >= 0 ? ring_row + tile * RD_TILE : new_row;
+            uint8_t* dst = smem + (size_t)s * RD_TILE_BYTES;
+            mbar_arrive_expect_tx(&full[s], RD_TILE_BYTES);
+#pragma unroll
+            for (int q = 0; q < 4; ++q) tma_load_2d(dst + q * RD_SUB_BYTES, map, q * 64, y, &full[s]);
           }
           __syncwarp();
         }
@@ -145,7 +190,8 @@ __global__ void __launch_bounds__(RD_THREADS, 1) ring_decode_kernel(const AttnAr
   }
 
   // ===================================== consumers =====================================
-  const int dp = tid & 127, par = tid >> 7;
+  const int g = lane >> 2, c4 = lane & 3;     // mma fragment coordinates
+  const int kh = warp & 1, kr = warp >> 1;    // pass 1: key half of the tile, dim range
   int cnt = 0, k = 0;
   bool ok = true;
   for (int j = blockIdx.x; j < n_items && ok; j += gridDim.x, ++k) {
@@ -168,137 +214,129 @@ __global__ void __launch_bounds__(RD_THREADS, 1) ring_decode_kernel(const AttnAr
       mbar_arrive(&meta_free[b]);
       continue;
     }
-    // queries: lane holds dims 8*lane..+7 of the 4 rows of group h
-    float q[ATT_G][8];
+    // pass-1 B fragments: Q^T for this warp's 64 dims (4 k-steps); query row = fragment column g (rows >= 4 zero)
+    uint32_t qb[4][2];
+    {
+      const float* qrow = args.qbuf + (((size_t)n * ATT_HKV + h) * ATT_G + (g & 3)) * ATT_D + kr * 64;
 #pragma unroll
-    for (int r = 0; r < ATT_G; ++r) {
-      const float* src = args.qbuf + (((size_t)n * ATT_HKV + h) * ATT_G + r) * ATT_D + lane * 8;
-      const float4 a = reinterpret_cast<const float4*>(src)[0], c = reinterpret_cast<const float4*>(src)[1];
-      q[r][0] = a.x; q[r][1] = a.y; q[r][2] = a.z; q[r][3] = a.w;
-      q[r][4] = c.x; q[r][5] = c.y; q[r][6] = c.z; q[r][7] = c.w;
+      for (int ks = 0; ks < 4; ++ks) {
+        const float2 lo2 = *reinterpret_cast<const float2*>(qrow + ks * 16 + 2 * c4);
+        const float2 hi2 = *reinterpret_cast<const float2*>(qrow + ks * 16 + 8 + 2 * c4);
+        qb[ks][0] = g < ATT_G ? pack_half2(lo2.x, lo2.y) : 0u;
+        qb[ks][1] = g < ATT_G ? pack_half2(hi2.x, hi2.y) : 0u;
+      }
     }
-    // ---- pass 1: scores ----
+    float* sp = scp + (size_t)kr * RD_MAXK * 4;
+    // ---- pass 1: partial scores over this warp's dim range ----
     for (int t = 0; t < nt && ok; ++t, ++cnt) {
       const int s = cnt % RD_STAGES;
       if (!mbar_wait(&full[s], (cnt / RD_STAGES) & 1, args.err, ERR_TIMEOUT_TMA)) { ok = false; break; }
-      const __half* kt = stages + (size_t)s * RD_TILE * ATT_D;
-      const int ncols = m.tile[t] >= 0 ? RD_TILE : 1;
-      float part[4 * ATT_G];
+      const uint32_t sub = smem_u32(smem + (size_t)s * RD_TILE_BYTES + kr * RD_SUB_BYTES);
+      float d[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-      for (int kk = 0; kk < 4; ++kk) {
-        const int c = warp * 4 + kk;
-        float kf[8];
-        if (c < ncols) {
-          const uint4 raw = *reinterpret_cast<const uint4*>(kt + c * ATT_D + lane * 8);
-          const __half2* h2 = reinterpret_cast<const __half2*>(&raw);
-#pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            const float2 f = __half22float2(h2[i]);
-            kf[2 * i] = f.x; kf[2 * i + 1] = f.y;
-          }
-        } else {
-#pragma unroll
-          for (int i = 0; i < 8; ++i) kf[i] = 0.f;
-        }
-#pragma unroll
-        for (int r = 0; r < ATT_G; ++r) {
-          float d = 0.f;
-#pragma unroll
-          for (int i = 0; i < 8; ++i) d = fmaf(q[r][i], kf[i], d);
-          part[kk * ATT_G + r] = d;
-        }
+      for (int ks = 0; ks < 4; ++ks) {
+        // A = K[keys 16kh..+15][dims 16ks..+15]: matrix mi = lane/8 -> key +8*(mi&1), chunk +(mi>>1)
+        const int mi = lane >> 3, r = 16 * kh + (mi & 1) * 8 + (lane & 7), ch = 2 * ks + (mi >> 1);
+        uint32_t a0, a1, a2, a3;
+        ldmatrix_x4(sub + sw128_off(r, ch), a0, a1, a2, a3);
+        mma_f16_16816(d, a0, a1, a2, a3, qb[ks][0], qb[ks][1]);
       }
-      mbar_arrive(&empty[s]);  // the K tile has been read
-      const float sres = reduce_scatter<4 * ATT_G>(part, lane);
-      const int idx = lane >> 1, kk = idx / ATT_G, r = idx % ATT_G;
-      const int c = warp * 4 + kk;
-      const int kp = m.kpos[t * RD_TILE + c];
-      const bool vis = c < ncols && kp >= 0 && kp <= qpos && kp > qpos - WIN;
-      if (!(lane & 1)) sc[(t * RD_TILE + c) * 4 + r] = vis ? sres * args.scale : -INFINITY;
+      mbar_arrive(&empty[s]);  // this warp has read the K tile
+      if (c4 < 2) {             // fragment columns 2*c4, +1 are query rows 0..3
+        const int key = t * RD_TILE + 16 * kh + g;
+        *reinterpret_cast<float2*>(sp + key * 4 + 2 * c4) = make_float2(d[0], d[1]);
+        *reinterpret_cast<float2*>(sp + (key + 8) * 4 + 2 * c4) = make_float2(d[2], d[3]);
+      }
     }
     if (!named_sync_and<RD_CONS>(ok)) break;
-    // ---- softmax per query row (warp r) ----
+    // ---- softmax per query row (warp r): sum the four dim ranges, mask, normalise ----
     if (warp < ATT_G) {
       const int r = warp, nk = nt * RD_TILE;
       float mx = -INFINITY;
-      for (int c = lane; c < nk; c += 32) mx = fmaxf(mx, sc[c * 4 + r]);
+      for (int c = lane; c < nk; c += 32) {
+        const int kp = m.kpos[c];
+        float sc = -INFINITY;
+        if (kp >= 0 && kp <= qpos && kp > qpos - WIN)
+          sc = (scp[c * 4 + r] + scp[(RD_MAXK + c) * 4 + r] + scp[(2 * RD_MAXK + c) * 4 + r] +
+                scp[(3 * RD_MAXK + c) * 4 + r]) * args.scale;
+        scp[c * 4 + r] = sc;
+        mx = fmaxf(mx, sc);
+      }
       mx = warp_max(mx);
       const float msafe = mx == -INFINITY ? 0.f : mx;
       float sum = 0.f;
       for (int c = lane; c < nk; c += 32) {
-        const float p = expf(sc[c * 4 + r] - msafe);
-        sc[c * 4 + r] = p;
+        const float p = expf(scp[c * 4 + r] - msafe);
+        pr[r * RD_PSTRIDE + c] = __float2half_rn(p);
         sum += p;
       }
       sum = warp_sum(sum);
       if (lane == 0) lsum[r] = sum;
     }
     named_sync<RD_CONS>();
-    // ---- pass 2: P.V ----
-    float acc[ATT_G][2];
+    // ---- pass 2: O^T[dims 32w..32w+31] += V^T P^T ----
+    float o[2][4];
 #pragma unroll
-    for (int r = 0; r < ATT_G; ++r) acc[r][0] = acc[r][1] = 0.f;
+    for (int mb = 0; mb < 2; ++mb) o[mb][0] = o[mb][1] = o[mb][2] = o[mb][3] = 0.f;
+    const int dsub = warp >> 1;              // the 64-dim box holding dims 32w..32w+31
+    const int cbase = (warp & 1) * 4;        // first 16-byte chunk of those dims inside the box
     for (int t = 0; t < nt && ok; ++t, ++cnt) {
       const int s = cnt % RD_STAGES;
       if (!mbar_wait(&full[s], (cnt / RD_STAGES) & 1, args.err, ERR_TIMEOUT_TMA)) { ok = false; break; }
-      const __half* vt = stages + (size_t)s * RD_TILE * ATT_D;
-      const int ncols = m.tile[t] >= 0 ? RD_TILE : 1;
-      for (int c = par; c < ncols; c += 2) {
-        const float2 vf = __half22float2(reinterpret_cast<const __half2*>(vt + c * ATT_D)[dp]);
-        const float4 p = *reinterpret_cast<const float4*>(sc + (t * RD_TILE + c) * 4);
-        acc[0][0] = fmaf(p.x, vf.x, acc[0][0]); acc[0][1] = fmaf(p.x, vf.y, acc[0][1]);
-        acc[1][0] = fmaf(p.y, vf.x, acc[1][0]); acc[1][1] = fmaf(p.y, vf.y, acc[1][1]);
-        acc[2][0] = fmaf(p.z, vf.x, acc[2][0]); acc[2][1] = fmaf(p.z, vf.y, acc[2][1]);
-        acc[3][0] = fmaf(p.w, vf.x, acc[3][0]); acc[3][1] = fmaf(p.w, vf.y, acc[3][1]);
+      const uint32_t sub = smem_u32(smem + (size_t)s * RD_TILE_BYTES + dsub * RD_SUB_BYTES);
+#pragma unroll
+      for (int ks = 0; ks < 2; ++ks) {   // 16 keys per k-step
+        // B = P^T[keys][rows]: fragment column g = query row (rows >= 4 zero)
+        const int kc = t * RD_TILE + 16 * ks + 2 * c4;
+        const uint32_t b0 = g < ATT_G ? *reinterpret_cast<const uint32_t*>(pr + (g & 3) * RD_PSTRIDE + kc) : 0u;
+        const uint32_t b1 = g < ATT_G ? *reinterpret_cast<const uint32_t*>(pr + (g & 3) * RD_PSTRIDE + kc + 8) : 0u;
+#pragma unroll
+        for (int mb = 0; mb < 2; ++mb) {
+          // A = V^T[dims 16mb..+15][keys 16ks..+15] via transposed loads of the stored [key][dim] blocks:
+          // matrix mi: keys +8*(mi>>1), dim chunk +(mi&1)
+          const int mi = lane >> 3, r = 16 * ks + (mi >> 1) * 8 + (lane & 7), ch = cbase + 2 * mb + (mi & 1);
+          uint32_t a0, a1, a2, a3;
+          ldmatrix_x4_trans(sub + sw128_off(r, ch), a0, a1, a2, a3);
+          mma_f16_16816(o[mb], a0, a1, a2, a3, b0, b1);
+        }
       }
       mbar_arrive(&empty[s]);
     }
-    if (par == 1) {
+    if (!named_sync_and<RD_CONS>(ok)) break;
+    // ---- output: lanes with c4 < 2 hold query rows 2*c4, 2*c4+1 for dims 32w + 16mb + g (+8) ----
+    if (c4 < 2) {
 #pragma unroll
-      for (int r = 0; r < ATT_G; ++r) {
-        xacc[r * ATT_D + 2 * dp] = acc[r][0];
-        xacc[r * ATT_D + 2 * dp + 1] = acc[r][1];
+      for (int mb = 0; mb < 2; ++mb) {
+#pragma unroll
+        for (int half = 0; half < 2; ++half) {
+          const int dim = 32 * warp + 16 * mb + g + 8 * half;
+#pragma unroll
+          for (int cc = 0; cc < 2; ++cc) {
+            const int r = 2 * c4 + cc;
+            const float l = lsum[r];
+            const float val = l > 0.f ? o[mb][2 * half + cc] / l : 0.f;
+            if (args.out_raw) {
+              args.out_raw[(((size_t)n * ATT_HKV + h) * ATT_G + r) * ATT_D + dim] = val;
+            } else {
+              const int jq = h * ATT_G + r;
+              const float gate = args.proj[(size_t)n * ATT_IN + jq * 2 * ATT_D + ATT_D + dim];
+              split_bf16(val * sigmoidf_(gate), ohi[r * ATT_D + dim], olo[r * ATT_D + dim]);
+            }
+          }
+        }
       }
     }
-    if (!named_sync_and<RD_CONS>(ok)) break;
-    if (par == 0 && args.out_raw) {
-      // isolated kernel: ungated fp32 output [n][2][4][256]
-#pragma unroll
-      for (int r = 0; r < ATT_G; ++r) {
-        const float l = lsum[r];
-        const float inv = l > 0.f ? 1.0f / l : 0.f;
-        float* o = args.out_raw + (((size_t)n * ATT_HKV + h) * ATT_G + r) * ATT_D + 2 * dp;
-        o[0] = (acc[r][0] + xacc[r * ATT_D + 2 * dp]) * inv;
-        o[1] = (acc[r][1] + xacc[r * ATT_D + 2 * dp + 1]) * inv;
-      }
-    } else if (par == 0) {
-      const float* gate_row = args.proj + (size_t)n * ATT_IN;
-#pragma unroll
-      for (int r = 0; r < ATT_G; ++r) {
-        const int jq = h * ATT_G + r;
-        const float l = lsum[r];
-        const float inv = l > 0.f ? 1.0f / l : 0.f;
-        const float a0 = (acc[r][0] + xacc[r * ATT_D + 2 * dp]) * inv;
-        const float a1 = (acc[r][1] + xacc[r * ATT_D + 2 * dp + 1]) * inv;
-        const float* g = gate_row + jq * 2 * ATT_D + ATT_D + 2 * dp;
-        const float y0 = a0 * sigmoidf_(g[0]), y1 = a1 * sigmoidf_(g[1]);
-        __nv_bfloat16 hv[2], lv[2];
-        split_bf16(y0, hv[0], lv[0]);
-        split_bf16(y1, hv[1], lv[1]);
-        *reinterpret_cast<__nv_bfloat162*>(ohi + r * ATT_D + 2 * dp) = *reinterpret_cast<__nv_bfloat162*>(hv);
-        *reinterpret_cast<__nv_bfloat162*>(olo + r * ATT_D + 2 * dp) = *reinterpret_cast<__nv_bfloat162*>(lv);
-      }
-    } else if (args.write_ring) {
-      // par 1 threads: the new key/value go into ring column start % 512 (every copy of this item has landed)
+    if (args.write_ring && tid < ATT_D / 2) {
+      // the new key/value go into ring column start % 512 (every copy of this item has landed)
       const int64_t slot = args.slots[n];
       const size_t col = (size_t)(qpos % WIN);
-      const size_t dst = (((size_t)slot * ATT_HKV + h) * RING_COLS + col) * ATT_D + 2 * dp;
-      const size_t src = ((size_t)n * ATT_HKV + h) * ATT_D + 2 * dp;
+      const size_t dst = (((size_t)slot * ATT_HKV + h) * RING_COLS + col) * ATT_D + 2 * tid;
+      const size_t src = ((size_t)n * ATT_HKV + h) * ATT_D + 2 * tid;
       *reinterpret_cast<__half2*>(args.ring_k + dst) = *reinterpret_cast<const __half2*>(args.knew + src);
       *reinterpret_cast<__half2*>(args.ring_v + dst) = *reinterpret_cast<const __half2*>(args.vnew + src);
     }
     mbar_arrive(&meta_free[b]);
-    named_sync<RD_CONS>();  // scores and partial sums are reused by the next item
+    named_sync<RD_CONS>();  // scores and probabilities are reused by the next item
   }
 }
 
