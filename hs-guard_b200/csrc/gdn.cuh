@@ -201,8 +201,7 @@ __global__ void __launch_bounds__(GDN_THREADS, 1) gdn_step_kernel(const GdnArgs 
     a = 0.f;
     b = 0.f;
     if (i >= n_items || tid >= lb) return;
-    const int n = row_of(i);
-    if (tid >= args.lens[n]) return;
+    const int n = row_of(i);  // padded tokens' values are loaded too (in bounds) and never used
     if (FUSED) {
       const float* row = args.proj + ((size_t)n * lb + tid) * GDN_IN;
       a = row[GDN_A_OFF + h];
@@ -281,28 +280,26 @@ __global__ void __launch_bounds__(GDN_THREADS, 1) gdn_step_kernel(const GdnArgs 
         gv[tid] = expf(negA * sp);
         bv[tid] = sigmoidf_(cur_b);
       }
-      named_sync<GDN_CONSUMERS>();
-      const float scale = 0.08838834764831845f;  // 128^-1/2, correctly rounded
-      for (int t = warp; t < len; t += GDN_CWARPS) {
-        float4* qp = reinterpret_cast<float4*>(x + (t * 4 + 0) * GDN_D) + lane;
-        float4* kp = reinterpret_cast<float4*>(x + (t * 4 + 1) * GDN_D) + lane;
-        float4 q4 = *qp, k4 = *kp;
-        const float sq = warp_sum(q4.x * q4.x + q4.y * q4.y + q4.z * q4.z + q4.w * q4.w);
-        const float sk = warp_sum(k4.x * k4.x + k4.y * k4.y + k4.z * k4.z + k4.w * k4.w);
-        const float rq = scale / sqrtf(sq + 1e-6f), rk = 1.0f / sqrtf(sk + 1e-6f);
-        q4.x *= rq; q4.y *= rq; q4.z *= rq; q4.w *= rq;
-        k4.x *= rk; k4.y *= rk; k4.z *= rk; k4.w *= rk;
-        *qp = q4;
-        *kp = k4;
-        const float d = warp_sum(q4.x * k4.x + q4.y * k4.y + q4.z * k4.z + q4.w * k4.w);
-        if (lane == 0) qk[t] = d;
-      }
-      named_sync<GDN_CONSUMERS>();
+      named_sync<GDN_CONSUMERS>();  // conv outputs, decay and beta of every token are in shared memory
       // ---- recurrence ----
       float sv[32];
 #pragma unroll
       for (int r = 0; r < 32; ++r) sv[r] = stile[(rg * 32 + r) * GDN_D + col];
+      const float scale = 0.08838834764831845f;  // 128^-1/2, correctly rounded
       for (int t = 0; t < len; ++t) {
+        // L2 norms (eps 1e-6) and q.k of token t, computed by every warp from the raw conv outputs (no barrier);
+        // the normalisation is folded into the dot products and the update below
+        float rq, rk, dqk;
+        {
+          const float4 qa = reinterpret_cast<const float4*>(x + (t * 4 + 0) * GDN_D)[lane];
+          const float4 ka = reinterpret_cast<const float4*>(x + (t * 4 + 1) * GDN_D)[lane];
+          const float sq = warp_sum(qa.x * qa.x + qa.y * qa.y + qa.z * qa.z + qa.w * qa.w);
+          const float sk = warp_sum(ka.x * ka.x + ka.y * ka.y + ka.z * ka.z + ka.w * ka.w);
+          const float sqk = warp_sum(qa.x * ka.x + qa.y * ka.y + qa.z * ka.z + qa.w * ka.w);
+          rq = scale / sqrtf(sq + 1e-6f);
+          rk = 1.0f / sqrtf(sk + 1e-6f);
+          dqk = sqk * rq * rk;
+        }
         const float4* q4 = reinterpret_cast<const float4*>(x + (t * 4 + 0) * GDN_D + rg * 32);
         const float4* k4 = reinterpret_cast<const float4*>(x + (t * 4 + 1) * GDN_D + rg * 32);
         float pk0 = 0.f, pk1 = 0.f, pq0 = 0.f, pq1 = 0.f;
@@ -315,7 +312,7 @@ __global__ void __launch_bounds__(GDN_THREADS, 1) gdn_step_kernel(const GdnArgs 
           pq0 = fmaf(sv[4 * r4 + 2], qq.z, pq0); pq1 = fmaf(sv[4 * r4 + 3], qq.w, pq1);
         }
         float2* rb = red + (t & 1) * GDN_RG * GDN_D;
-        rb[rg * GDN_D + col] = make_float2(pk0 + pk1, pq0 + pq1);
+        rb[rg * GDN_D + col] = make_float2((pk0 + pk1) * rk, (pq0 + pq1) * rq);
         named_sync<GDN_CONSUMERS>();
         float kvs = 0.f, qss = 0.f;
 #pragma unroll
@@ -327,14 +324,15 @@ __global__ void __launch_bounds__(GDN_THREADS, 1) gdn_step_kernel(const GdnArgs 
         const float eg = gv[t];
         const float dl = bv[t] * (x[(t * 4 + 2) * GDN_D + col] - eg * kvs);
         // q[t] was consumed before the barrier above: its slot now holds o[t]
-        if (rg == 0) x[(t * 4 + 0) * GDN_D + col] = fmaf(eg, qss, qk[t] * dl);
+        if (rg == 0) x[(t * 4 + 0) * GDN_D + col] = fmaf(eg, qss, dqk * dl);
+        const float kdl = rk * dl;
 #pragma unroll
         for (int r4 = 0; r4 < 8; ++r4) {
           const float4 kk = k4[r4];
-          sv[4 * r4 + 0] = fmaf(eg, sv[4 * r4 + 0], kk.x * dl);
-          sv[4 * r4 + 1] = fmaf(eg, sv[4 * r4 + 1], kk.y * dl);
-          sv[4 * r4 + 2] = fmaf(eg, sv[4 * r4 + 2], kk.z * dl);
-          sv[4 * r4 + 3] = fmaf(eg, sv[4 * r4 + 3], kk.w * dl);
+          sv[4 * r4 + 0] = fmaf(eg, sv[4 * r4 + 0], kk.x * kdl);
+          sv[4 * r4 + 1] = fmaf(eg, sv[4 * r4 + 1], kk.y * kdl);
+          sv[4 * r4 + 2] = fmaf(eg, sv[4 * r4 + 2], kk.z * kdl);
+          sv[4 * r4 + 3] = fmaf(eg, sv[4 * r4 + 3], kk.w * kdl);
         }
       }
 #pragma unroll
