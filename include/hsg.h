@@ -48,8 +48,7 @@ typedef struct hsg_config {
  * GDN layers use w_in = [in_proj_qkv | in_proj_z | in_proj_b | in_proj_a | zero pad] (8320 x 1024 bf16) and
  * conv_w / A_log / dt_bias / gnorm_w; attention layers use w_in = [q_proj | k_proj | v_proj] (5120 x 1024 bf16)
  * and q_norm / k_norm. w_gu interleaves gate_proj and up_proj row by row (row 2f = gate f, row 2f+1 = up f;
- * 7168 x 1024 bf16). All RMSNorm
- * weights are passed as fp32 (1 + w); gnorm_w is the gated norm's plain w. */
+ * 7168 x 1024 bf16). All RMSNorm weights are passed as fp32 (1 + w); gnorm_w is the gated norm's plain w. */
 typedef struct hsg_layer_weights {
   const void* w_in;
   const void* w_out;     /* out_proj / o_proj, 1024 x 2048 bf16 */
