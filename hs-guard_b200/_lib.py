@@ -78,6 +78,7 @@ def lib():
             "hsg_gdn_step": [P, P, P, P, P, P, P, P, I, I, I, P, P, P],
             "hsg_ring_attention": [P, P, P, P, P, P, P, P, P, I, I, I, F, P, I, P, P],
             "hsg_gemm": [P, I, I, P, P, I, I, P, P, P, I, I, P, P],
+            "hsg_gemm_f32_noalloc": [P, I, I, P, I, P, P, P, I, I, P, P],
         }
         for name, args in sig.items():
             fn = getattr(L, name)

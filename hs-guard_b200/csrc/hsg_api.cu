@@ -845,3 +845,83 @@ int hsg_gemm(const void* w, int n, int k, const void* x_hi, const void* x_lo, in
 }
 
 }  // extern "C"
+
+// ---- GEMM without allocation --------------------------------------------------------------------------------------
+// Some callers cannot allocate device memory on their call path. A host whose caching allocator (PyTorch's, for one)
+// already holds the GPU's free memory can see cudaMalloc fail although that allocator has room, and cudaFree waits
+// for the whole device, which would stall every other stream of a serving loop that must answer within milliseconds.
+// hsg_gemm_f32_noalloc therefore takes fp32 activations and splits them into the bf16 (hi, lo) operand pair inside a
+// scratch area that is part of the library image, so the call allocates nothing. No element of the area needs to
+// start at zero: the split kernel writes every element the GEMM then reads, in stream order, in the same call.
+static __device__ __align__(256) __nv_bfloat16 g_noalloc_operands[2 * (size_t)HSG_NOALLOC_MAX_ELEMS];
+
+namespace {
+constexpr int kNoallocMaxDevices = 64;
+std::mutex g_noalloc_mu;
+__nv_bfloat16* g_noalloc_base[kNoallocMaxDevices];  // scratch address per device, looked up on first use
+
+// The current device's copy of the scratch area; the first call on a device resolves its address.
+int noalloc_scratch(__nv_bfloat16** out) {
+  int dev = 0;
+  CU(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= kNoallocMaxDevices)
+    return fail(HSG_ERR_UNSUPPORTED, "device ordinal %d is beyond the %d the scratch table covers", dev,
+                kNoallocMaxDevices);
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (!g_noalloc_base[dev]) {
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_operands);
+    if (e != cudaSuccess || !p)
+      return fail(HSG_ERR_CUDA, "cudaGetSymbolAddress of the GEMM scratch area failed on device %d: %s", dev,
+                  cudaGetErrorString(e));
+    g_noalloc_base[dev] = static_cast<__nv_bfloat16*>(p);
+  }
+  *out = g_noalloc_base[dev];
+  return HSG_OK;
+}
+
+// x [count] fp32 -> hi = bf16(x), lo = bf16(x - hi); count is a multiple of 4 and x is 16-byte aligned.
+__global__ void __launch_bounds__(256) split_operand_kernel(const float4* __restrict__ x, __nv_bfloat162* hi,
+                                                            __nv_bfloat162* lo, int64_t count4) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < count4; i += (int64_t)gridDim.x * blockDim.x) {
+    const float4 v = x[i];
+    __nv_bfloat16 h0, h1, h2, h3, l0, l1, l2, l3;
+    split_bf16(v.x, h0, l0);
+    split_bf16(v.y, h1, l1);
+    split_bf16(v.z, h2, l2);
+    split_bf16(v.w, h3, l3);
+    hi[2 * i] = __halves2bfloat162(h0, h1);
+    hi[2 * i + 1] = __halves2bfloat162(h2, h3);
+    lo[2 * i] = __halves2bfloat162(l0, l1);
+    lo[2 * i + 1] = __halves2bfloat162(l2, l3);
+  }
+}
+}  // namespace
+
+extern "C" int hsg_gemm_f32_noalloc(const void* w, int n, int k, const float* x, int m, float* y, void* act_hi,
+                                    void* act_lo, int mode, int splits, int* err, void* stream) {
+  if (!w || !x) return fail(HSG_ERR_INVALID, "NULL argument");
+  if (n <= 0 || n % 128 || k <= 0 || k % 64 || m < 1) return fail(HSG_ERR_INVALID, "bad GEMM shape");
+  if ((int64_t)m * k > HSG_NOALLOC_MAX_ELEMS)
+    return fail(HSG_ERR_INVALID, "m * k = %lld exceeds the scratch limit HSG_NOALLOC_MAX_ELEMS = %d elements",
+                (long long)m * k, HSG_NOALLOC_MAX_ELEMS);
+  if (reinterpret_cast<uintptr_t>(x) & 15) return fail(HSG_ERR_INVALID, "x must be 16-byte aligned");
+  if (mode < 0 || mode > 2) return fail(HSG_ERR_INVALID, "bad mode %d", mode);
+  if (mode != GEMM_SILU_MUL && !y) return fail(HSG_ERR_INVALID, "y is NULL");
+  if (mode == GEMM_SILU_MUL && (!act_hi || !act_lo)) return fail(HSG_ERR_INVALID, "act_hi/act_lo are NULL");
+  int rc;
+  if ((rc = set_kernel_attributes()) != HSG_OK) return rc;
+  __nv_bfloat16* hi = nullptr;
+  if ((rc = noalloc_scratch(&hi)) != HSG_OK) return rc;
+  __nv_bfloat16* lo = hi + HSG_NOALLOC_MAX_ELEMS;
+  const int64_t count4 = (int64_t)m * k / 4;
+  const int64_t want = (count4 + 255) / 256;
+  const int blocks = want < 8 * SM_COUNT ? (int)want : 8 * SM_COUNT;
+  cudaStream_t st = (cudaStream_t)stream;
+  split_operand_kernel<<<blocks, 256, 0, st>>>(reinterpret_cast<const float4*>(x),
+                                               reinterpret_cast<__nv_bfloat162*>(hi),
+                                               reinterpret_cast<__nv_bfloat162*>(lo), count4);
+  CU(cudaGetLastError());
+  return launch_gemm(st, w, n, k, hi, lo, m, m, mode, y, n, static_cast<__nv_bfloat16*>(act_hi),
+                     static_cast<__nv_bfloat16*>(act_lo), n / 2, err, splits);
+}
