@@ -45,6 +45,8 @@ def parse():
     ap.add_argument("--contexts", default=",".join(map(str, CONTEXTS)))
     ap.add_argument("--cpu-slots", type=int, default=32)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--state-dtype", default="float16", choices=("float16", "float32"),
+                    help="recurrent-state storage (float16 = the reference StreamingGuard's)")
     return ap.parse_args()
 
 
@@ -161,22 +163,23 @@ def run_reference(args):
 
 
 # ---- ours --------------------------------------------------------------------------------------------------------
-def gdn_bytes_per_launch(nb, lb):
-    """Algorithmic HBM bytes of one gated-delta-rule launch: per row, 16 heads x 64 KB state read + write, the fp32
-    conv history (3 x 6144) read + write, the projection columns it reads (q|k|v|z|a|b) and its bf16 hi/lo output."""
-    state = 16 * 128 * 128 * 4 * 2
+def gdn_bytes_per_launch(nb, lb, state_elem=2):
+    """Algorithmic HBM bytes of one gated-delta-rule launch: per row, 16 heads x one 128 x 128 state tile read + write
+    (``state_elem`` bytes per element: 32 KB fp16 / 64 KB fp32), the fp32 conv history (3 x 6144) read + write, the
+    projection columns it reads (q|k|v|z|a|b) and its bf16 hi/lo output."""
+    state = 16 * 128 * 128 * state_elem * 2
     conv = 3 * 6144 * 4 * 2
     proj = lb * (6144 + 2048 + 32) * 4
     out = lb * 2048 * 2 * 2
     return nb * (state + conv + proj + out)
 
 
-def tick_bytes(nb, lb):
-    """Algorithmic HBM bytes of one whole tick: bf16 weights once (non-embedding), per row the fp32 recurrent state
-    (18 layers, read + write), fp32 conv history (read + write), the fp16 ring (6 layers x 2 heads x 512 x 256 x K,V
-    read) and embedding rows."""
+def tick_bytes(nb, lb, state_elem=2):
+    """Algorithmic HBM bytes of one whole tick: bf16 weights once (non-embedding), per row the recurrent state
+    (18 layers, read + write, ``state_elem`` bytes per element), fp32 conv history (read + write), the fp16 ring
+    (6 layers x 2 heads x 512 x 256 x K,V read) and embedding rows."""
     weights = 498_113_344 * 2 + 2 * 512 * 1024 * 2
-    per_row = 18 * (16 * 128 * 128 * 4 * 2 + 3 * 6144 * 4 * 2) + 6 * 2 * 512 * 256 * 2 * 2 + lb * 1024 * 2
+    per_row = 18 * (16 * 128 * 128 * state_elem * 2 + 3 * 6144 * 4 * 2) + 6 * 2 * 512 * 256 * 2 * 2 + lb * 1024 * 2
     return weights + nb * per_row
 
 
@@ -201,7 +204,8 @@ def run_ours(args):
         torch.distributed.barrier()
     S = args.slots
     sd = W.random_state_dict(0)
-    eng = SlotEngine(sd, S)
+    eng = SlotEngine(sd, S, state_dtype=args.state_dtype)
+    state_elem = 2 if args.state_dtype == "float16" else 4
     guard = StreamingGuard.from_engine(eng, DEFAULT_METADATA)
     lens = tuple(int(x) for x in args.contexts.split(","))
     t0 = time.perf_counter()
@@ -277,14 +281,15 @@ def run_ours(args):
     except (OSError, ValueError):
         pass
     hbm_peak, peak_src = (peaks["hbm_gbs"], "measured") if "hbm_gbs" in peaks else (6650.0, "fallback")
-    gdn_bytes = gdn_bytes_per_launch(S, 1)
+    gdn_bytes = gdn_bytes_per_launch(S, 1, state_elem)
     achieved = gdn_bytes / (gdn_avg_ms * 1e-3) / 1e9
     traffic = None
     try:
-        traffic = json.load(open(os.path.join(ROOT, "profiles", "traffic.json")))["gdn_step_c4"]["bytes_per_launch"]
+        key = "gdn_step_c4_" + ("f16" if state_elem == 2 else "f32")
+        traffic = json.load(open(os.path.join(ROOT, "profiles", "traffic.json")))[key]["bytes_per_launch"]
     except (OSError, ValueError, KeyError):
         pass
-    step_bytes = tick_bytes(S, 1)
+    step_bytes = tick_bytes(S, 1, state_elem)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -297,7 +302,8 @@ def run_ours(args):
             "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": K, "warmup": Wm,
             "ms_per_step": dev_ms, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": value / world / PUBLISHED_TOKENS_PER_S,
-            "dtype": "f32 (state, norms, accumulation; bf16 hi/lo tensor-core operands, fp16 ring)",
+            "dtype": f"f32 (norms, conv history, accumulation; {args.state_dtype} recurrent state; bf16 hi/lo "
+                     "tensor-core operands; fp16 ring)",
             "data": "synthetic (uniform random token ids; random-init weights, seed 0)",
             "config": {"workload": "C4: full-model streaming, 352 slots per GPU prefilled with 512/2048/8000 "
                                    "random tokens (1/3 each, seed 4), then single-token role=assistant steps",

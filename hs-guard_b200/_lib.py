@@ -13,6 +13,8 @@ LIB_PATH = os.path.join(HERE, "libhsg.so")
 
 HSG_OK, HSG_ERR_INVALID, HSG_ERR_CUDA, HSG_ERR_DEVICE, HSG_ERR_UNSUPPORTED = 0, -1, -2, -3, -4
 HSG_FLAG_BF16_ACT = 1
+HSG_FLAG_STATE_F32 = 2
+HSG_STATE_F32, HSG_STATE_F16 = 0, 1
 N_LAYERS = 24
 HSG_PROF_N = 13
 PROF_NAMES = ("embed", "gemm_in", "gdn", "attn_prep", "ring_attn", "ring_append", "gemm_out", "norm", "gemm_gu",
@@ -39,7 +41,8 @@ class Weights(C.Structure):
 
 class Pools(C.Structure):
     _fields_ = [("rec", C.c_void_p), ("conv", C.c_void_p), ("ring_k", C.c_void_p), ("ring_v", C.c_void_p),
-                ("ring_pos", C.c_void_p), ("max_slots", C.c_int32), ("n_gdn", C.c_int32), ("n_attn", C.c_int32)]
+                ("ring_pos", C.c_void_p), ("max_slots", C.c_int32), ("n_gdn", C.c_int32), ("n_attn", C.c_int32),
+                ("rec_dtype", C.c_int32)]
 
 
 class HsgError(RuntimeError):
@@ -75,7 +78,7 @@ def lib():
             "hsg_get_pools": [P, C.POINTER(Pools)],
             "hsg_profile_step": [P, P, I, I, P, P, P],
             "hsg_launches_per_step": [P, I, I],
-            "hsg_gdn_step": [P, P, P, P, P, P, P, P, I, I, I, P, P, P],
+            "hsg_gdn_step": [P, P, P, P, P, P, I, P, P, I, I, I, P, P, P],
             "hsg_ring_attention": [P, P, P, P, P, P, P, P, P, I, I, I, F, P, I, P, P],
             "hsg_gemm": [P, I, I, P, P, I, I, P, P, P, I, I, P, P],
             "hsg_gemm_f32_noalloc": [P, I, I, P, I, P, P, P, I, I, P, P],

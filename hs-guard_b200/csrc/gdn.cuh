@@ -4,9 +4,12 @@
 // CTA (h, p) serves rows p, p + P, p + 2P, ... of head h, so its conv and gated-norm weights, A_log and dt_bias stay
 // in registers for the whole launch.
 //
+// The recurrent state is kept in HBM as fp16 (the reference StreamingGuard's state_dtype, runtime.py:157) or fp32
+// (template parameter ST); in shared memory it keeps that type and in registers it is fp32.
+//
 // Producer warp (warp 16): for each item, waits until its shared-memory stage is free, writes the previous occupant's
-// updated 64 KB state back to HBM with one TMA bulk store, then loads the item's inputs with TMA bulk copies -- the
-// state tile (contiguous in the pool [S+1][16][128][128]), the head's q/k/v/z projection slices for the tick's tokens
+// updated state tile (32 KB fp16 / 64 KB fp32) back to HBM with one TMA bulk store, then loads the item's inputs with
+// TMA bulk copies -- the state tile (contiguous in the pool [S+1][16][128][128]), the head's q/k/v/z projection slices
 // and the slot's 3-row conv history -- completing on the stage's `full` barrier. It runs up to STAGES items ahead.
 // Consumer warps (16 warps; thread t owns state column t % 128, rows 32*(t/128)..+31, in registers), per item:
 //   conv: silu(causal depthwise conv, kernel 4) over [history | new tokens] in place, history rolled to global;
@@ -44,7 +47,7 @@ struct GdnArgs {
   // both
   const float* A_log;   // [16]
   const float* dt_bias; // [16]
-  float* state;         // [max_slots+1, 16, 128, 128] fp32, updated in place
+  void* state;          // [max_slots+1, 16, 128, 128] ST (fp16 or fp32), updated in place
   int* err;
 };
 
@@ -52,42 +55,50 @@ constexpr int GDN_CONSUMERS = 512;
 constexpr int GDN_THREADS = GDN_CONSUMERS + 32;  // + one producer warp
 constexpr int GDN_CWARPS = GDN_CONSUMERS / 32;
 constexpr int GDN_RG = GDN_CONSUMERS / GDN_D;    // 4 row groups of 32 rows
-constexpr int GDN_TILE_BYTES = GDN_D * GDN_D * 4;
 constexpr int GDN_CTAS_PER_HEAD = 9;             // 16 x 9 = 144 persistent CTAs on the 148 SMs
 constexpr int GDN_SMEM_LIMIT = 227 * 1024;
+constexpr int GDN_MAX_STAGES = 6;
+template <typename ST>
+__host__ __device__ constexpr int gdn_tile_bytes() { return GDN_D * GDN_D * (int)sizeof(ST); }
 
 struct GdnMeta {  // per stage, written by the producer before it arrives on `full`
   int64_t slot;
   int len, pad;
 };
 
-// Stage layout: state tile | x [lb][4][128] fp32 (q, k, v, z slices; RAW: q, k, v bf16 in the first half) |
-// hist [3][3][128] fp32 (q, k, v channel blocks).
-__host__ __device__ inline int gdn_stage_bytes(int lb) { return GDN_TILE_BYTES + lb * 4 * GDN_D * 4 + 9 * GDN_D * 4; }
+// Stage layout: state tile (tile_bytes) | x [lb][4][128] fp32 (q, k, v, z slices; RAW: q, k, v bf16 in the first
+// half) | hist [3][3][128] fp32 (q, k, v channel blocks).
+__host__ __device__ inline int gdn_stage_bytes(int lb, int tile_bytes) {
+  return tile_bytes + lb * 4 * GDN_D * 4 + 9 * GDN_D * 4;
+}
 __host__ __device__ inline int gdn_fixed_bytes() {
-  // partial sums [2][4][128] float2 | g, beta, q.k [64] | meta [3] | full, empty barriers [3] | alignment slack
-  return 2 * GDN_RG * GDN_D * 8 + 3 * MAX_LB * 4 + 3 * 16 + 6 * 8 + 128;
+  // partial sums [2][4][128] float2 | g, beta, q.k [64] | meta, full, empty barriers [GDN_MAX_STAGES] | alignment
+  return 2 * GDN_RG * GDN_D * 8 + 3 * MAX_LB * 4 + GDN_MAX_STAGES * (16 + 2 * 8) + 128;
 }
-__host__ __device__ inline int gdn_stages(int lb) {
-  int s = (GDN_SMEM_LIMIT - gdn_fixed_bytes()) / gdn_stage_bytes(lb);
-  return s > 3 ? 3 : (s < 1 ? 1 : s);
+__host__ __device__ inline int gdn_stages(int lb, int tile_bytes) {
+  int s = (GDN_SMEM_LIMIT - gdn_fixed_bytes()) / gdn_stage_bytes(lb, tile_bytes);
+  return s > GDN_MAX_STAGES ? GDN_MAX_STAGES : (s < 1 ? 1 : s);
 }
-__host__ __device__ inline int gdn_smem_bytes(int lb) { return gdn_stages(lb) * gdn_stage_bytes(lb) + gdn_fixed_bytes(); }
+__host__ __device__ inline int gdn_smem_bytes(int lb, int tile_bytes) {
+  return gdn_stages(lb, tile_bytes) * gdn_stage_bytes(lb, tile_bytes) + gdn_fixed_bytes();
+}
 
-template <bool FUSED>
+template <bool FUSED, typename ST>
 __global__ void __launch_bounds__(GDN_THREADS, 1) gdn_step_kernel(const GdnArgs args) {
+  constexpr int TILE = gdn_tile_bytes<ST>();
+  ST* const state_pool = static_cast<ST*>(args.state);
   extern __shared__ __align__(128) uint8_t gdn_smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(gdn_smem_raw) + 127) & ~uintptr_t(127));
   const int lb = args.lb, S = args.stages;
-  const int sbytes = gdn_stage_bytes(lb);
+  const int sbytes = gdn_stage_bytes(lb, TILE);
   uint8_t* fixed = smem + S * sbytes;
   float2* red = reinterpret_cast<float2*>(fixed);                  // [2][4][128]
   float* gv = reinterpret_cast<float*>(red + 2 * GDN_RG * GDN_D);  // decay factors e^g per token
   float* bv = gv + MAX_LB;                                         // beta per token
   float* qk = bv + MAX_LB;                                         // q.k per token
-  GdnMeta* meta = reinterpret_cast<GdnMeta*>(qk + MAX_LB);         // [3]
-  uint64_t* full = reinterpret_cast<uint64_t*>(meta + 3);          // [3]
-  uint64_t* empty = full + 3;                                      // [3]
+  GdnMeta* meta = reinterpret_cast<GdnMeta*>(qk + MAX_LB);         // [GDN_MAX_STAGES]
+  uint64_t* full = reinterpret_cast<uint64_t*>(meta + GDN_MAX_STAGES);
+  uint64_t* empty = full + GDN_MAX_STAGES;
 
   const int h = blockIdx.x, p = blockIdx.y, P = gridDim.y;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -106,8 +117,8 @@ __global__ void __launch_bounds__(GDN_THREADS, 1) gdn_step_kernel(const GdnArgs 
 
   if (warp == GDN_CWARPS) {
     // ===================================== producer =====================================
-    int64_t held_slot[3] = {0, 0, 0};
-    int held_len[3] = {0, 0, 0};
+    int64_t held_slot[GDN_MAX_STAGES] = {};
+    int held_len[GDN_MAX_STAGES] = {};
     // Part 1 of an item's loads: metadata, expected bytes, the state tile and the conv history. These belong to this
     // layer alone (no earlier kernel of the tick touches them), so for the first stages they are issued before the
     // dependency wait. Part 2: the projection slices written by the preceding GEMM.
@@ -126,19 +137,19 @@ __global__ void __launch_bounds__(GDN_THREADS, 1) gdn_step_kernel(const GdnArgs 
       held_slot[s] = slot;
       held_len[s] = len;
       uint8_t* st = stage_ptr(s);
-      float* hist = reinterpret_cast<float*>(st + GDN_TILE_BYTES) + lb * 4 * GDN_D;
+      float* hist = reinterpret_cast<float*>(st + TILE) + lb * 4 * GDN_D;
       if (lane == 0) {
         meta[s].slot = slot;
         meta[s].len = len;
         if (len > 0)
-          mbar_arrive_expect_tx(&full[s], GDN_TILE_BYTES +
+          mbar_arrive_expect_tx(&full[s], TILE +
                                               (FUSED ? len * 4 * GDN_D * 4 + 9 * GDN_D * 4 : len * 3 * GDN_D * 2));
         else
           mbar_arrive(&full[s]);
       }
       __syncwarp();
       if (len == 0) return;
-      if (lane == 0) bulk_g2s(st, args.state + ((size_t)slot * GDN_H + h) * (GDN_D * GDN_D), GDN_TILE_BYTES, &full[s]);
+      if (lane == 0) bulk_g2s(st, state_pool + ((size_t)slot * GDN_H + h) * (GDN_D * GDN_D), TILE, &full[s]);
       if (FUSED && lane < 9) {  // conv history: 3 rows x (q, k, v) channel blocks
         const int rr = lane / 3, part = lane % 3;
         const float* src = args.conv_pool + ((size_t)slot * CONV_KEEP + rr) * CONV_DIM + part * KEY_DIM + h * GDN_D;
@@ -148,7 +159,7 @@ __global__ void __launch_bounds__(GDN_THREADS, 1) gdn_step_kernel(const GdnArgs 
     auto issue_inputs = [&](int i) {
       const int s = i % S, n = row_of(i), len = held_len[s];
       if (len == 0) return;
-      float* x = reinterpret_cast<float*>(stage_ptr(s) + GDN_TILE_BYTES);
+      float* x = reinterpret_cast<float*>(stage_ptr(s) + TILE);
       if (FUSED) {
         for (int j = lane; j < len * 4; j += 32) {  // q, k, v, z slices of each token: 4 x 512 B
           const int t = j >> 2, part = j & 3;
@@ -174,7 +185,7 @@ __global__ void __launch_bounds__(GDN_THREADS, 1) gdn_step_kernel(const GdnArgs 
         // the consumers are done with item i - S in stage s: write its state back
         if (!mbar_wait(&empty[s], (r - 1) & 1, args.err, ERR_TIMEOUT_TMA)) break;
         if (lane == 0 && held_len[s] > 0) {
-          bulk_s2g(args.state + ((size_t)held_slot[s] * GDN_H + h) * (GDN_D * GDN_D), stage_ptr(s), GDN_TILE_BYTES);
+          bulk_s2g(state_pool + ((size_t)held_slot[s] * GDN_H + h) * (GDN_D * GDN_D), stage_ptr(s), TILE);
           bulk_commit();
         }
       }
@@ -222,8 +233,8 @@ __global__ void __launch_bounds__(GDN_THREADS, 1) gdn_step_kernel(const GdnArgs 
     load_ab(i + 1, nxt_a, nxt_b);
     const int s = i % S, n = row_of(i);
     uint8_t* st = stage_ptr(s);
-    float* stile = reinterpret_cast<float*>(st);
-    float* x = reinterpret_cast<float*>(st + GDN_TILE_BYTES);
+    ST* stile = reinterpret_cast<ST*>(st);
+    float* x = reinterpret_cast<float*>(st + TILE);
     float* hist = x + lb * 4 * GDN_D;
     if (!named_sync_and<GDN_CONSUMERS>(mbar_wait(&full[s], (i / S) & 1, args.err, ERR_TIMEOUT_TMA))) {
       broken = true;
@@ -284,7 +295,7 @@ __global__ void __launch_bounds__(GDN_THREADS, 1) gdn_step_kernel(const GdnArgs 
       // ---- recurrence ----
       float sv[32];
 #pragma unroll
-      for (int r = 0; r < 32; ++r) sv[r] = stile[(rg * 32 + r) * GDN_D + col];
+      for (int r = 0; r < 32; ++r) sv[r] = to_f32(stile[(rg * 32 + r) * GDN_D + col]);
       const float scale = 0.08838834764831845f;  // 128^-1/2, correctly rounded
       for (int t = 0; t < len; ++t) {
         // L2 norms (eps 1e-6) and q.k of token t, computed by every warp from the raw conv outputs (no barrier);
@@ -336,7 +347,7 @@ __global__ void __launch_bounds__(GDN_THREADS, 1) gdn_step_kernel(const GdnArgs 
         }
       }
 #pragma unroll
-      for (int r = 0; r < 32; ++r) stile[(rg * 32 + r) * GDN_D + col] = sv[r];
+      for (int r = 0; r < 32; ++r) stile[(rg * 32 + r) * GDN_D + col] = from_f32<ST>(sv[r]);
       named_sync<GDN_CONSUMERS>();  // o[t] complete for the epilogue
       // ---- epilogue ----
       if (FUSED) {

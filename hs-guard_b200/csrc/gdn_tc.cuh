@@ -1,0 +1,417 @@
+// Gated delta rule slot step for fp16 recurrent state and ticks of up to 16 tokens, with the state-vector products
+// on the tensor cores (warp-level mma.sync). Longer ticks use gdn_step_kernel<., __half> (gdn.cuh).
+//
+// Work split and pipeline as in gdn.cuh: a persistent, head-stationary grid (16 heads x 9 CTAs); a producer warp
+// streams each (row, head) item's inputs into a STAGES-deep shared-memory ring with TMA and writes the updated state
+// back with TMA. Eight consumer warps process one item at a time:
+//
+//  * Prologue. Thread c < 128 runs the causal conv of q and k channel c (FUSED) or widens them from bf16 (RAW), and
+//    writes k back as fp32 plus the MMA operand columns k_hi, k_lo, q_hi, q_lo in fp16 (hi = fp16(x),
+//    lo = fp16(x - hi)); its warp adds up the per-token partial sums of q.q, k.k and q.k. Thread 128 + c does the
+//    same for v channel c, then the decay e^g and beta of token c. One barrier.
+//  * The fp16 state tile arrives by 2-D TMA as two [128 k][64 v] halves with 128-byte swizzle (one tensor map over
+//    the pool viewed as [(S+1)*16*128 rows][128]); warp w loads the sixteen v columns [16 w, 16 w + 16) for all
+//    128 k with `ldmatrix.trans` as eight 16 x 16 fragments of A = S^T and keeps them in registers as fp32 for the
+//    whole tick.
+//  * Per token, no barrier: one m16n8k16 MMA per fragment against B = [k_hi | k_lo | q_hi | q_lo | 0 0 0 0] gives
+//    S^T k and S^T q for the warp's columns, exact up to the fp16 state; then
+//      delta = beta (v - e^g rk S^T k),   o = e^g rq S^T q + (k.q) rk rq delta,   S <- e^g S + rk k delta^T
+//    (rk, rq: the L2-norm factors with eps 1e-6, rq including 128^-1/2), the update applied to the fragments with
+//    packed fp32x2 arithmetic.
+//  * After the tick's last token the fragments are rounded to fp16 once and written back with `stmatrix.trans`; one
+//    barrier; the gated RMSNorm epilogue as in gdn.cuh.
+// The reference keeps StreamingGuard's state in fp16 (runtime.py:157) and computes in fp32 inside its kernel
+// (engine/fused_kernels.py:140-194, gdn_slot_kernel.py:66), rounding once per tick: the same here.
+#pragma once
+#include "gdn.cuh"
+
+namespace hsg {
+
+constexpr int GDNT_CONS = 256;                 // 8 consumer warps
+constexpr int GDNT_CWARPS = GDNT_CONS / 32;
+constexpr int GDNT_THREADS = GDNT_CONS + 32;   // + producer warp
+constexpr int GDNT_MAX_LB = 16;
+constexpr int GDNT_HALF = GDN_D * 64 * 2;      // one [128 k][64 v] fp16 half of the tile: 16 KB
+constexpr int GDNT_TILE = 2 * GDNT_HALF;
+
+// Stage: state halves | x [lb][4][128] fp32 (q, k, v, z) | FUSED: conv history [9][128] fp32, RAW: bf16 q|k|v
+// [lb][3][128]; rounded up to 1 KB so every stage's tile is 1024-aligned for the swizzle.
+__host__ __device__ inline int gdnt_stage_bytes(int lb, bool fused) {
+  return (GDNT_TILE + lb * 4 * GDN_D * 4 + (fused ? 9 * GDN_D * 4 : lb * 3 * GDN_D * 2) + 1023) & ~1023;
+}
+__host__ __device__ inline int gdnt_fixed_bytes() {
+  // B operand columns [16][4][128] fp16 | norm partials [16][3][4] f32 | g, beta [16] | meta, full, empty | align
+  return GDNT_MAX_LB * 4 * GDN_D * 2 + GDNT_MAX_LB * 12 * 4 + 2 * GDNT_MAX_LB * 4 + GDN_MAX_STAGES * (16 + 2 * 8) +
+         1024;
+}
+__host__ __device__ inline int gdnt_stages(int lb, bool fused) {
+  int s = (GDN_SMEM_LIMIT - gdnt_fixed_bytes()) / gdnt_stage_bytes(lb, fused);
+  return s > GDN_MAX_STAGES ? GDN_MAX_STAGES : (s < 1 ? 1 : s);
+}
+__host__ __device__ inline int gdnt_smem_bytes(int lb, bool fused) {
+  return gdnt_stages(lb, fused) * gdnt_stage_bytes(lb, fused) + gdnt_fixed_bytes();
+}
+
+template <bool FUSED>
+__global__ void __launch_bounds__(GDNT_THREADS, 1)
+gdn_tc_kernel(const __grid_constant__ CUtensorMap tm_state, const GdnArgs args) {
+  extern __shared__ __align__(1024) uint8_t gdnt_smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(gdnt_smem_raw) + 1023) & ~uintptr_t(1023));
+  const int lb = args.lb, S = args.stages;
+  const int sbytes = gdnt_stage_bytes(lb, FUSED);
+  uint8_t* fixed = smem + S * sbytes;
+  __half* bop = reinterpret_cast<__half*>(fixed);                        // [16][4][128]: k_hi, k_lo, q_hi, q_lo
+  float* part = reinterpret_cast<float*>(bop + GDNT_MAX_LB * 4 * GDN_D);  // [16][3][4]: q.q, k.k, q.k per q/k warp
+  float* gv = part + GDNT_MAX_LB * 12;                                    // e^g per token
+  float* bv = gv + GDNT_MAX_LB;                                           // beta per token
+  GdnMeta* meta = reinterpret_cast<GdnMeta*>(bv + GDNT_MAX_LB);
+  uint64_t* full = reinterpret_cast<uint64_t*>(meta + GDN_MAX_STAGES);
+  uint64_t* empty = full + GDN_MAX_STAGES;
+
+  const int h = blockIdx.x, p = blockIdx.y, P = gridDim.y;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int n_items = args.nb > p ? (args.nb - p + P - 1) / P : 0;
+  auto row_of = [&](int i) { return p + i * P; };
+  auto stage_ptr = [&](int s) { return smem + s * sbytes; };
+  auto tile_row = [&](int64_t slot) { return (int)((slot * GDN_H + h) * GDN_D); };
+
+  if (tid == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], GDNT_CONS);
+    }
+    fence_barrier_init();
+    prefetch_tmap(&tm_state);
+  }
+  __syncthreads();
+
+  if (warp == GDNT_CWARPS) {
+    // ===================================== producer =====================================
+    int64_t held_slot[GDN_MAX_STAGES] = {};
+    int held_len[GDN_MAX_STAGES] = {};
+    auto issue_state = [&](int i) {
+      const int s = i % S, n = row_of(i);
+      int len = (int)args.lens[n];
+      const int64_t slot = args.slots[n];
+      if (len < 0 || len > lb) {
+        if (lane == 0) set_error(args.err, ERR_BAD_LEN);
+        len = 0;
+      }
+      if (len > 0 && (slot < 0 || slot > args.max_slots)) {
+        if (lane == 0) set_error(args.err, ERR_BAD_SLOT);
+        len = 0;
+      }
+      held_slot[s] = slot;
+      held_len[s] = len;
+      uint8_t* st = stage_ptr(s);
+      float* hist = reinterpret_cast<float*>(st + GDNT_TILE) + lb * 4 * GDN_D;
+      if (lane == 0) {
+        meta[s].slot = slot;
+        meta[s].len = len;
+        if (len > 0)
+          mbar_arrive_expect_tx(&full[s], GDNT_TILE +
+                                              (FUSED ? len * 4 * GDN_D * 4 + 9 * GDN_D * 4 : len * 3 * GDN_D * 2));
+        else
+          mbar_arrive(&full[s]);
+      }
+      __syncwarp();
+      if (len == 0) return;
+      if (lane == 0) {
+        tma_load_2d(st, &tm_state, 0, tile_row(slot), &full[s]);
+        tma_load_2d(st + GDNT_HALF, &tm_state, 64, tile_row(slot), &full[s]);
+      }
+      if (FUSED && lane < 9) {  // conv history: 3 rows x (q, k, v) channel blocks
+        const int rr = lane / 3, part = lane % 3;
+        const float* src = args.conv_pool + ((size_t)slot * CONV_KEEP + rr) * CONV_DIM + part * KEY_DIM + h * GDN_D;
+        bulk_g2s(hist + (rr * 3 + part) * GDN_D, src, GDN_D * 4, &full[s]);
+      }
+    };
+    auto issue_inputs = [&](int i) {
+      const int s = i % S, n = row_of(i), len = held_len[s];
+      if (len == 0) return;
+      float* x = reinterpret_cast<float*>(stage_ptr(s) + GDNT_TILE);
+      if (FUSED) {
+        for (int j = lane; j < len * 4; j += 32) {  // q, k, v, z slices of each token: 4 x 512 B
+          const int t = j >> 2, part = j & 3;
+          const float* src = args.proj + ((size_t)n * lb + t) * GDN_IN + part * KEY_DIM + h * GDN_D;
+          bulk_g2s(x + (t * 4 + part) * GDN_D, src, GDN_D * 4, &full[s]);
+        }
+      } else {
+        __nv_bfloat16* xb = reinterpret_cast<__nv_bfloat16*>(x + lb * 4 * GDN_D);
+        for (int j = lane; j < len * 3; j += 32) {
+          const int t = j / 3, part = j % 3;
+          const __nv_bfloat16* src = args.packed + ((size_t)n * lb + t) * CONV_DIM + part * KEY_DIM + h * GDN_D;
+          bulk_g2s(xb + (t * 3 + part) * GDN_D, src, GDN_D * 2, &full[s]);
+        }
+      }
+    };
+    const int pre = n_items < S ? n_items : S;
+    for (int i = 0; i < pre; ++i) issue_state(i);
+    pdl_wait();
+    for (int i = 0; i < pre; ++i) issue_inputs(i);
+    for (int i = S; i < n_items + S; ++i) {
+      const int s = i % S, r = i / S;
+      if (i - S < n_items) {
+        // the consumers are done with item i - S in stage s: write its state back
+        if (!mbar_wait(&empty[s], (r - 1) & 1, args.err, ERR_TIMEOUT_TMA)) break;
+        if (lane == 0 && held_len[s] > 0) {
+          tma_store_2d(&tm_state, stage_ptr(s), 0, tile_row(held_slot[s]));
+          tma_store_2d(&tm_state, stage_ptr(s) + GDNT_HALF, 64, tile_row(held_slot[s]));
+          bulk_commit();
+        }
+      }
+      if (i >= n_items) continue;
+      if (lane == 0) bulk_wait_read_all();  // the stores have read the stage
+      __syncwarp();
+      issue_state(i);
+      issue_inputs(i);
+    }
+    if (lane == 0) bulk_wait_all();
+    return;
+  }
+
+  // ===================================== consumers =====================================
+  const int c = tid & (GDN_D - 1);             // prologue channel
+  const bool qk_thread = tid < GDN_D;          // thread c: q and k channel c; thread 128 + c: v channel c
+  const int g = lane >> 2, t4 = lane & 3;      // mma fragment coordinates
+  // conv weights: q/k threads hold q's (cw) and k's (cw2) taps of channel c, v threads v's taps
+  float4 cw = make_float4(0.f, 0.f, 0.f, 0.f), cw2 = cw;
+  if (FUSED) {
+    const float4* w4 = reinterpret_cast<const float4*>(args.conv_w);
+    if (qk_thread) {
+      cw = w4[0 * KEY_DIM + h * GDN_D + c];
+      cw2 = w4[1 * KEY_DIM + h * GDN_D + c];
+    } else {
+      cw = w4[2 * KEY_DIM + h * GDN_D + c];
+    }
+  }
+  const float4 gw = FUSED ? reinterpret_cast<const float4*>(args.gnorm_w)[lane] : make_float4(0.f, 0.f, 0.f, 0.f);
+  const float negA = -expf(args.A_log[h]), dtb = args.dt_bias[h];
+  // this lane's ldmatrix/stmatrix row within each 16 x 16 fragment: k row and 16-byte v chunk of its 8 x 8 matrix
+  const int frag_k = (lane & 7) + ((lane >> 4) & 1) * 8;
+  const int frag_c = 2 * (warp & 3) + ((lane >> 3) & 1);
+
+  // a, b of token tid - 128 of an item (v threads), loaded one item ahead so the latency hides behind compute
+  auto load_ab = [&](int i, float& a, float& b) {
+    a = 0.f;
+    b = 0.f;
+    const int t = tid - GDN_D;
+    if (i >= n_items || t < 0 || t >= lb) return;
+    const int n = row_of(i);  // padded tokens' values are loaded too (in bounds) and never used
+    if (FUSED) {
+      const float* row = args.proj + ((size_t)n * lb + t) * GDN_IN;
+      a = row[GDN_A_OFF + h];
+      b = row[GDN_B_OFF + h];
+    } else {
+      a = args.a_raw[((size_t)n * lb + t) * GDN_H + h];
+      b = args.b_raw[((size_t)n * lb + t) * GDN_H + h];
+    }
+  };
+  // decay e^g and beta of a token from its raw a, b
+  auto decay_beta = [&](float a, float b, float& eg, float& beta) {
+    const float xg = a + dtb;
+    const float sp = xg > 20.f ? xg : log1pf(expf(xg));
+    eg = expf(negA * sp);
+    beta = sigmoidf_(b);
+  };
+  pdl_wait();
+  if (tid == 0) pdl_trigger();
+  float cur_a, cur_b, cur_g, cur_beta;
+  load_ab(0, cur_a, cur_b);
+  decay_beta(cur_a, cur_b, cur_g, cur_beta);
+
+  for (int i = 0; i < n_items; ++i) {
+    float nxt_a, nxt_b;
+    load_ab(i + 1, nxt_a, nxt_b);
+    const int s = i % S, n = row_of(i);
+    uint8_t* st = stage_ptr(s);
+    float* x = reinterpret_cast<float*>(st + GDNT_TILE);
+    // Each warp waits for the stage itself (no block barrier: warp 7 may still be finishing the previous item's
+    // epilogue); the first barrier below combines the outcomes so that every warp leaves together on a failure.
+    const bool ok = mbar_wait(&full[s], (i / S) & 1, args.err, ERR_TIMEOUT_TMA);
+    const int len = ok ? meta[s].len : 0;
+    const int64_t slot = ok ? meta[s].slot : 0;
+    if (len == 0) {
+      if (!named_sync_and<GDNT_CONS>(ok)) break;
+      for (int e = tid; e < lb * GDN_D; e += GDNT_CONS) {
+        const size_t row = (size_t)n * lb + e / GDN_D;
+        if (FUSED) {
+          args.out_hi[row * KEY_DIM + h * GDN_D + (e & 127)] = __float2bfloat16_rn(0.f);
+          args.out_lo[row * KEY_DIM + h * GDN_D + (e & 127)] = __float2bfloat16_rn(0.f);
+        } else {
+          args.o_raw[(row * GDN_H + h) * GDN_D + (e & 127)] = 0.f;
+        }
+      }
+    } else {
+      // ---- prologue ----
+      const float* hist = x + lb * 4 * GDN_D;
+      const __nv_bfloat16* raw = reinterpret_cast<const __nv_bfloat16*>(x + lb * 4 * GDN_D);
+      if (qk_thread) {
+        float q0 = 0.f, q1 = 0.f, q2 = 0.f, k0 = 0.f, k1 = 0.f, k2 = 0.f;
+        if (FUSED) {
+          q0 = hist[0 * GDN_D + c]; q1 = hist[3 * GDN_D + c]; q2 = hist[6 * GDN_D + c];
+          k0 = hist[1 * GDN_D + c]; k1 = hist[4 * GDN_D + c]; k2 = hist[7 * GDN_D + c];
+        }
+        for (int t = 0; t < len; ++t) {
+          float qv, kv;
+          if (FUSED) {
+            const float xq = x[(t * 4 + 0) * GDN_D + c], xk = x[(t * 4 + 1) * GDN_D + c];
+            qv = silu(fmaf(cw.w, xq, fmaf(cw.z, q2, fmaf(cw.y, q1, cw.x * q0))));
+            kv = silu(fmaf(cw2.w, xk, fmaf(cw2.z, k2, fmaf(cw2.y, k1, cw2.x * k0))));
+            q0 = q1; q1 = q2; q2 = xq;
+            k0 = k1; k1 = k2; k2 = xk;
+          } else {
+            qv = __bfloat162float(raw[(t * 3 + 0) * GDN_D + c]);
+            kv = __bfloat162float(raw[(t * 3 + 1) * GDN_D + c]);
+          }
+          x[(t * 4 + 1) * GDN_D + c] = kv;
+          const __half khi = __float2half_rn(kv), qhi = __float2half_rn(qv);
+          __half* bt = bop + t * 4 * GDN_D + c;
+          bt[0 * GDN_D] = khi;
+          bt[1 * GDN_D] = __float2half_rn(kv - __half2float(khi));
+          bt[2 * GDN_D] = qhi;
+          bt[3 * GDN_D] = __float2half_rn(qv - __half2float(qhi));
+          const float sq = warp_sum(qv * qv), sk = warp_sum(kv * kv), sqk = warp_sum(qv * kv);
+          if (lane == 0) {
+            part[(t * 3 + 0) * 4 + warp] = sq;
+            part[(t * 3 + 1) * 4 + warp] = sk;
+            part[(t * 3 + 2) * 4 + warp] = sqk;
+          }
+        }
+        if (FUSED) {
+          float* gp = args.conv_pool + (size_t)slot * CONV_KEEP * CONV_DIM + h * GDN_D + c;
+          gp[0] = q0; gp[CONV_DIM] = q1; gp[2 * CONV_DIM] = q2;
+          gp[KEY_DIM] = k0; gp[CONV_DIM + KEY_DIM] = k1; gp[2 * CONV_DIM + KEY_DIM] = k2;
+        }
+      } else {
+        if (FUSED) {
+          float e0 = hist[2 * GDN_D + c], e1 = hist[5 * GDN_D + c], e2 = hist[8 * GDN_D + c];
+          for (int t = 0; t < len; ++t) {
+            float* xp = x + (t * 4 + 2) * GDN_D + c;
+            const float xv = *xp;
+            *xp = silu(fmaf(cw.w, xv, fmaf(cw.z, e2, fmaf(cw.y, e1, cw.x * e0))));
+            e0 = e1; e1 = e2; e2 = xv;
+          }
+          float* gp = args.conv_pool + (size_t)slot * CONV_KEEP * CONV_DIM + 2 * KEY_DIM + h * GDN_D + c;
+          gp[0] = e0; gp[CONV_DIM] = e1; gp[2 * CONV_DIM] = e2;
+        } else {
+          for (int t = 0; t < len; ++t) x[(t * 4 + 2) * GDN_D + c] = __bfloat162float(raw[(t * 3 + 2) * GDN_D + c]);
+        }
+        if (c < len) {
+          gv[c] = cur_g;
+          bv[c] = cur_beta;
+        }
+      }
+      // ---- this warp's state columns: A = S^T fragments (v 16 w + [0, 16), k 16 kt + [0, 16)) as fp32 ----
+      const uint32_t half_base = smem_u32(st) + (warp >> 2) * GDNT_HALF;
+      float sv[8][8];
+#pragma unroll
+      for (int kt = 0; kt < 8; ++kt) {
+        uint32_t r[4];
+        ldmatrix_x4_trans(half_base + sw128_off(16 * kt + frag_k, frag_c), r[0], r[1], r[2], r[3]);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const float2 f = unpack_half2(r[j]);
+          sv[kt][2 * j] = f.x;
+          sv[kt][2 * j + 1] = f.y;
+        }
+      }
+      // conv outputs, operand columns, norm partials, decay and beta are in shared memory
+      if (!named_sync_and<GDNT_CONS>(ok)) break;
+      // ---- recurrence ----
+      const float scale = 0.08838834764831845f;  // 128^-1/2, correctly rounded
+      const int v0 = 16 * warp + g;
+      for (int t = 0; t < len; ++t) {
+        const float4 pq = *reinterpret_cast<const float4*>(part + (t * 3 + 0) * 4);
+        const float4 pk = *reinterpret_cast<const float4*>(part + (t * 3 + 1) * 4);
+        const float4 pqk = *reinterpret_cast<const float4*>(part + (t * 3 + 2) * 4);
+        const float rq = scale * rsqrtf((pq.x + pq.y) + (pq.z + pq.w) + 1e-6f);
+        const float rk = rsqrtf((pk.x + pk.y) + (pk.z + pk.w) + 1e-6f);
+        const float dqk = ((pqk.x + pqk.y) + (pqk.z + pqk.w)) * rq * rk;
+        // S^T [k_hi k_lo q_hi q_lo] for this warp's 16 columns
+        const __half* bcol = bop + (t * 4 + (g & 3)) * GDN_D + 2 * t4;
+        float d[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};  // two chains: even and odd k tiles
+#pragma unroll
+        for (int kt = 0; kt < 8; ++kt) {
+          const uint32_t b0 = g < 4 ? *reinterpret_cast<const uint32_t*>(bcol + 16 * kt) : 0u;
+          const uint32_t b1 = g < 4 ? *reinterpret_cast<const uint32_t*>(bcol + 16 * kt + 8) : 0u;
+          mma_f16_16816(d[kt & 1], pack_half2(sv[kt][0], sv[kt][1]), pack_half2(sv[kt][2], sv[kt][3]),
+                        pack_half2(sv[kt][4], sv[kt][5]), pack_half2(sv[kt][6], sv[kt][7]), b0, b1);
+        }
+        // lane (g, t4 = 0): S^T k at v = v0, v0 + 8; lane (g, t4 = 1): S^T q
+        const float p0 = (d[0][0] + d[0][1]) + (d[1][0] + d[1][1]), p1 = (d[0][2] + d[0][3]) + (d[1][2] + d[1][3]);
+        const float q0 = __shfl_xor_sync(0xffffffffu, p0, 1), q1 = __shfl_xor_sync(0xffffffffu, p1, 1);
+        const float eg = gv[t], beta = bv[t];
+        float dl0 = 0.f, dl1 = 0.f;
+        if (t4 == 0) {
+          const float* xv = x + (t * 4 + 2) * GDN_D;
+          dl0 = beta * (xv[v0] - eg * rk * p0);
+          dl1 = beta * (xv[v0 + 8] - eg * rk * p1);
+          float* o = x + (t * 4 + 0) * GDN_D;  // the q slot is free after the prologue: it holds o[t]
+          o[v0] = fmaf(eg * rq, q0, dqk * dl0);
+          o[v0 + 8] = fmaf(eg * rq, q1, dqk * dl1);
+        }
+        dl0 = rk * __shfl_sync(0xffffffffu, dl0, lane & ~3);
+        dl1 = rk * __shfl_sync(0xffffffffu, dl1, lane & ~3);
+        // S <- e^g S + k (rk delta)^T: fragment pairs (k, k + 1) at v0 (regs 0, 2) and v0 + 8 (regs 1, 3)
+        const float* kx = x + (t * 4 + 1) * GDN_D + 2 * t4;
+        const float2 eg2 = make_float2(eg, eg), d02 = make_float2(dl0, dl0), d12 = make_float2(dl1, dl1);
+#pragma unroll
+        for (int kt = 0; kt < 8; ++kt) {
+          const float2 ka = *reinterpret_cast<const float2*>(kx + 16 * kt);
+          const float2 kc = *reinterpret_cast<const float2*>(kx + 16 * kt + 8);
+          const float2 u0 = __ffma2_rn(eg2, make_float2(sv[kt][0], sv[kt][1]), __fmul2_rn(ka, d02));
+          const float2 u1 = __ffma2_rn(eg2, make_float2(sv[kt][2], sv[kt][3]), __fmul2_rn(ka, d12));
+          const float2 u2 = __ffma2_rn(eg2, make_float2(sv[kt][4], sv[kt][5]), __fmul2_rn(kc, d02));
+          const float2 u3 = __ffma2_rn(eg2, make_float2(sv[kt][6], sv[kt][7]), __fmul2_rn(kc, d12));
+          sv[kt][0] = u0.x; sv[kt][1] = u0.y; sv[kt][2] = u1.x; sv[kt][3] = u1.y;
+          sv[kt][4] = u2.x; sv[kt][5] = u2.y; sv[kt][6] = u3.x; sv[kt][7] = u3.y;
+        }
+      }
+      // ---- the new state, rounded to fp16 once, back into the stage ----
+#pragma unroll
+      for (int kt = 0; kt < 8; ++kt)
+        stmatrix_x4_trans(half_base + sw128_off(16 * kt + frag_k, frag_c), pack_half2(sv[kt][0], sv[kt][1]),
+                          pack_half2(sv[kt][2], sv[kt][3]), pack_half2(sv[kt][4], sv[kt][5]),
+                          pack_half2(sv[kt][6], sv[kt][7]));
+      named_sync<GDNT_CONS>();  // o[t] complete for the epilogue
+      // ---- epilogue ----
+      if (FUSED) {  // token t on warp 7 - t % 8: the v warps, whose prologue is light, take the first tokens
+        for (int t = GDNT_CWARPS - 1 - warp; t < lb; t += GDNT_CWARPS) {
+          const size_t row = (size_t)n * lb + t;
+          __nv_bfloat16* oh = args.out_hi + row * KEY_DIM + h * GDN_D + lane * 4;
+          __nv_bfloat16* ol = args.out_lo + row * KEY_DIM + h * GDN_D + lane * 4;
+          __nv_bfloat16 hv[4], lv[4];
+          if (t >= len) {
+#pragma unroll
+            for (int j = 0; j < 4; ++j) hv[j] = lv[j] = __float2bfloat16_rn(0.f);
+          } else {
+            const float4 o4 = reinterpret_cast<const float4*>(x + (t * 4 + 0) * GDN_D)[lane];
+            const float4 z4 = reinterpret_cast<const float4*>(x + (t * 4 + 3) * GDN_D)[lane];
+            const float var = warp_sum(o4.x * o4.x + o4.y * o4.y + o4.z * o4.z + o4.w * o4.w) * (1.0f / GDN_D);
+            const float r = 1.0f / sqrtf(var + args.eps);
+            const float y[4] = {gw.x * (o4.x * r) * silu(z4.x), gw.y * (o4.y * r) * silu(z4.y),
+                                gw.z * (o4.z * r) * silu(z4.z), gw.w * (o4.w * r) * silu(z4.w)};
+#pragma unroll
+            for (int j = 0; j < 4; ++j) split_bf16(y[j], hv[j], lv[j]);
+          }
+          *reinterpret_cast<uint2*>(oh) = *reinterpret_cast<uint2*>(hv);
+          *reinterpret_cast<uint2*>(ol) = *reinterpret_cast<uint2*>(lv);
+        }
+      } else {
+        for (int e = tid; e < lb * GDN_D; e += GDNT_CONS) {
+          const int t = e >> 7;
+          const size_t row = (size_t)n * lb + t;
+          args.o_raw[(row * GDN_H + h) * GDN_D + (e & 127)] = t < len ? x[(t * 4 + 0) * GDN_D + (e & 127)] : 0.f;
+        }
+      }
+    }
+    fence_proxy_async();   // this thread's writes to the stage are visible to the TMA store
+    mbar_arrive(&empty[s]);
+    cur_a = nxt_a;
+    cur_b = nxt_b;
+    decay_beta(cur_a, cur_b, cur_g, cur_beta);
+  }
+}
+
+}  // namespace hsg

@@ -14,6 +14,7 @@
 #include "attn.cuh"
 #include "common.cuh"
 #include "gdn.cuh"
+#include "gdn_tc.cuh"
 #include "gemm.cuh"
 #include "norm.cuh"
 #include "ring_decode.cuh"
@@ -208,6 +209,13 @@ static int launch_gemm(cudaStream_t st, const void* w, int n_w, int K, const voi
   return HSG_OK;
 }
 
+// Tensor map of an fp16 recurrent-state pool [(slots+1)*16 tiles][128 k][128 v] viewed as [rows][128], read and
+// written in [128 k x 64 v] halves with 128-byte swizzle (gdn_tc_kernel).
+static int make_state_map(CUtensorMap* map, const void* base, int64_t slots_plus_one) {
+  return make_map_2d(map, base, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, (uint64_t)slots_plus_one * GDN_H * GDN_D, GDN_D,
+                     GDN_D * 2, 64, GDN_D, CU_TENSOR_MAP_SWIZZLE_128B);
+}
+
 // Tensor maps of the single-token decode kernel: a [rows][256] fp16 tensor read in [64 dims x 32 rows] boxes.
 static int make_decode_map(CUtensorMap* map, const void* base, uint64_t rows) {
   return make_map_2d(map, base, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, rows, ATT_D, ATT_D * 2, 64, RD_TILE,
@@ -216,8 +224,13 @@ static int make_decode_map(CUtensorMap* map, const void* base, uint64_t rows) {
 
 static int set_kernel_attributes() {
   CU(cudaFuncSetAttribute(gemm_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_MAX));
-  CU(cudaFuncSetAttribute(gdn_step_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, GDN_SMEM_LIMIT));
-  CU(cudaFuncSetAttribute(gdn_step_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, GDN_SMEM_LIMIT));
+  CU(cudaFuncSetAttribute(gdn_step_kernel<true, float>, cudaFuncAttributeMaxDynamicSharedMemorySize, GDN_SMEM_LIMIT));
+  CU(cudaFuncSetAttribute(gdn_step_kernel<false, float>, cudaFuncAttributeMaxDynamicSharedMemorySize, GDN_SMEM_LIMIT));
+  CU(cudaFuncSetAttribute(gdn_step_kernel<true, __half>, cudaFuncAttributeMaxDynamicSharedMemorySize, GDN_SMEM_LIMIT));
+  CU(cudaFuncSetAttribute(gdn_step_kernel<false, __half>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                          GDN_SMEM_LIMIT));
+  CU(cudaFuncSetAttribute(gdn_tc_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, GDN_SMEM_LIMIT));
+  CU(cudaFuncSetAttribute(gdn_tc_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, GDN_SMEM_LIMIT));
   CU(cudaFuncSetAttribute(ring_attn_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, attn_smem_bytes(4)));
   CU(cudaFuncSetAttribute(ring_attn_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, attn_smem_bytes(8)));
   CU(cudaFuncSetAttribute(ring_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, rd_smem_bytes()));
@@ -238,7 +251,8 @@ struct hsg_engine {
   int max_tokens = 0, m_alloc = 0;
   cudaStream_t stream = nullptr;
   // pools
-  float* rec = nullptr;
+  char* rec = nullptr;  // recurrent state, rec_elem bytes per element (fp16 by default, fp32 with HSG_FLAG_STATE_F32)
+  int rec_elem = 2;
   float* conv = nullptr;
   __half* ring_k = nullptr;
   __half* ring_v = nullptr;
@@ -257,6 +271,7 @@ struct hsg_engine {
   std::map<std::pair<int, int>, Bucket> graphs;
   CUtensorMap ring_maps[6][2];  // per attention layer: ring K, ring V as 2-D [rows][256] fp16, [64 x 32] SW128 boxes
   CUtensorMap new_maps[2];      // the tick's new K, V ([rows = row*2 + head][256], 1-token ticks)
+  CUtensorMap state_maps[18];   // per GDN layer: the fp16 state pool (gdn_tc_kernel)
   std::vector<void*> allocations;
   // profiling
   std::vector<cudaEvent_t> events;
@@ -265,7 +280,7 @@ struct hsg_engine {
   bool pdl = true;
   int launch_count = 0;
 
-  size_t rec_slot() const { return (size_t)GDN_H * GDN_D * GDN_D; }
+  size_t rec_slot() const { return (size_t)GDN_H * GDN_D * GDN_D; }  // elements per slot and layer
   size_t conv_slot() const { return (size_t)CONV_KEEP * CONV_DIM; }
   size_t ring_slot() const { return (size_t)ATT_HKV * RING_COLS * ATT_D; }
 };
@@ -342,13 +357,26 @@ static int enqueue_step(hsg_engine* e, int nb, int lb) {
       g.conv_w = L.conv_w; g.gnorm_w = L.gnorm_w; g.eps = eps;
       g.out_hi = e->ohi; g.out_lo = e->olo;
       g.A_log = L.A_log; g.dt_bias = L.dt_bias;
-      g.state = e->rec + (size_t)gi * (e->S + 1) * e->rec_slot();
+      g.state = e->rec + (size_t)gi * (e->S + 1) * e->rec_slot() * e->rec_elem;
       g.err = e->err;
-      g.stages = gdn_stages(lb);
       {
         ProfScope ps(e, HSG_PROF_GDN);
-        CU(launch_k(gdn_step_kernel<true>, dim3(GDN_H, std::min(nb, GDN_CTAS_PER_HEAD)), dim3(GDN_THREADS),
-                    gdn_smem_bytes(lb), st, e->pdl, g));
+        const dim3 grid(GDN_H, std::min(nb, GDN_CTAS_PER_HEAD));
+        if (e->rec_elem == 2 && lb <= GDNT_MAX_LB) {
+          g.stages = gdnt_stages(lb, true);
+          CU(launch_k(gdn_tc_kernel<true>, grid, dim3(GDNT_THREADS), gdnt_smem_bytes(lb, true), st, e->pdl,
+                      e->state_maps[gi], g));
+        } else if (e->rec_elem == 2) {
+          const int tile = GDN_D * GDN_D * 2;
+          g.stages = gdn_stages(lb, tile);
+          CU(launch_k(gdn_step_kernel<true, __half>, grid, dim3(GDN_THREADS), gdn_smem_bytes(lb, tile), st, e->pdl,
+                      g));
+        } else {
+          const int tile = GDN_D * GDN_D * 4;
+          g.stages = gdn_stages(lb, tile);
+          CU(launch_k(gdn_step_kernel<true, float>, grid, dim3(GDN_THREADS), gdn_smem_bytes(lb, tile), st, e->pdl,
+                      g));
+        }
       }
       ++gi;
     } else {
@@ -528,7 +556,8 @@ int hsg_create(const hsg_config* cfg, const hsg_weights* w, int max_slots, int d
     hsg_destroy(e);            \
     return rc;                 \
   }
-  TRY(dalloc(e, &e->rec, (size_t)e->n_gdn * S1 * e->rec_slot()));
+  e->rec_elem = (flags & HSG_FLAG_STATE_F32) ? 4 : 2;
+  TRY(dalloc(e, &e->rec, (size_t)e->n_gdn * S1 * e->rec_slot() * e->rec_elem));
   TRY(dalloc(e, &e->conv, (size_t)e->n_gdn * S1 * e->conv_slot()));
   TRY(dalloc(e, &e->ring_k, (size_t)e->n_attn * S1 * e->ring_slot()));
   TRY(dalloc(e, &e->ring_v, (size_t)e->n_attn * S1 * e->ring_slot()));
@@ -553,6 +582,9 @@ int hsg_create(const hsg_config* cfg, const hsg_weights* w, int max_slots, int d
     TRY(make_decode_map(&e->ring_maps[a][0], e->ring_k + (size_t)a * S1 * e->ring_slot(), rows));
     TRY(make_decode_map(&e->ring_maps[a][1], e->ring_v + (size_t)a * S1 * e->ring_slot(), rows));
   }
+  if (e->rec_elem == 2)
+    for (int gi = 0; gi < e->n_gdn; ++gi)
+      TRY(make_state_map(&e->state_maps[gi], e->rec + (size_t)gi * S1 * e->rec_slot() * 2, (int64_t)S1));
   TRY(make_decode_map(&e->new_maps[0], e->knew, M * ATT_HKV));
   TRY(make_decode_map(&e->new_maps[1], e->vnew, M * ATT_HKV));
 #undef TRY
@@ -687,7 +719,7 @@ int hsg_reset_all(hsg_engine* e) {
   if (!e) return fail(HSG_ERR_INVALID, "engine is NULL");
   CU(cudaSetDevice(e->device));
   const size_t S1 = (size_t)e->S + 1;
-  CU(cudaMemsetAsync(e->rec, 0, (size_t)e->n_gdn * S1 * e->rec_slot() * sizeof(float), e->stream));
+  CU(cudaMemsetAsync(e->rec, 0, (size_t)e->n_gdn * S1 * e->rec_slot() * e->rec_elem, e->stream));
   CU(cudaMemsetAsync(e->conv, 0, (size_t)e->n_gdn * S1 * e->conv_slot() * sizeof(float), e->stream));
   CU(cudaMemsetAsync(e->ring_k, 0, (size_t)e->n_attn * S1 * e->ring_slot() * sizeof(__half), e->stream));
   CU(cudaMemsetAsync(e->ring_v, 0, (size_t)e->n_attn * S1 * e->ring_slot() * sizeof(__half), e->stream));
@@ -704,7 +736,7 @@ struct PoolView {
 };
 
 static void pool_views(const hsg_engine* e, PoolView v[5]) {
-  v[0] = {(char*)e->rec, e->rec_slot() * sizeof(float), e->n_gdn};
+  v[0] = {e->rec, e->rec_slot() * e->rec_elem, e->n_gdn};
   v[1] = {(char*)e->conv, e->conv_slot() * sizeof(float), e->n_gdn};
   v[2] = {(char*)e->ring_k, e->ring_slot() * sizeof(__half), e->n_attn};
   v[3] = {(char*)e->ring_v, e->ring_slot() * sizeof(__half), e->n_attn};
@@ -761,6 +793,7 @@ int hsg_restore_slot(hsg_engine* e, int slot, const void* src) { return copy_slo
 int hsg_get_pools(const hsg_engine* e, hsg_pools* out) {
   if (!e || !out) return fail(HSG_ERR_INVALID, "NULL argument");
   out->rec = e->rec;
+  out->rec_dtype = e->rec_elem == 2 ? HSG_STATE_F16 : HSG_STATE_F32;
   out->conv = e->conv;
   out->ring_k = e->ring_k;
   out->ring_v = e->ring_v;
@@ -773,12 +806,14 @@ int hsg_get_pools(const hsg_engine* e, hsg_pools* out) {
 
 // ---- isolated kernels ---------------------------------------------------------------------------------------------
 int hsg_gdn_step(const void* packed, const float* a, const float* b, const float* A_log, const float* dt_bias,
-                 float* state, const int64_t* slots, const int64_t* lens, int n, int lb, int max_slots, float* o,
-                 int* err, void* stream) {
+                 void* state, int state_dtype, const int64_t* slots, const int64_t* lens, int n, int lb,
+                 int max_slots, float* o, int* err, void* stream) {
   if (!packed || !a || !b || !A_log || !dt_bias || !state || !slots || !lens || !o)
     return fail(HSG_ERR_INVALID, "NULL argument");
   if (n < 1 || lb < 1 || lb > MAX_LB || max_slots < 1) return fail(HSG_ERR_INVALID, "bad shape n=%d lb=%d", n, lb);
   if (reinterpret_cast<uintptr_t>(state) & 15) return fail(HSG_ERR_INVALID, "state must be 16-byte aligned");
+  if (state_dtype != HSG_STATE_F32 && state_dtype != HSG_STATE_F16)
+    return fail(HSG_ERR_INVALID, "state_dtype must be HSG_STATE_F32 or HSG_STATE_F16");
   int rc;
   if ((rc = set_kernel_attributes()) != HSG_OK) return rc;
   GdnArgs g{};
@@ -786,9 +821,21 @@ int hsg_gdn_step(const void* packed, const float* a, const float* b, const float
   g.packed = static_cast<const __nv_bfloat16*>(packed);
   g.a_raw = a; g.b_raw = b; g.o_raw = o;
   g.A_log = A_log; g.dt_bias = dt_bias; g.state = state; g.err = err;
-  g.stages = gdn_stages(lb);
-  gdn_step_kernel<false><<<dim3(GDN_H, std::min(n, GDN_CTAS_PER_HEAD)), GDN_THREADS, gdn_smem_bytes(lb),
-                           (cudaStream_t)stream>>>(g);
+  const dim3 grid(GDN_H, std::min(n, GDN_CTAS_PER_HEAD));
+  if (state_dtype == HSG_STATE_F16 && lb <= GDNT_MAX_LB) {
+    CUtensorMap tm;
+    if ((rc = make_state_map(&tm, state, (int64_t)max_slots + 1)) != HSG_OK) return rc;
+    g.stages = gdnt_stages(lb, false);
+    gdn_tc_kernel<false><<<grid, GDNT_THREADS, gdnt_smem_bytes(lb, false), (cudaStream_t)stream>>>(tm, g);
+  } else if (state_dtype == HSG_STATE_F16) {
+    const int tile = GDN_D * GDN_D * 2;
+    g.stages = gdn_stages(lb, tile);
+    gdn_step_kernel<false, __half><<<grid, GDN_THREADS, gdn_smem_bytes(lb, tile), (cudaStream_t)stream>>>(g);
+  } else {
+    const int tile = GDN_D * GDN_D * 4;
+    g.stages = gdn_stages(lb, tile);
+    gdn_step_kernel<false, float><<<grid, GDN_THREADS, gdn_smem_bytes(lb, tile), (cudaStream_t)stream>>>(g);
+  }
   CU(cudaGetLastError());
   return HSG_OK;
 }

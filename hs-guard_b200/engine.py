@@ -61,14 +61,17 @@ class SlotEngine:
     """Fixed per-slot state pools on one GPU and one tick per call (see module docstring).
 
     model: a reference ``Classifier`` (``.backbone`` + ``.heads``), a ``RandomInitModel`` or a reference-named state
-    dict. ``precise_activations=False`` feeds the tensor cores bf16 activations only (the reference's autocast
-    precision) instead of the hi/lo pair.
+    dict. ``state_dtype`` is the recurrent state's storage type, "float16" (what the reference's StreamingGuard
+    uses, runtime.py:157) or "float32". ``precise_activations=False`` feeds the tensor cores bf16 activations only
+    (the reference's autocast precision) instead of the hi/lo pair.
     """
 
     def __init__(self, model, max_slots, head="redline", device=None, session_buckets=None,
-                 precise_activations=True, roles=ROLES):
+                 precise_activations=True, roles=ROLES, state_dtype="float16"):
         if not isinstance(max_slots, int) or max_slots < 1:
             raise ValueError("max_slots must be a positive integer")
+        if state_dtype not in ("float16", "float32"):
+            raise ValueError("state_dtype must be float16 or float32")
         if tuple(roles) != ROLES:
             raise ValueError("the engine computes both roles (user, assistant)")
         cfg, sd = extract_state_dict(model, head)
@@ -84,7 +87,9 @@ class SlotEngine:
         self._cw = c_weights(self.weights)
         self._cc = c_config(cfg)
         handle = C.c_void_p()
-        flags = 0 if precise_activations else _lib.HSG_FLAG_BF16_ACT
+        flags = (0 if precise_activations else _lib.HSG_FLAG_BF16_ACT) | \
+            (_lib.HSG_FLAG_STATE_F32 if state_dtype == "float32" else 0)
+        self.state_dtype = state_dtype
         check(self._lib.hsg_create(C.byref(self._cc), C.byref(self._cw), max_slots, self.device.index, flags,
                                    C.byref(handle)))
         self._h = handle
@@ -145,7 +150,8 @@ class SlotEngine:
 
         def view(addr, shape, dtype):
             return _from_device(addr, int(np.prod(shape)), dtype, self.device).view(shape)
-        return {"rec": view(p.rec, (p.n_gdn, S1, c.gdn_heads, c.gdn_head_dim, c.gdn_head_dim), torch.float32),
+        rec_dtype = torch.float16 if p.rec_dtype == _lib.HSG_STATE_F16 else torch.float32
+        return {"rec": view(p.rec, (p.n_gdn, S1, c.gdn_heads, c.gdn_head_dim, c.gdn_head_dim), rec_dtype),
                 "conv": view(p.conv, (p.n_gdn, S1, c.conv_kernel - 1, c.conv_dim), torch.float32),
                 "ring_k": view(p.ring_k, (p.n_attn, S1, c.kv_heads, c.window + 1, c.attn_head_dim), torch.float16),
                 "ring_v": view(p.ring_v, (p.n_attn, S1, c.kv_heads, c.window + 1, c.attn_head_dim), torch.float16),

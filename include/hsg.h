@@ -81,19 +81,25 @@ typedef struct hsg_engine hsg_engine;
 
 /* Device pointers of the engine's state pools (for snapshots, tests and diagnostics). S = max_slots; slot S is
  * the scratch slot padded rows use (reference engine/bucketed_engine.py:37-42). */
+#define HSG_STATE_F32 0
+#define HSG_STATE_F16 1
 typedef struct hsg_pools {
-  float* rec;          /* [n_gdn=18][S+1][16][128][128] fp32 gated-delta-rule state */
+  void* rec;           /* [n_gdn=18][S+1][16][128][128] gated-delta-rule state, element type rec_dtype */
   float* conv;         /* [18][S+1][3][6144] fp32 causal-conv history */
   void* ring_k;        /* [n_attn=6][S+1][2][513][256] fp16 */
   void* ring_v;        /* same */
   int64_t* ring_pos;   /* [S+1][513], -1 = empty; column 512 is scratch */
   int32_t max_slots, n_gdn, n_attn;
+  int32_t rec_dtype;   /* HSG_STATE_F16 (default) or HSG_STATE_F32 */
 } hsg_pools;
 
 /* Create an engine for slots 0..max_slots-1 on CUDA device `device` (replaces SlotStreamEngineV8.__init__,
- * engine/slot_engine_v8.py:179-195, with pools of engine/bucketed_engine.py:37-42). flags: HSG_FLAG_BF16_ACT feeds
- * the GEMMs the bf16 activation only (the reference's autocast precision) instead of the hi/lo pair. */
+ * engine/slot_engine_v8.py:179-195, with pools of engine/bucketed_engine.py:37-42). The recurrent state is stored
+ * as fp16, the state_dtype StreamingGuard gives the reference engine (runtime.py:157); HSG_FLAG_STATE_F32 keeps it in
+ * fp32 instead. HSG_FLAG_BF16_ACT feeds the GEMMs the bf16 activation only (the reference's autocast precision)
+ * instead of the hi/lo pair. */
 #define HSG_FLAG_BF16_ACT 1
+#define HSG_FLAG_STATE_F32 2
 int hsg_create(const hsg_config* cfg, const hsg_weights* weights, int max_slots, int device, int flags,
                hsg_engine** out);
 int hsg_destroy(hsg_engine* eng);
@@ -141,11 +147,11 @@ int hsg_launches_per_step(const hsg_engine* eng, int nb, int lb);
 
 /* Gated-delta-rule slot step with the contract of the reference's gdn_slot_v8 (engine/fused_kernels.py:197-211):
  * packed [n][lb][6144] bf16 (q | k | v after conv+SiLU), a, b [n][lb][16] fp32 raw projections, A_log, dt_bias [16],
- * state [max_slots+1][16][128][128] fp32 updated in place at rows slots[i] with lens[i] > 0; writes
- * o [n][lb][16][128] fp32 (zeros at padded positions). All device pointers. */
+ * state [max_slots+1][16][128][128] (HSG_STATE_F32 or HSG_STATE_F16) updated in place at rows slots[i] with
+ * lens[i] > 0; writes o [n][lb][16][128] fp32 (zeros at padded positions). All device pointers. */
 int hsg_gdn_step(const void* packed, const float* a, const float* b, const float* A_log, const float* dt_bias,
-                 float* state, const int64_t* slots, const int64_t* lens, int n, int lb, int max_slots, float* o,
-                 int* err, void* stream);
+                 void* state, int state_dtype, const int64_t* slots, const int64_t* lens, int n, int lb,
+                 int max_slots, float* o, int* err, void* stream);
 
 /* Ring-window GQA attention with the contract of the reference's ring_attention (engine/ring_attention_kernel.py:
  * 164-178): q [n][2][4*lb][256] fp32, ring_k/v [max_slots+1][2][513][256] fp16, new_k/v [n][2][lb][256] fp16,

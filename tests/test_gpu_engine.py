@@ -13,11 +13,14 @@ P_TOL = 2e-3       # |delta p| per class (the north-star bound on p(safe))
 STATE_RTOL = 1e-2  # recurrent state vs the reference streaming path
 
 
-@pytest.fixture(scope="module")
-def engine_run(golden, weights_seed0):
+@pytest.fixture(scope="module", params=["float16", "float32"])
+def engine_run(request, golden, weights_seed0):
+    """The script through the engine with the recurrent state stored in fp16 (default, the reference StreamingGuard's
+    state_dtype) and in fp32."""
     from hs_guard_b200.engine import SlotEngine
     assert W.state_dict_digest(weights_seed0) == str(golden["weights_digest"])
-    eng = SlotEngine(weights_seed0, STREAM_MAX_SLOTS)
+    eng = SlotEngine(weights_seed0, STREAM_MAX_SLOTS, state_dtype=request.param)
+    assert eng.pools()["rec"].dtype == getattr(torch, request.param)
     pu, pa = [], []
     for tick in stream_script():
         res = eng.step(tick)
@@ -59,7 +62,7 @@ def test_ring_and_lengths_bit_exact(golden, engine_run):
 def test_state_pools_match_reference(golden, engine_run):
     eng, _, _ = engine_run
     pools = eng.pools()
-    rec = pools["rec"][:, :STREAM_MAX_SLOTS].cpu()
+    rec = pools["rec"][:, :STREAM_MAX_SLOTS].float().cpu()
     norms = rec.pow(2).sum((-1, -2)).sqrt().numpy()
     np.testing.assert_allclose(norms, golden["stream_rec_norm"], rtol=STATE_RTOL)
     sample = rec.reshape(-1)[torch.from_numpy(sample_index(rec.numel(), 1))].numpy()
