@@ -1,25 +1,30 @@
 // Gated delta rule slot step for fp16 recurrent state and ticks of up to 16 tokens, with the state-vector products
 // on the tensor cores (warp-level mma.sync). Longer ticks use gdn_step_kernel<., __half> (gdn.cuh).
 //
-// Work split and pipeline as in gdn.cuh: a persistent, head-stationary grid (16 heads x 9 CTAs); a producer warp
-// streams each (row, head) item's inputs into a STAGES-deep shared-memory ring with TMA and writes the updated state
-// back with TMA. Eight consumer warps process one item at a time:
+// Persistent, head-stationary grid (16 heads x 9 CTAs, one per SM); work item = (session row, head). Warp roles:
 //
-//  * Prologue. Thread c < 128 runs the causal conv of q and k channel c (FUSED) or widens them from bf16 (RAW), and
-//    writes k back as fp32 plus the MMA operand columns k_hi, k_lo, q_hi, q_lo in fp16 (hi = fp16(x),
-//    lo = fp16(x - hi)); its warp adds up the per-token partial sums of q.q, k.k and q.k. Thread 128 + c does the
-//    same for v channel c, then the decay e^g and beta of token c. One barrier.
-//  * The fp16 state tile arrives by 2-D TMA as two [128 k][64 v] halves with 128-byte swizzle (one tensor map over
-//    the pool viewed as [(S+1)*16*128 rows][128]); warp w loads the sixteen v columns [16 w, 16 w + 16) for all
-//    128 k with `ldmatrix.trans` as eight 16 x 16 fragments of A = S^T and keeps them in registers as fp32 for the
-//    whole tick.
-//  * Per token, no barrier: one m16n8k16 MMA per fragment against B = [k_hi | k_lo | q_hi | q_lo | 0 0 0 0] gives
-//    S^T k and S^T q for the warp's columns, exact up to the fp16 state; then
-//      delta = beta (v - e^g rk S^T k),   o = e^g rq S^T q + (k.q) rk rq delta,   S <- e^g S + rk k delta^T
-//    (rk, rq: the L2-norm factors with eps 1e-6, rq including 128^-1/2), the update applied to the fragments with
-//    packed fp32x2 arithmetic.
-//  * After the tick's last token the fragments are rounded to fp16 once and written back with `stmatrix.trans`; one
-//    barrier; the gated RMSNorm epilogue as in gdn.cuh.
+//  * Producer warp (warp 9). Streams each item's inputs into a STAGES-deep shared-memory ring with TMA: the fp16
+//    state tile as two [128 k][64 v] halves with 128-byte swizzle (one 2-D tensor map over the pool viewed as
+//    [(S+1)*16*128 rows][128]), the q/k/v/z projection slices (FUSED) or bf16 q|k|v (RAW), the raw b|a gate inputs
+//    and the conv history. When a stage is released it writes the item's new state back (two 2-D TMA stores) and
+//    loads the next item into it.
+//  * Epilogue warp (warp 8). When the consumers are done with an item it writes the item's output rows -- the gated
+//    RMSNorm w * (o * rsqrt(mean(o^2) + eps)) * silu(z) as the out_proj operand (bf16 hi/lo pair), or the raw o --
+//    and releases the stage to the producer.
+//  * Eight consumer warps, one item at a time:
+//    - prologue: thread c < 128 runs the causal conv of q and k channel c (FUSED) or widens them (RAW), writes k back
+//      as fp32 and the MMA operand columns k_hi, k_lo, q_hi, q_lo in fp16 (hi = fp16(x), lo = fp16(x - hi)); its
+//      warp adds up per-token partial sums of q.q, k.k, q.k. Thread 128 + c does v channel c, then e^g and beta of
+//      token c. Warp w also loads the state columns v in [16 w, 16 w + 16), all 128 k, with `ldmatrix.trans` as
+//      eight 16 x 16 fragments of A = S^T. One barrier (the only block barrier per item).
+//    - per token, no barrier: one m16n8k16 MMA per fragment against B = [k_hi | k_lo | q_hi | q_lo | unused x 4]
+//      gives S^T k and S^T q for the warp's columns, exact up to the fp16 state; then
+//        delta = beta (v - e^g rk S^T k),   o = e^g rq S^T q + (k.q) rk rq delta,   S <- e^g S + rk k delta^T
+//      (rk, rq: L2-norm factors with eps 1e-6, rq including 128^-1/2); the state stays in registers as fp32 across
+//      the tick's tokens and is updated with packed fp32x2 arithmetic.
+//    - after the last token: round to fp16 once, `stmatrix.trans` back into the stage, release the stage.
+//    Per-item scratch (operand columns, partial sums, decay, beta) alternates between two buffers by item parity,
+//    so a warp may start the next item's prologue while others finish this item's tokens.
 // The reference keeps StreamingGuard's state in fp16 (runtime.py:157) and computes in fp32 inside its kernel
 // (engine/fused_kernels.py:140-194, gdn_slot_kernel.py:66), rounding once per tick: the same here.
 #pragma once
@@ -29,27 +34,31 @@ namespace hsg {
 
 constexpr int GDNT_CONS = 256;                 // 8 consumer warps
 constexpr int GDNT_CWARPS = GDNT_CONS / 32;
-constexpr int GDNT_THREADS = GDNT_CONS + 32;   // + producer warp
+constexpr int GDNT_EPI_WARP = GDNT_CWARPS;     // warp 8
+constexpr int GDNT_PROD_WARP = GDNT_CWARPS + 1; // warp 9
+constexpr int GDNT_THREADS = GDNT_CONS + 64;
 constexpr int GDNT_MAX_LB = 16;
 constexpr int GDNT_HALF = GDN_D * 64 * 2;      // one [128 k][64 v] fp16 half of the tile: 16 KB
 constexpr int GDNT_TILE = 2 * GDNT_HALF;
+constexpr int GDNT_AB = 32;                    // per token: b[16] | a[16] fp32
 
-// Stage: state halves | x [lb][4][128] fp32 (q, k, v, z) | FUSED: conv history [9][128] fp32, RAW: bf16 q|k|v
-// [lb][3][128]; rounded up to 1 KB so every stage's tile is 1024-aligned for the swizzle.
+// Stage: state halves | x [lb][4][128] fp32 (q, k, v, z; o replaces q) | ab [lb][32] fp32 | FUSED: conv history
+// [9][128] fp32, RAW: bf16 q|k|v [lb][3][128]; rounded up to 1 KB so every stage's tile is 1024-aligned.
 __host__ __device__ inline int gdnt_stage_bytes(int lb, bool fused) {
-  return (GDNT_TILE + lb * 4 * GDN_D * 4 + (fused ? 9 * GDN_D * 4 : lb * 3 * GDN_D * 2) + 1023) & ~1023;
+  return (GDNT_TILE + lb * 4 * GDN_D * 4 + lb * GDNT_AB * 4 + (fused ? 9 * GDN_D * 4 : lb * 3 * GDN_D * 2) + 1023) &
+         ~1023;
 }
-__host__ __device__ inline int gdnt_fixed_bytes() {
-  // B operand columns [16][4][128] fp16 | norm partials [16][3][4] f32 | g, beta [16] | meta, full, empty | align
-  return GDNT_MAX_LB * 4 * GDN_D * 2 + GDNT_MAX_LB * 12 * 4 + 2 * GDNT_MAX_LB * 4 + GDN_MAX_STAGES * (16 + 2 * 8) +
-         1024;
+// Per-item scratch, x2 (item parity): operand columns [lb][4][128] fp16 | partials [lb][3][4] f32 | e^g, beta [lb]
+__host__ __device__ inline int gdnt_scratch_bytes(int lb) { return lb * 4 * GDN_D * 2 + lb * 12 * 4 + 2 * lb * 4; }
+__host__ __device__ inline int gdnt_fixed_bytes(int lb) {
+  return 2 * ((gdnt_scratch_bytes(lb) + 15) & ~15) + GDN_MAX_STAGES * (16 + 3 * 8) + 1024;
 }
 __host__ __device__ inline int gdnt_stages(int lb, bool fused) {
-  int s = (GDN_SMEM_LIMIT - gdnt_fixed_bytes()) / gdnt_stage_bytes(lb, fused);
+  int s = (GDN_SMEM_LIMIT - gdnt_fixed_bytes(lb)) / gdnt_stage_bytes(lb, fused);
   return s > GDN_MAX_STAGES ? GDN_MAX_STAGES : (s < 1 ? 1 : s);
 }
 __host__ __device__ inline int gdnt_smem_bytes(int lb, bool fused) {
-  return gdnt_stages(lb, fused) * gdnt_stage_bytes(lb, fused) + gdnt_fixed_bytes();
+  return gdnt_stages(lb, fused) * gdnt_stage_bytes(lb, fused) + gdnt_fixed_bytes(lb);
 }
 
 template <bool FUSED>
@@ -59,40 +68,46 @@ gdn_tc_kernel(const __grid_constant__ CUtensorMap tm_state, const GdnArgs args) 
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(gdnt_smem_raw) + 1023) & ~uintptr_t(1023));
   const int lb = args.lb, S = args.stages;
   const int sbytes = gdnt_stage_bytes(lb, FUSED);
+  const int scratch = (gdnt_scratch_bytes(lb) + 15) & ~15;
   uint8_t* fixed = smem + S * sbytes;
-  __half* bop = reinterpret_cast<__half*>(fixed);                        // [16][4][128]: k_hi, k_lo, q_hi, q_lo
-  float* part = reinterpret_cast<float*>(bop + GDNT_MAX_LB * 4 * GDN_D);  // [16][3][4]: q.q, k.k, q.k per q/k warp
-  float* gv = part + GDNT_MAX_LB * 12;                                    // e^g per token
-  float* bv = gv + GDNT_MAX_LB;                                           // beta per token
-  GdnMeta* meta = reinterpret_cast<GdnMeta*>(bv + GDNT_MAX_LB);
+  GdnMeta* meta = reinterpret_cast<GdnMeta*>(fixed + 2 * scratch);
   uint64_t* full = reinterpret_cast<uint64_t*>(meta + GDN_MAX_STAGES);
-  uint64_t* empty = full + GDN_MAX_STAGES;
+  uint64_t* done = full + GDN_MAX_STAGES;   // consumers -> epilogue warp
+  uint64_t* empty = done + GDN_MAX_STAGES;  // epilogue warp -> producer
 
   const int h = blockIdx.x, p = blockIdx.y, P = gridDim.y;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int n_items = args.nb > p ? (args.nb - p + P - 1) / P : 0;
   auto row_of = [&](int i) { return p + i * P; };
   auto stage_ptr = [&](int s) { return smem + s * sbytes; };
+  auto x_of = [&](int s) { return reinterpret_cast<float*>(stage_ptr(s) + GDNT_TILE); };
   auto tile_row = [&](int64_t slot) { return (int)((slot * GDN_H + h) * GDN_D); };
 
   if (tid == 0) {
     for (int s = 0; s < S; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&empty[s], GDNT_CONS);
+      mbar_init(&done[s], GDNT_CONS);
+      mbar_init(&empty[s], 1);
     }
     fence_barrier_init();
     prefetch_tmap(&tm_state);
   }
   __syncthreads();
 
-  if (warp == GDNT_CWARPS) {
+  if (warp == GDNT_PROD_WARP) {
     // ===================================== producer =====================================
     int64_t held_slot[GDN_MAX_STAGES] = {};
     int held_len[GDN_MAX_STAGES] = {};
+    // each item's length and slot are loaded one item ahead, off the critical path
+    int64_t nxt_len = n_items > 0 ? args.lens[row_of(0)] : 0, nxt_slot = n_items > 0 ? args.slots[row_of(0)] : 0;
     auto issue_state = [&](int i) {
-      const int s = i % S, n = row_of(i);
-      int len = (int)args.lens[n];
-      const int64_t slot = args.slots[n];
+      const int s = i % S;
+      int len = (int)nxt_len;
+      const int64_t slot = nxt_slot;
+      if (i + 1 < n_items) {
+        nxt_len = args.lens[row_of(i + 1)];
+        nxt_slot = args.slots[row_of(i + 1)];
+      }
       if (len < 0 || len > lb) {
         if (lane == 0) set_error(args.err, ERR_BAD_LEN);
         len = 0;
@@ -104,12 +119,12 @@ gdn_tc_kernel(const __grid_constant__ CUtensorMap tm_state, const GdnArgs args) 
       held_slot[s] = slot;
       held_len[s] = len;
       uint8_t* st = stage_ptr(s);
-      float* hist = reinterpret_cast<float*>(st + GDNT_TILE) + lb * 4 * GDN_D;
+      float* hist = x_of(s) + lb * (4 * GDN_D + GDNT_AB);
       if (lane == 0) {
         meta[s].slot = slot;
         meta[s].len = len;
         if (len > 0)
-          mbar_arrive_expect_tx(&full[s], GDNT_TILE +
+          mbar_arrive_expect_tx(&full[s], GDNT_TILE + len * GDNT_AB * 4 +
                                               (FUSED ? len * 4 * GDN_D * 4 + 9 * GDN_D * 4 : len * 3 * GDN_D * 2));
         else
           mbar_arrive(&full[s]);
@@ -129,19 +144,24 @@ gdn_tc_kernel(const __grid_constant__ CUtensorMap tm_state, const GdnArgs args) 
     auto issue_inputs = [&](int i) {
       const int s = i % S, n = row_of(i), len = held_len[s];
       if (len == 0) return;
-      float* x = reinterpret_cast<float*>(stage_ptr(s) + GDNT_TILE);
+      float* x = x_of(s);
+      float* ab = x + lb * 4 * GDN_D;
       if (FUSED) {
-        for (int j = lane; j < len * 4; j += 32) {  // q, k, v, z slices of each token: 4 x 512 B
-          const int t = j >> 2, part = j & 3;
-          const float* src = args.proj + ((size_t)n * lb + t) * GDN_IN + part * KEY_DIM + h * GDN_D;
-          bulk_g2s(x + (t * 4 + part) * GDN_D, src, GDN_D * 4, &full[s]);
+        for (int j = lane; j < len * 5; j += 32) {  // q, k, v, z slices (4 x 512 B) and b|a (128 B) of each token
+          const int t = j / 5, part = j % 5;
+          const float* row = args.proj + ((size_t)n * lb + t) * GDN_IN;
+          if (part < 4) bulk_g2s(x + (t * 4 + part) * GDN_D, row + part * KEY_DIM + h * GDN_D, GDN_D * 4, &full[s]);
+          else bulk_g2s(ab + t * GDNT_AB, row + GDN_B_OFF, GDNT_AB * 4, &full[s]);
         }
       } else {
-        __nv_bfloat16* xb = reinterpret_cast<__nv_bfloat16*>(x + lb * 4 * GDN_D);
-        for (int j = lane; j < len * 3; j += 32) {
-          const int t = j / 3, part = j % 3;
-          const __nv_bfloat16* src = args.packed + ((size_t)n * lb + t) * CONV_DIM + part * KEY_DIM + h * GDN_D;
-          bulk_g2s(xb + (t * 3 + part) * GDN_D, src, GDN_D * 2, &full[s]);
+        __nv_bfloat16* xb = reinterpret_cast<__nv_bfloat16*>(ab + lb * GDNT_AB);
+        for (int j = lane; j < len * 5; j += 32) {  // q, k, v (3 x 256 B), b, a (2 x 64 B) of each token
+          const int t = j / 5, part = j % 5;
+          const size_t rt = (size_t)n * lb + t;
+          if (part < 3) bulk_g2s(xb + (t * 3 + part) * GDN_D, args.packed + rt * CONV_DIM + part * KEY_DIM + h * GDN_D,
+                                 GDN_D * 2, &full[s]);
+          else bulk_g2s(ab + t * GDNT_AB + (part - 3) * GDN_H, (part == 3 ? args.b_raw : args.a_raw) + rt * GDN_H,
+                        GDN_H * 4, &full[s]);
         }
       }
     };
@@ -152,7 +172,7 @@ gdn_tc_kernel(const __grid_constant__ CUtensorMap tm_state, const GdnArgs args) 
     for (int i = S; i < n_items + S; ++i) {
       const int s = i % S, r = i / S;
       if (i - S < n_items) {
-        // the consumers are done with item i - S in stage s: write its state back
+        // item i - S is finished (outputs written): write its state back
         if (!mbar_wait(&empty[s], (r - 1) & 1, args.err, ERR_TIMEOUT_TMA)) break;
         if (lane == 0 && held_len[s] > 0) {
           tma_store_2d(&tm_state, stage_ptr(s), 0, tile_row(held_slot[s]));
@@ -170,12 +190,58 @@ gdn_tc_kernel(const __grid_constant__ CUtensorMap tm_state, const GdnArgs args) 
     return;
   }
 
+  if (warp == GDNT_EPI_WARP) {
+    // ===================================== epilogue =====================================
+    const float4 gw = FUSED ? reinterpret_cast<const float4*>(args.gnorm_w)[lane] : make_float4(0.f, 0.f, 0.f, 0.f);
+    // item j in stage s is done by the consumers: its output rows (o sits in the q slot of x)
+    auto epilogue = [&](int j, int s) {
+      const int n = row_of(j), len = meta[s].len;
+      const float* x = x_of(s);
+      for (int t = 0; t < lb; ++t) {
+        const size_t row = (size_t)n * lb + t;
+        if (FUSED) {
+          __nv_bfloat16 hv[4], lv[4];
+          if (t >= len) {
+#pragma unroll
+            for (int q = 0; q < 4; ++q) hv[q] = lv[q] = __float2bfloat16_rn(0.f);
+          } else {
+            const float4 o4 = reinterpret_cast<const float4*>(x + (t * 4 + 0) * GDN_D)[lane];
+            const float4 z4 = reinterpret_cast<const float4*>(x + (t * 4 + 3) * GDN_D)[lane];
+            const float var = warp_sum(o4.x * o4.x + o4.y * o4.y + o4.z * o4.z + o4.w * o4.w) * (1.0f / GDN_D);
+            const float r = rsqrtf(var + args.eps);
+            split_bf16(gw.x * (o4.x * r) * silu_fast(z4.x), hv[0], lv[0]);
+            split_bf16(gw.y * (o4.y * r) * silu_fast(z4.y), hv[1], lv[1]);
+            split_bf16(gw.z * (o4.z * r) * silu_fast(z4.z), hv[2], lv[2]);
+            split_bf16(gw.w * (o4.w * r) * silu_fast(z4.w), hv[3], lv[3]);
+          }
+          *reinterpret_cast<uint2*>(args.out_hi + row * KEY_DIM + h * GDN_D + lane * 4) =
+              *reinterpret_cast<uint2*>(hv);
+          *reinterpret_cast<uint2*>(args.out_lo + row * KEY_DIM + h * GDN_D + lane * 4) =
+              *reinterpret_cast<uint2*>(lv);
+        } else {
+          const float4 o4 = t < len ? reinterpret_cast<const float4*>(x + (t * 4 + 0) * GDN_D)[lane]
+                                    : make_float4(0.f, 0.f, 0.f, 0.f);
+          reinterpret_cast<float4*>(args.o_raw + (row * GDN_H + h) * GDN_D)[lane] = o4;
+        }
+      }
+      __syncwarp();
+      fence_proxy_async();  // the reads above are ordered before the TMA writes that refill the stage
+    };
+    pdl_wait();  // the outputs may still be read by an earlier kernel
+    for (int i = 0; i < n_items; ++i) {
+      const int s = i % S;
+      if (!mbar_wait(&done[s], (i / S) & 1, args.err, ERR_TIMEOUT_TMA)) break;
+      epilogue(i, s);
+      if (lane == 0) mbar_arrive(&empty[s]);
+    }
+    return;
+  }
+
   // ===================================== consumers =====================================
   const int c = tid & (GDN_D - 1);             // prologue channel
   const bool qk_thread = tid < GDN_D;          // thread c: q and k channel c; thread 128 + c: v channel c
   const int g = lane >> 2, t4 = lane & 3;      // mma fragment coordinates
-  // conv weights: q/k threads hold q's (cw) and k's (cw2) taps of channel c, v threads v's taps
-  float4 cw = make_float4(0.f, 0.f, 0.f, 0.f), cw2 = cw;
+  float4 cw = make_float4(0.f, 0.f, 0.f, 0.f), cw2 = cw;  // conv taps: q (or v) and k of channel c
   if (FUSED) {
     const float4* w4 = reinterpret_cast<const float4*>(args.conv_w);
     if (qk_thread) {
@@ -185,67 +251,36 @@ gdn_tc_kernel(const __grid_constant__ CUtensorMap tm_state, const GdnArgs args) 
       cw = w4[2 * KEY_DIM + h * GDN_D + c];
     }
   }
-  const float4 gw = FUSED ? reinterpret_cast<const float4*>(args.gnorm_w)[lane] : make_float4(0.f, 0.f, 0.f, 0.f);
   const float negA = -expf(args.A_log[h]), dtb = args.dt_bias[h];
   // this lane's ldmatrix/stmatrix row within each 16 x 16 fragment: k row and 16-byte v chunk of its 8 x 8 matrix
   const int frag_k = (lane & 7) + ((lane >> 4) & 1) * 8;
   const int frag_c = 2 * (warp & 3) + ((lane >> 3) & 1);
-
-  // a, b of token tid - 128 of an item (v threads), loaded one item ahead so the latency hides behind compute
-  auto load_ab = [&](int i, float& a, float& b) {
-    a = 0.f;
-    b = 0.f;
-    const int t = tid - GDN_D;
-    if (i >= n_items || t < 0 || t >= lb) return;
-    const int n = row_of(i);  // padded tokens' values are loaded too (in bounds) and never used
-    if (FUSED) {
-      const float* row = args.proj + ((size_t)n * lb + t) * GDN_IN;
-      a = row[GDN_A_OFF + h];
-      b = row[GDN_B_OFF + h];
-    } else {
-      a = args.a_raw[((size_t)n * lb + t) * GDN_H + h];
-      b = args.b_raw[((size_t)n * lb + t) * GDN_H + h];
-    }
-  };
-  // decay e^g and beta of a token from its raw a, b
-  auto decay_beta = [&](float a, float b, float& eg, float& beta) {
-    const float xg = a + dtb;
-    const float sp = xg > 20.f ? xg : log1pf(expf(xg));
-    eg = expf(negA * sp);
-    beta = sigmoidf_(b);
-  };
+  const float scale = 0.08838834764831845f;  // 128^-1/2, correctly rounded
+  const int v0 = 16 * warp + g;
   pdl_wait();
   if (tid == 0) pdl_trigger();
-  float cur_a, cur_b, cur_g, cur_beta;
-  load_ab(0, cur_a, cur_b);
-  decay_beta(cur_a, cur_b, cur_g, cur_beta);
 
   for (int i = 0; i < n_items; ++i) {
-    float nxt_a, nxt_b;
-    load_ab(i + 1, nxt_a, nxt_b);
-    const int s = i % S, n = row_of(i);
+    const int s = i % S;
     uint8_t* st = stage_ptr(s);
-    float* x = reinterpret_cast<float*>(st + GDNT_TILE);
-    // Each warp waits for the stage itself (no block barrier: warp 7 may still be finishing the previous item's
-    // epilogue); the first barrier below combines the outcomes so that every warp leaves together on a failure.
+    float* x = x_of(s);
+    uint8_t* scr = fixed + (i & 1) * scratch;
+    __half* bop = reinterpret_cast<__half*>(scr);                     // [lb][4][128]: k_hi, k_lo, q_hi, q_lo
+    float* part = reinterpret_cast<float*>(bop + lb * 4 * GDN_D);     // [lb][3][4]: q.q, k.k, q.k per q/k warp
+    float* gv = part + lb * 12;                                       // e^g per token
+    float* bv = gv + lb;                                              // beta per token
+    // Each warp waits for the stage itself; the barrier below combines the outcomes so that every warp leaves
+    // together on a failure.
     const bool ok = mbar_wait(&full[s], (i / S) & 1, args.err, ERR_TIMEOUT_TMA);
     const int len = ok ? meta[s].len : 0;
-    const int64_t slot = ok ? meta[s].slot : 0;
     if (len == 0) {
       if (!named_sync_and<GDNT_CONS>(ok)) break;
-      for (int e = tid; e < lb * GDN_D; e += GDNT_CONS) {
-        const size_t row = (size_t)n * lb + e / GDN_D;
-        if (FUSED) {
-          args.out_hi[row * KEY_DIM + h * GDN_D + (e & 127)] = __float2bfloat16_rn(0.f);
-          args.out_lo[row * KEY_DIM + h * GDN_D + (e & 127)] = __float2bfloat16_rn(0.f);
-        } else {
-          args.o_raw[(row * GDN_H + h) * GDN_D + (e & 127)] = 0.f;
-        }
-      }
     } else {
+      const int64_t slot = meta[s].slot;
       // ---- prologue ----
-      const float* hist = x + lb * 4 * GDN_D;
-      const __nv_bfloat16* raw = reinterpret_cast<const __nv_bfloat16*>(x + lb * 4 * GDN_D);
+      const float* ab = x + lb * 4 * GDN_D;
+      const float* hist = ab + lb * GDNT_AB;
+      const __nv_bfloat16* raw = reinterpret_cast<const __nv_bfloat16*>(hist);
       if (qk_thread) {
         float q0 = 0.f, q1 = 0.f, q2 = 0.f, k0 = 0.f, k1 = 0.f, k2 = 0.f;
         if (FUSED) {
@@ -256,8 +291,8 @@ gdn_tc_kernel(const __grid_constant__ CUtensorMap tm_state, const GdnArgs args) 
           float qv, kv;
           if (FUSED) {
             const float xq = x[(t * 4 + 0) * GDN_D + c], xk = x[(t * 4 + 1) * GDN_D + c];
-            qv = silu(fmaf(cw.w, xq, fmaf(cw.z, q2, fmaf(cw.y, q1, cw.x * q0))));
-            kv = silu(fmaf(cw2.w, xk, fmaf(cw2.z, k2, fmaf(cw2.y, k1, cw2.x * k0))));
+            qv = silu_fast(fmaf(cw.w, xq, fmaf(cw.z, q2, fmaf(cw.y, q1, cw.x * q0))));
+            kv = silu_fast(fmaf(cw2.w, xk, fmaf(cw2.z, k2, fmaf(cw2.y, k1, cw2.x * k0))));
             q0 = q1; q1 = q2; q2 = xq;
             k0 = k1; k1 = k2; k2 = xk;
           } else {
@@ -289,7 +324,7 @@ gdn_tc_kernel(const __grid_constant__ CUtensorMap tm_state, const GdnArgs args) 
           for (int t = 0; t < len; ++t) {
             float* xp = x + (t * 4 + 2) * GDN_D + c;
             const float xv = *xp;
-            *xp = silu(fmaf(cw.w, xv, fmaf(cw.z, e2, fmaf(cw.y, e1, cw.x * e0))));
+            *xp = silu_fast(fmaf(cw.w, xv, fmaf(cw.z, e2, fmaf(cw.y, e1, cw.x * e0))));
             e0 = e1; e1 = e2; e2 = xv;
           }
           float* gp = args.conv_pool + (size_t)slot * CONV_KEEP * CONV_DIM + 2 * KEY_DIM + h * GDN_D + c;
@@ -297,12 +332,14 @@ gdn_tc_kernel(const __grid_constant__ CUtensorMap tm_state, const GdnArgs args) 
         } else {
           for (int t = 0; t < len; ++t) x[(t * 4 + 2) * GDN_D + c] = __bfloat162float(raw[(t * 3 + 2) * GDN_D + c]);
         }
-        if (c < len) {
-          gv[c] = cur_g;
-          bv[c] = cur_beta;
+        if (c < len) {  // g = -exp(A_log) softplus(a + dt_bias) (threshold 20), beta = sigmoid(b)
+          const float xg = ab[c * GDNT_AB + GDN_H + h] + dtb;
+          const float sp = xg > 20.f ? xg : log1pf(expf(xg));
+          gv[c] = expf(negA * sp);
+          bv[c] = sigmoidf_(ab[c * GDNT_AB + h]);
         }
       }
-      // ---- this warp's state columns: A = S^T fragments (v 16 w + [0, 16), k 16 kt + [0, 16)) as fp32 ----
+      // this warp's state columns: A = S^T fragments (v 16 w + [0, 16), k 16 kt + [0, 16)), as fp32
       const uint32_t half_base = smem_u32(st) + (warp >> 2) * GDNT_HALF;
       float sv[8][8];
 #pragma unroll
@@ -319,8 +356,6 @@ gdn_tc_kernel(const __grid_constant__ CUtensorMap tm_state, const GdnArgs args) 
       // conv outputs, operand columns, norm partials, decay and beta are in shared memory
       if (!named_sync_and<GDNT_CONS>(ok)) break;
       // ---- recurrence ----
-      const float scale = 0.08838834764831845f;  // 128^-1/2, correctly rounded
-      const int v0 = 16 * warp + g;
       for (int t = 0; t < len; ++t) {
         const float4 pq = *reinterpret_cast<const float4*>(part + (t * 3 + 0) * 4);
         const float4 pk = *reinterpret_cast<const float4*>(part + (t * 3 + 1) * 4);
@@ -328,16 +363,15 @@ gdn_tc_kernel(const __grid_constant__ CUtensorMap tm_state, const GdnArgs args) 
         const float rq = scale * rsqrtf((pq.x + pq.y) + (pq.z + pq.w) + 1e-6f);
         const float rk = rsqrtf((pk.x + pk.y) + (pk.z + pk.w) + 1e-6f);
         const float dqk = ((pqk.x + pqk.y) + (pqk.z + pqk.w)) * rq * rk;
-        // S^T [k_hi k_lo q_hi q_lo] for this warp's 16 columns
+        // S^T [k_hi k_lo q_hi q_lo] for this warp's 16 columns (B columns 4..7 repeat 0..3; their results are unused)
         const __half* bcol = bop + (t * 4 + (g & 3)) * GDN_D + 2 * t4;
         float d[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};  // two chains: even and odd k tiles
 #pragma unroll
-        for (int kt = 0; kt < 8; ++kt) {
-          const uint32_t b0 = g < 4 ? *reinterpret_cast<const uint32_t*>(bcol + 16 * kt) : 0u;
-          const uint32_t b1 = g < 4 ? *reinterpret_cast<const uint32_t*>(bcol + 16 * kt + 8) : 0u;
+        for (int kt = 0; kt < 8; ++kt)
           mma_f16_16816(d[kt & 1], pack_half2(sv[kt][0], sv[kt][1]), pack_half2(sv[kt][2], sv[kt][3]),
-                        pack_half2(sv[kt][4], sv[kt][5]), pack_half2(sv[kt][6], sv[kt][7]), b0, b1);
-        }
+                        pack_half2(sv[kt][4], sv[kt][5]), pack_half2(sv[kt][6], sv[kt][7]),
+                        *reinterpret_cast<const uint32_t*>(bcol + 16 * kt),
+                        *reinterpret_cast<const uint32_t*>(bcol + 16 * kt + 8));
         // lane (g, t4 = 0): S^T k at v = v0, v0 + 8; lane (g, t4 = 1): S^T q
         const float p0 = (d[0][0] + d[0][1]) + (d[1][0] + d[1][1]), p1 = (d[0][2] + d[0][3]) + (d[1][2] + d[1][3]);
         const float q0 = __shfl_xor_sync(0xffffffffu, p0, 1), q1 = __shfl_xor_sync(0xffffffffu, p1, 1);
@@ -374,43 +408,9 @@ gdn_tc_kernel(const __grid_constant__ CUtensorMap tm_state, const GdnArgs args) 
         stmatrix_x4_trans(half_base + sw128_off(16 * kt + frag_k, frag_c), pack_half2(sv[kt][0], sv[kt][1]),
                           pack_half2(sv[kt][2], sv[kt][3]), pack_half2(sv[kt][4], sv[kt][5]),
                           pack_half2(sv[kt][6], sv[kt][7]));
-      named_sync<GDNT_CONS>();  // o[t] complete for the epilogue
-      // ---- epilogue ----
-      if (FUSED) {  // token t on warp 7 - t % 8: the v warps, whose prologue is light, take the first tokens
-        for (int t = GDNT_CWARPS - 1 - warp; t < lb; t += GDNT_CWARPS) {
-          const size_t row = (size_t)n * lb + t;
-          __nv_bfloat16* oh = args.out_hi + row * KEY_DIM + h * GDN_D + lane * 4;
-          __nv_bfloat16* ol = args.out_lo + row * KEY_DIM + h * GDN_D + lane * 4;
-          __nv_bfloat16 hv[4], lv[4];
-          if (t >= len) {
-#pragma unroll
-            for (int j = 0; j < 4; ++j) hv[j] = lv[j] = __float2bfloat16_rn(0.f);
-          } else {
-            const float4 o4 = reinterpret_cast<const float4*>(x + (t * 4 + 0) * GDN_D)[lane];
-            const float4 z4 = reinterpret_cast<const float4*>(x + (t * 4 + 3) * GDN_D)[lane];
-            const float var = warp_sum(o4.x * o4.x + o4.y * o4.y + o4.z * o4.z + o4.w * o4.w) * (1.0f / GDN_D);
-            const float r = 1.0f / sqrtf(var + args.eps);
-            const float y[4] = {gw.x * (o4.x * r) * silu(z4.x), gw.y * (o4.y * r) * silu(z4.y),
-                                gw.z * (o4.z * r) * silu(z4.z), gw.w * (o4.w * r) * silu(z4.w)};
-#pragma unroll
-            for (int j = 0; j < 4; ++j) split_bf16(y[j], hv[j], lv[j]);
-          }
-          *reinterpret_cast<uint2*>(oh) = *reinterpret_cast<uint2*>(hv);
-          *reinterpret_cast<uint2*>(ol) = *reinterpret_cast<uint2*>(lv);
-        }
-      } else {
-        for (int e = tid; e < lb * GDN_D; e += GDNT_CONS) {
-          const int t = e >> 7;
-          const size_t row = (size_t)n * lb + t;
-          args.o_raw[(row * GDN_H + h) * GDN_D + (e & 127)] = t < len ? x[(t * 4 + 0) * GDN_D + (e & 127)] : 0.f;
-        }
-      }
     }
     fence_proxy_async();   // this thread's writes to the stage are visible to the TMA store
-    mbar_arrive(&empty[s]);
-    cur_a = nxt_a;
-    cur_b = nxt_b;
-    decay_beta(cur_a, cur_b, cur_g, cur_beta);
+    mbar_arrive(&done[s]);
   }
 }
 

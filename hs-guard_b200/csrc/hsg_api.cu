@@ -812,6 +812,8 @@ int hsg_gdn_step(const void* packed, const float* a, const float* b, const float
     return fail(HSG_ERR_INVALID, "NULL argument");
   if (n < 1 || lb < 1 || lb > MAX_LB || max_slots < 1) return fail(HSG_ERR_INVALID, "bad shape n=%d lb=%d", n, lb);
   if (reinterpret_cast<uintptr_t>(state) & 15) return fail(HSG_ERR_INVALID, "state must be 16-byte aligned");
+  if ((reinterpret_cast<uintptr_t>(packed) | reinterpret_cast<uintptr_t>(a) | reinterpret_cast<uintptr_t>(b)) & 15)
+    return fail(HSG_ERR_INVALID, "packed, a and b must be 16-byte aligned");
   if (state_dtype != HSG_STATE_F32 && state_dtype != HSG_STATE_F16)
     return fail(HSG_ERR_INVALID, "state_dtype must be HSG_STATE_F32 or HSG_STATE_F16");
   int rc;
