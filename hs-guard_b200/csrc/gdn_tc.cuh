@@ -6,11 +6,10 @@
 //  * Producer warp (warp 9). Streams each item's inputs into a STAGES-deep shared-memory ring with TMA: the fp16
 //    state tile as two [128 k][64 v] halves with 128-byte swizzle (one 2-D tensor map over the pool viewed as
 //    [(S+1)*16*128 rows][128]), the q/k/v/z projection slices (FUSED) or bf16 q|k|v (RAW), the raw b|a gate inputs
-//    and the conv history. When a stage is released it writes the item's new state back (two 2-D TMA stores) and
-//    loads the next item into it.
+//    and the conv history; a released stage gets the next item.
 //  * Epilogue warp (warp 8). When the consumers are done with an item it writes the item's output rows -- the gated
 //    RMSNorm w * (o * rsqrt(mean(o^2) + eps)) * silu(z) as the out_proj operand (bf16 hi/lo pair), or the raw o --
-//    and releases the stage to the producer.
+//    then the item's new state back to the pool (two 2-D TMA stores), and releases the stage to the producer.
 //  * Eight consumer warps, one item at a time:
 //    - prologue: thread c < 128 runs the causal conv of q and k channel c (FUSED) or widens them (RAW), writes k back
 //      as fp32 and the MMA operand columns k_hi, k_lo, q_hi, q_lo in fp16 (hi = fp16(x), lo = fp16(x - hi)); its
@@ -96,19 +95,18 @@ gdn_tc_kernel(const __grid_constant__ CUtensorMap tm_state, const GdnArgs args) 
 
   if (warp == GDNT_PROD_WARP) {
     // ===================================== producer =====================================
-    int64_t held_slot[GDN_MAX_STAGES] = {};
     int held_len[GDN_MAX_STAGES] = {};
-    // each item's length and slot are loaded one item ahead, off the critical path
-    int64_t nxt_len = n_items > 0 ? args.lens[row_of(0)] : 0, nxt_slot = n_items > 0 ? args.slots[row_of(0)] : 0;
-    auto issue_state = [&](int i) {
+    // lengths and slots: the first stages' items are read by one lane each up front; later items one item ahead,
+    // issued after the stage's barrier arrive so that the arrive does not wait for them
+    int64_t my_len = 0, my_slot = 0, nxt_len = 0, nxt_slot = 0;
+    if (lane < n_items && lane < S) {
+      my_len = args.lens[row_of(lane)];
+      my_slot = args.slots[row_of(lane)];
+    }
+    auto issue_state = [&](int i, int64_t len64, int64_t slot) {
       const int s = i % S;
-      int len = (int)nxt_len;
-      const int64_t slot = nxt_slot;
-      if (i + 1 < n_items) {
-        nxt_len = args.lens[row_of(i + 1)];
-        nxt_slot = args.slots[row_of(i + 1)];
-      }
-      if (len < 0 || len > lb) {
+      int len = (int)len64;
+      if (len64 < 0 || len64 > lb) {
         if (lane == 0) set_error(args.err, ERR_BAD_LEN);
         len = 0;
       }
@@ -116,7 +114,6 @@ gdn_tc_kernel(const __grid_constant__ CUtensorMap tm_state, const GdnArgs args) 
         if (lane == 0) set_error(args.err, ERR_BAD_SLOT);
         len = 0;
       }
-      held_slot[s] = slot;
       held_len[s] = len;
       uint8_t* st = stage_ptr(s);
       float* hist = x_of(s) + lb * (4 * GDN_D + GDNT_AB);
@@ -166,27 +163,24 @@ gdn_tc_kernel(const __grid_constant__ CUtensorMap tm_state, const GdnArgs args) 
       }
     };
     const int pre = n_items < S ? n_items : S;
-    for (int i = 0; i < pre; ++i) issue_state(i);
+    for (int i = 0; i < pre; ++i)
+      issue_state(i, __shfl_sync(0xffffffffu, my_len, i), __shfl_sync(0xffffffffu, my_slot, i));
+    if (pre < n_items) {
+      nxt_len = args.lens[row_of(pre)];
+      nxt_slot = args.slots[row_of(pre)];
+    }
     pdl_wait();
     for (int i = 0; i < pre; ++i) issue_inputs(i);
-    for (int i = S; i < n_items + S; ++i) {
-      const int s = i % S, r = i / S;
-      if (i - S < n_items) {
-        // item i - S is finished (outputs written): write its state back
-        if (!mbar_wait(&empty[s], (r - 1) & 1, args.err, ERR_TIMEOUT_TMA)) break;
-        if (lane == 0 && held_len[s] > 0) {
-          tma_store_2d(&tm_state, stage_ptr(s), 0, tile_row(held_slot[s]));
-          tma_store_2d(&tm_state, stage_ptr(s) + GDNT_HALF, 64, tile_row(held_slot[s]));
-          bulk_commit();
-        }
+    for (int i = pre; i < n_items; ++i) {
+      // the epilogue warp has stored item i - S's state and released the stage
+      if (!mbar_wait(&empty[i % S], ((i / S) - 1) & 1, args.err, ERR_TIMEOUT_TMA)) break;
+      issue_state(i, nxt_len, nxt_slot);
+      if (i + 1 < n_items) {
+        nxt_len = args.lens[row_of(i + 1)];
+        nxt_slot = args.slots[row_of(i + 1)];
       }
-      if (i >= n_items) continue;
-      if (lane == 0) bulk_wait_read_all();  // the stores have read the stage
-      __syncwarp();
-      issue_state(i);
       issue_inputs(i);
     }
-    if (lane == 0) bulk_wait_all();
     return;
   }
 
@@ -232,8 +226,19 @@ gdn_tc_kernel(const __grid_constant__ CUtensorMap tm_state, const GdnArgs args) 
       const int s = i % S;
       if (!mbar_wait(&done[s], (i / S) & 1, args.err, ERR_TIMEOUT_TMA)) break;
       epilogue(i, s);
-      if (lane == 0) mbar_arrive(&empty[s]);
+      if (lane == 0) {
+        if (meta[s].len > 0) {  // the new state back to the pool
+          const int row = tile_row(meta[s].slot);
+          tma_store_2d(&tm_state, stage_ptr(s), 0, row);
+          tma_store_2d(&tm_state, stage_ptr(s) + GDNT_HALF, 64, row);
+          bulk_commit();
+          bulk_wait_read_all();  // the stores have read the stage
+        }
+        mbar_arrive(&empty[s]);
+      }
+      __syncwarp();
     }
+    if (lane == 0) bulk_wait_all();
     return;
   }
 
