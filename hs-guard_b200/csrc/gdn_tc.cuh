@@ -1,32 +1,36 @@
 // Gated delta rule slot step for fp16 recurrent state and ticks of up to 16 tokens, with the state-vector products
 // on the tensor cores (warp-level mma.sync). Longer ticks use gdn_step_kernel<., __half> (gdn.cuh).
 //
-// Persistent, head-stationary grid (16 heads x 9 CTAs, one per SM); work item = (session row, head). Warp roles:
+// Persistent, head-stationary grid (16 heads x 9 CTAs, one per SM); work item = (session row, head). Twelve warps in
+// four roles hand each item along through mbarriers, so no role waits for a block-wide barrier:
 //
-//  * Producer warp (warp 9). Streams each item's inputs into a STAGES-deep shared-memory ring with TMA: the fp16
-//    state tile as two [128 k][64 v] halves with 128-byte swizzle (one 2-D tensor map over the pool viewed as
-//    [(S+1)*16*128 rows][128]), the q/k/v/z projection slices (FUSED) or bf16 q|k|v (RAW), the raw b|a gate inputs
-//    and the conv history; a released stage gets the next item.
-//  * Epilogue warp (warp 8). When the consumers are done with an item it writes the item's output rows -- the gated
-//    RMSNorm w * (o * rsqrt(mean(o^2) + eps)) * silu(z) as the out_proj operand (bf16 hi/lo pair), or the raw o --
-//    then the item's new state back to the pool (two 2-D TMA stores), and releases the stage to the producer.
-//  * Eight consumer warps, one item at a time:
-//    - prologue: thread c < 128 runs the causal conv of q and k channel c (FUSED) or widens them (RAW), writes k back
-//      as fp32 and the MMA operand columns k_hi, k_lo, q_hi, q_lo in fp16 (hi = fp16(x), lo = fp16(x - hi)); its
-//      warp adds up per-token partial sums of q.q, k.k, q.k. Thread 128 + c does v channel c, then e^g and beta of
-//      token c. Warp w also loads the state columns v in [16 w, 16 w + 16), all 128 k, with `ldmatrix.trans` as
-//      eight 16 x 16 fragments of A = S^T. One barrier (the only block barrier per item).
-//    - per token, no barrier: one m16n8k16 MMA per fragment against B = [k_hi | k_lo | q_hi | q_lo | unused x 4]
-//      gives S^T k and S^T q for the warp's columns, exact up to the fp16 state; then
-//        delta = beta (v - e^g rk S^T k),   o = e^g rq S^T q + (k.q) rk rq delta,   S <- e^g S + rk k delta^T
-//      (rk, rq: L2-norm factors with eps 1e-6, rq including 128^-1/2); the state stays in registers as fp32 across
-//      the tick's tokens and is updated with packed fp32x2 arithmetic.
-//    - after the last token: round to fp16 once, `stmatrix.trans` back into the stage, release the stage.
-//    Per-item scratch (operand columns, partial sums, decay, beta) alternates between two buffers by item parity,
-//    so a warp may start the next item's prologue while others finish this item's tokens.
+//  * Producer (warp 9). Streams each item's inputs into a STAGES-deep shared-memory ring with TMA: the fp16 state
+//    tile as two [128 k][64 v] halves with 128-byte swizzle (one 2-D tensor map over the pool viewed as
+//    [(S+1)*16*128 rows][128]), the tick's q|k|v|z projection slices and b|a gate inputs of the row (FUSED) or bf16
+//    q|k|v and raw b, a (RAW), and the conv history; a released stage gets the next item.            -> full[s]
+//  * Prologue (warps 10, 11), one item ahead of the consumers: causal conv + SiLU of q, k, v (FUSED) or their
+//    widening (RAW), k and v back as fp32, the MMA operand columns k_hi, k_lo, q_hi, q_lo in fp16 (hi = fp16(x),
+//    lo = fp16(x - hi)), per-token partial sums of q.q, k.k, q.k, e^g (g = -exp(A_log) softplus(a + dt_bias),
+//    threshold 20) and beta = sigmoid(b); the conv history back to the pool. Warp 10 takes q, k channels 0-127
+//    (one-token ticks) or 0-95, warp 11 the other q, k channels, all of v and the gates.             -> pro[s]
+//  * Consumers (warps 0-7). Warp w loads its state columns v in [16 w, 16 w + 16), all 128 k, with `ldmatrix.trans`
+//    as eight 16 x 16 fragments of A = S^T, kept in registers as fp32 across the tick's tokens. Per token, with the
+//    L2-norm factors rk, rq (eps 1e-6, rq including 128^-1/2) from the prologue's partial sums, one
+//    m16n8k16 MMA per fragment against B = [k_hi | k_lo | q_hi | q_lo | unused x 4] gives S^T k and S^T q for the
+//    warp's columns, exact up to the fp16 state; then
+//      delta = beta (v - e^g rk S^T k),   o = e^g rq S^T q + (k.q) rk rq delta,   S <- e^g S + rk k delta^T
+//    with packed fp32x2 arithmetic. After the last token: round to fp16 once, `stmatrix.trans` into the stage.
+//                                                                                                    -> done[s]
+//  * Epilogue (warp 8). The item's output rows -- the gated RMSNorm w * (o * rsqrt(mean(o^2) + eps)) * silu(z) as the
+//    out_proj operand (bf16 hi/lo pair), or the raw o -- then the new state back to the pool (two 2-D TMA stores).
+//                                                                                                    -> empty[s]
+// Per-item scratch (operand columns, norm factors, decay, beta) alternates between two buffers by item parity; the
+// prologue writes item i's buffer only after the consumers are done with item i - 2.
 // The reference keeps StreamingGuard's state in fp16 (runtime.py:157) and computes in fp32 inside its kernel
 // (engine/fused_kernels.py:140-194, gdn_slot_kernel.py:66), rounding once per tick: the same here.
 #pragma once
+#include <type_traits>
+
 #include "gdn.cuh"
 
 namespace hsg {
@@ -35,22 +39,32 @@ constexpr int GDNT_CONS = 256;                 // 8 consumer warps
 constexpr int GDNT_CWARPS = GDNT_CONS / 32;
 constexpr int GDNT_EPI_WARP = GDNT_CWARPS;     // warp 8
 constexpr int GDNT_PROD_WARP = GDNT_CWARPS + 1; // warp 9
-constexpr int GDNT_THREADS = GDNT_CONS + 64;
+constexpr int GDNT_QK_WARP = GDNT_CWARPS + 2;  // warp 10
+constexpr int GDNT_V_WARP = GDNT_CWARPS + 3;   // warp 11
+constexpr int GDNT_THREADS = GDNT_CONS + 128;
 constexpr int GDNT_MAX_LB = 16;
 constexpr int GDNT_HALF = GDN_D * 64 * 2;      // one [128 k][64 v] fp16 half of the tile: 16 KB
 constexpr int GDNT_TILE = 2 * GDNT_HALF;
 constexpr int GDNT_AB = 32;                    // per token: b[16] | a[16] fp32
 
+// Tensor maps of one launch. FUSED: in0 = this layer's conv history [(S+1)*3 rows][3 parts][2048] fp32, box
+// [3][3][128]; in1 = the projection's q|k|v|z columns [rows][4 parts][2048] fp32, box [lb][4][128]; in2 = its b|a
+// columns [rows][32] fp32, box [lb][32]. RAW: in0 = bf16 q|k|v [rows][3 parts][2048], box [lb][3][128].
+struct GdntMaps {
+  CUtensorMap state, in0, in1, in2;
+};
+
 // Stage: state halves | x [lb][4][128] fp32 (q, k, v, z; o replaces q) | ab [lb][32] fp32 | FUSED: conv history
-// [9][128] fp32, RAW: bf16 q|k|v [lb][3][128]; rounded up to 1 KB so every stage's tile is 1024-aligned.
+// [3][3][128] fp32, RAW: bf16 q|k|v [lb][3][128]; rounded up to 1 KB so every stage's tile is 1024-aligned.
 __host__ __device__ inline int gdnt_stage_bytes(int lb, bool fused) {
   return (GDNT_TILE + lb * 4 * GDN_D * 4 + lb * GDNT_AB * 4 + (fused ? 9 * GDN_D * 4 : lb * 3 * GDN_D * 2) + 1023) &
          ~1023;
 }
-// Per-item scratch, x2 (item parity): operand columns [lb][4][128] fp16 | partials [lb][3][4] f32 | e^g, beta [lb]
-__host__ __device__ inline int gdnt_scratch_bytes(int lb) { return lb * 4 * GDN_D * 2 + lb * 12 * 4 + 2 * lb * 4; }
+// Per-item scratch, x2 (item parity): operand columns [lb][4][128] fp16 | partial sums of q.q, k.k, q.k from the two
+// prologue warps [lb][2][4] f32 | e^g [lb] | beta [lb]
+__host__ __device__ inline int gdnt_scratch_bytes(int lb) { return lb * 4 * GDN_D * 2 + lb * 8 * 4 + 2 * lb * 4; }
 __host__ __device__ inline int gdnt_fixed_bytes(int lb) {
-  return 2 * ((gdnt_scratch_bytes(lb) + 15) & ~15) + GDN_MAX_STAGES * (16 + 3 * 8) + 1024;
+  return 2 * ((gdnt_scratch_bytes(lb) + 15) & ~15) + GDN_MAX_STAGES * (16 + 4 * 8) + 1024;
 }
 __host__ __device__ inline int gdnt_stages(int lb, bool fused) {
   int s = (GDN_SMEM_LIMIT - gdnt_fixed_bytes(lb)) / gdnt_stage_bytes(lb, fused);
@@ -60,9 +74,11 @@ __host__ __device__ inline int gdnt_smem_bytes(int lb, bool fused) {
   return gdnt_stages(lb, fused) * gdnt_stage_bytes(lb, fused) + gdnt_fixed_bytes(lb);
 }
 
-template <bool FUSED>
+// NQK10: q/k channels per lane of prologue warp 10 (4 for one-token ticks, 3 otherwise; the rest go to warp 11).
+template <bool FUSED, int NQK10>
 __global__ void __launch_bounds__(GDNT_THREADS, 1)
-gdn_tc_kernel(const __grid_constant__ CUtensorMap tm_state, const GdnArgs args) {
+gdn_tc_kernel(const __grid_constant__ GdntMaps maps, const GdnArgs args) {
+  const CUtensorMap* tm_state = &maps.state;
   extern __shared__ __align__(1024) uint8_t gdnt_smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(gdnt_smem_raw) + 1023) & ~uintptr_t(1023));
   const int lb = args.lb, S = args.stages;
@@ -70,9 +86,10 @@ gdn_tc_kernel(const __grid_constant__ CUtensorMap tm_state, const GdnArgs args) 
   const int scratch = (gdnt_scratch_bytes(lb) + 15) & ~15;
   uint8_t* fixed = smem + S * sbytes;
   GdnMeta* meta = reinterpret_cast<GdnMeta*>(fixed + 2 * scratch);
-  uint64_t* full = reinterpret_cast<uint64_t*>(meta + GDN_MAX_STAGES);
-  uint64_t* done = full + GDN_MAX_STAGES;   // consumers -> epilogue warp
-  uint64_t* empty = done + GDN_MAX_STAGES;  // epilogue warp -> producer
+  uint64_t* full = reinterpret_cast<uint64_t*>(meta + GDN_MAX_STAGES);  // producer -> prologue, consumers
+  uint64_t* pro = full + GDN_MAX_STAGES;                                // prologue -> consumers
+  uint64_t* done = pro + GDN_MAX_STAGES;                                // consumers -> epilogue, prologue
+  uint64_t* empty = done + GDN_MAX_STAGES;                              // epilogue -> producer
 
   const int h = blockIdx.x, p = blockIdx.y, P = gridDim.y;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -81,15 +98,24 @@ gdn_tc_kernel(const __grid_constant__ CUtensorMap tm_state, const GdnArgs args) 
   auto stage_ptr = [&](int s) { return smem + s * sbytes; };
   auto x_of = [&](int s) { return reinterpret_cast<float*>(stage_ptr(s) + GDNT_TILE); };
   auto tile_row = [&](int64_t slot) { return (int)((slot * GDN_H + h) * GDN_D); };
+  // item i's scratch buffer
+  auto bop_of = [&](int i) { return reinterpret_cast<__half*>(fixed + (i & 1) * scratch); };
+  auto nrm_of = [&](int i) { return reinterpret_cast<float*>(bop_of(i) + lb * 4 * GDN_D); };
 
   if (tid == 0) {
     for (int s = 0; s < S; ++s) {
       mbar_init(&full[s], 1);
+      mbar_init(&pro[s], 64);
       mbar_init(&done[s], GDNT_CONS);
       mbar_init(&empty[s], 1);
     }
     fence_barrier_init();
-    prefetch_tmap(&tm_state);
+    prefetch_tmap(&maps.state);
+    prefetch_tmap(&maps.in0);
+    if (FUSED) {
+      prefetch_tmap(&maps.in1);
+      prefetch_tmap(&maps.in2);
+    }
   }
   __syncthreads();
 
@@ -120,22 +146,18 @@ gdn_tc_kernel(const __grid_constant__ CUtensorMap tm_state, const GdnArgs args) 
       if (lane == 0) {
         meta[s].slot = slot;
         meta[s].len = len;
-        if (len > 0)
-          mbar_arrive_expect_tx(&full[s], GDNT_TILE + len * GDNT_AB * 4 +
-                                              (FUSED ? len * 4 * GDN_D * 4 + 9 * GDN_D * 4 : len * 3 * GDN_D * 2));
+        if (len > 0)  // whole boxes: padded tokens' rows are fetched too (in bounds) and never used
+          mbar_arrive_expect_tx(&full[s], GDNT_TILE + (FUSED ? lb * (4 * GDN_D + GDNT_AB) * 4 + 9 * GDN_D * 4
+                                                             : lb * 3 * GDN_D * 2 + len * GDNT_AB * 4));
         else
           mbar_arrive(&full[s]);
       }
       __syncwarp();
       if (len == 0) return;
       if (lane == 0) {
-        tma_load_2d(st, &tm_state, 0, tile_row(slot), &full[s]);
-        tma_load_2d(st + GDNT_HALF, &tm_state, 64, tile_row(slot), &full[s]);
-      }
-      if (FUSED && lane < 9) {  // conv history: 3 rows x (q, k, v) channel blocks
-        const int rr = lane / 3, part = lane % 3;
-        const float* src = args.conv_pool + ((size_t)slot * CONV_KEEP + rr) * CONV_DIM + part * KEY_DIM + h * GDN_D;
-        bulk_g2s(hist + (rr * 3 + part) * GDN_D, src, GDN_D * 4, &full[s]);
+        tma_load_2d(st, tm_state, 0, tile_row(slot), &full[s]);
+        tma_load_2d(st + GDNT_HALF, tm_state, 64, tile_row(slot), &full[s]);
+        if (FUSED) tma_load_3d(hist, &maps.in0, h * GDN_D, 0, (int)slot * CONV_KEEP, &full[s]);  // conv history
       }
     };
     auto issue_inputs = [&](int i) {
@@ -143,22 +165,19 @@ gdn_tc_kernel(const __grid_constant__ CUtensorMap tm_state, const GdnArgs args) 
       if (len == 0) return;
       float* x = x_of(s);
       float* ab = x + lb * 4 * GDN_D;
-      if (FUSED) {
-        for (int j = lane; j < len * 5; j += 32) {  // q, k, v, z slices (4 x 512 B) and b|a (128 B) of each token
-          const int t = j / 5, part = j % 5;
-          const float* row = args.proj + ((size_t)n * lb + t) * GDN_IN;
-          if (part < 4) bulk_g2s(x + (t * 4 + part) * GDN_D, row + part * KEY_DIM + h * GDN_D, GDN_D * 4, &full[s]);
-          else bulk_g2s(ab + t * GDNT_AB, row + GDN_B_OFF, GDNT_AB * 4, &full[s]);
+      if (FUSED) {  // the tick's q|k|v|z slices and b|a of this row: two boxes
+        if (lane == 0) {
+          tma_load_3d(x, &maps.in1, h * GDN_D, 0, n * lb, &full[s]);
+          tma_load_2d(ab, &maps.in2, 0, n * lb, &full[s]);
         }
-      } else {
-        __nv_bfloat16* xb = reinterpret_cast<__nv_bfloat16*>(ab + lb * GDNT_AB);
-        for (int j = lane; j < len * 5; j += 32) {  // q, k, v (3 x 256 B), b, a (2 x 64 B) of each token
-          const int t = j / 5, part = j % 5;
+      } else {  // bf16 q|k|v: one box; b, a of each token: 64-byte copies
+        if (lane == 0)
+          tma_load_3d(reinterpret_cast<__nv_bfloat16*>(ab + lb * GDNT_AB), &maps.in0, h * GDN_D, 0, n * lb, &full[s]);
+        for (int j = lane; j < len * 2; j += 32) {
+          const int t = j >> 1, part = j & 1;
           const size_t rt = (size_t)n * lb + t;
-          if (part < 3) bulk_g2s(xb + (t * 3 + part) * GDN_D, args.packed + rt * CONV_DIM + part * KEY_DIM + h * GDN_D,
-                                 GDN_D * 2, &full[s]);
-          else bulk_g2s(ab + t * GDNT_AB + (part - 3) * GDN_H, (part == 3 ? args.b_raw : args.a_raw) + rt * GDN_H,
-                        GDN_H * 4, &full[s]);
+          bulk_g2s(ab + t * GDNT_AB + part * GDN_H, (part == 0 ? args.b_raw : args.a_raw) + rt * GDN_H, GDN_H * 4,
+                   &full[s]);
         }
       }
     };
@@ -229,8 +248,8 @@ gdn_tc_kernel(const __grid_constant__ CUtensorMap tm_state, const GdnArgs args) 
       if (lane == 0) {
         if (meta[s].len > 0) {  // the new state back to the pool
           const int row = tile_row(meta[s].slot);
-          tma_store_2d(&tm_state, stage_ptr(s), 0, row);
-          tma_store_2d(&tm_state, stage_ptr(s) + GDNT_HALF, 64, row);
+          tma_store_2d(tm_state, stage_ptr(s), 0, row);
+          tma_store_2d(tm_state, stage_ptr(s) + GDNT_HALF, 64, row);
           bulk_commit();
           bulk_wait_read_all();  // the stores have read the stage
         }
@@ -242,110 +261,161 @@ gdn_tc_kernel(const __grid_constant__ CUtensorMap tm_state, const GdnArgs args) 
     return;
   }
 
-  // ===================================== consumers =====================================
-  const int c = tid & (GDN_D - 1);             // prologue channel
-  const bool qk_thread = tid < GDN_D;          // thread c: q and k channel c; thread 128 + c: v channel c
-  const int g = lane >> 2, t4 = lane & 3;      // mma fragment coordinates
-  float4 cw = make_float4(0.f, 0.f, 0.f, 0.f), cw2 = cw;  // conv taps: q (or v) and k of channel c
-  if (FUSED) {
-    const float4* w4 = reinterpret_cast<const float4*>(args.conv_w);
-    if (qk_thread) {
-      cw = w4[0 * KEY_DIM + h * GDN_D + c];
-      cw2 = w4[1 * KEY_DIM + h * GDN_D + c];
-    } else {
-      cw = w4[2 * KEY_DIM + h * GDN_D + c];
-    }
+  if (warp == GDNT_QK_WARP || warp == GDNT_V_WARP) {
+    // ===================================== prologue =====================================
+    // Warp 10: q and k channels lane + 32 j (j < NQK10). Warp 11: the remaining q and k channels, v channels
+    // lane + 32 j (j < 4), then e^g and beta. Each writes its partial sums of q.q, k.k, q.k per token. With one token
+    // per tick warp 10 takes all 128 q/k channels (NQK10 = 4), else 96 (the split measured fastest for each). Each
+    // warp's code is specialised to its channel counts.
+    const float negA = -expf(args.A_log[h]), dtb = args.dt_bias[h];
+    auto prologue = [&](auto nq_tag, auto v_tag) {
+      constexpr int NQ = decltype(nq_tag)::value;  // q/k channels per lane
+      constexpr bool WV = decltype(v_tag)::value;   // also v and the gates (warp 11)
+      constexpr int NQA = NQ > 0 ? NQ : 1;
+      const int qk0 = WV ? 32 * (4 - NQ) : 0;
+      float4 cq[NQA], ck[NQA], cv[4];
+      if (FUSED) {
+        const float4* w4 = reinterpret_cast<const float4*>(args.conv_w) + h * GDN_D;
+#pragma unroll
+        for (int j = 0; j < NQ; ++j) {
+          cq[j] = w4[qk0 + lane + 32 * j];
+          ck[j] = w4[KEY_DIM + qk0 + lane + 32 * j];
+        }
+        if (WV)
+#pragma unroll
+          for (int j = 0; j < 4; ++j) cv[j] = w4[2 * KEY_DIM + lane + 32 * j];
+      }
+      pdl_wait();  // the conv history written below may still be read by an earlier kernel
+      for (int i = 0; i < n_items; ++i) {
+        const int s = i % S;
+        if (!mbar_wait(&full[s], (i / S) & 1, args.err, ERR_TIMEOUT_TMA)) break;
+        // this item's scratch buffer was last used by item i - 2
+        if (i >= 2 && !mbar_wait(&done[(i - 2) % S], ((i - 2) / S) & 1, args.err, ERR_TIMEOUT_TMA)) break;
+        const int len = meta[s].len;
+        if (len > 0) {
+          const int64_t slot = meta[s].slot;
+          float* x = x_of(s);
+          const float* ab = x + lb * 4 * GDN_D;
+          const float* hist = ab + lb * GDNT_AB;
+          const __nv_bfloat16* raw = reinterpret_cast<const __nv_bfloat16*>(hist);
+          __half* bop = bop_of(i);
+          float* nrm = nrm_of(i);
+          float hq[NQA][3], hk[NQA][3], hv[4][3];
+          if (FUSED) {
+#pragma unroll
+            for (int r = 0; r < 3; ++r) {
+#pragma unroll
+              for (int j = 0; j < NQ; ++j) {
+                hq[j][r] = hist[(r * 3 + 0) * GDN_D + qk0 + lane + 32 * j];
+                hk[j][r] = hist[(r * 3 + 1) * GDN_D + qk0 + lane + 32 * j];
+              }
+              if (WV)
+#pragma unroll
+                for (int j = 0; j < 4; ++j) hv[j][r] = hist[(r * 3 + 2) * GDN_D + lane + 32 * j];
+            }
+          }
+          for (int t = 0; t < len; ++t) {
+            float sq = 0.f, sk = 0.f, sqk = 0.f;
+#pragma unroll
+            for (int j = 0; j < NQ; ++j) {
+              const int c = qk0 + lane + 32 * j;
+              float qv, kv;
+              if (FUSED) {
+                const float xq = x[(t * 4 + 0) * GDN_D + c], xk = x[(t * 4 + 1) * GDN_D + c];
+                qv = silu_fast(fmaf(cq[j].w, xq, fmaf(cq[j].z, hq[j][2], fmaf(cq[j].y, hq[j][1], cq[j].x * hq[j][0]))));
+                kv = silu_fast(fmaf(ck[j].w, xk, fmaf(ck[j].z, hk[j][2], fmaf(ck[j].y, hk[j][1], ck[j].x * hk[j][0]))));
+                hq[j][0] = hq[j][1]; hq[j][1] = hq[j][2]; hq[j][2] = xq;
+                hk[j][0] = hk[j][1]; hk[j][1] = hk[j][2]; hk[j][2] = xk;
+              } else {
+                qv = __bfloat162float(raw[(t * 3 + 0) * GDN_D + c]);
+                kv = __bfloat162float(raw[(t * 3 + 1) * GDN_D + c]);
+              }
+              x[(t * 4 + 1) * GDN_D + c] = kv;
+              const __half khi = __float2half_rn(kv), qhi = __float2half_rn(qv);
+              __half* bt = bop + t * 4 * GDN_D + c;
+              bt[0 * GDN_D] = khi;
+              bt[1 * GDN_D] = __float2half_rn(kv - __half2float(khi));
+              bt[2 * GDN_D] = qhi;
+              bt[3 * GDN_D] = __float2half_rn(qv - __half2float(qhi));
+              sq = fmaf(qv, qv, sq);
+              sk = fmaf(kv, kv, sk);
+              sqk = fmaf(qv, kv, sqk);
+            }
+            if (WV) {
+#pragma unroll
+              for (int j = 0; j < 4; ++j) {
+                float* xp = x + (t * 4 + 2) * GDN_D + lane + 32 * j;
+                if (FUSED) {
+                  const float xv = *xp;
+                  *xp = silu_fast(fmaf(cv[j].w, xv, fmaf(cv[j].z, hv[j][2], fmaf(cv[j].y, hv[j][1], cv[j].x * hv[j][0]))));
+                  hv[j][0] = hv[j][1]; hv[j][1] = hv[j][2]; hv[j][2] = xv;
+                } else {
+                  *xp = __bfloat162float(raw[(t * 3 + 2) * GDN_D + lane + 32 * j]);
+                }
+              }
+            }
+            if (NQ > 0) {
+              sq = warp_sum(sq);
+              sk = warp_sum(sk);
+              sqk = warp_sum(sqk);
+            }
+            if (lane == 0) *reinterpret_cast<float4*>(nrm + t * 8 + (WV ? 4 : 0)) = make_float4(sq, sk, sqk, 0.f);
+          }
+          if (FUSED) {
+            float* gp = args.conv_pool + (size_t)slot * CONV_KEEP * CONV_DIM + h * GDN_D + lane;
+#pragma unroll
+            for (int r = 0; r < 3; ++r) {
+#pragma unroll
+              for (int j = 0; j < NQ; ++j) {
+                gp[r * CONV_DIM + qk0 + 32 * j] = hq[j][r];
+                gp[r * CONV_DIM + KEY_DIM + qk0 + 32 * j] = hk[j][r];
+              }
+              if (WV)
+#pragma unroll
+                for (int j = 0; j < 4; ++j) gp[r * CONV_DIM + 2 * KEY_DIM + 32 * j] = hv[j][r];
+            }
+          }
+          if (WV) {
+            float* gv = nrm + lb * 8;
+            float* bv = gv + lb;
+            for (int t = lane; t < len; t += 32) {  // g = -exp(A_log) softplus(a + dt_bias) (threshold 20)
+              const float xg = ab[t * GDNT_AB + GDN_H + h] + dtb;
+              const float sp = xg > 20.f ? xg : log1pf(expf(xg));
+              gv[t] = expf(negA * sp);
+              bv[t] = sigmoidf_(ab[t * GDNT_AB + h]);
+            }
+          }
+        }
+        mbar_arrive(&pro[s]);
+      }
+    };
+    if (warp == GDNT_QK_WARP) prologue(std::integral_constant<int, NQK10>{}, std::false_type{});
+    else prologue(std::integral_constant<int, 4 - NQK10>{}, std::true_type{});
+    return;
   }
-  const float negA = -expf(args.A_log[h]), dtb = args.dt_bias[h];
+
+  // ===================================== consumers =====================================
+  const int g = lane >> 2, t4 = lane & 3;      // mma fragment coordinates
   // this lane's ldmatrix/stmatrix row within each 16 x 16 fragment: k row and 16-byte v chunk of its 8 x 8 matrix
   const int frag_k = (lane & 7) + ((lane >> 4) & 1) * 8;
   const int frag_c = 2 * (warp & 3) + ((lane >> 3) & 1);
-  const float scale = 0.08838834764831845f;  // 128^-1/2, correctly rounded
   const int v0 = 16 * warp + g;
-  pdl_wait();
+  const float scale = 0.08838834764831845f;  // 128^-1/2, correctly rounded
   if (tid == 0) pdl_trigger();
 
   for (int i = 0; i < n_items; ++i) {
     const int s = i % S;
-    uint8_t* st = stage_ptr(s);
-    float* x = x_of(s);
-    uint8_t* scr = fixed + (i & 1) * scratch;
-    __half* bop = reinterpret_cast<__half*>(scr);                     // [lb][4][128]: k_hi, k_lo, q_hi, q_lo
-    float* part = reinterpret_cast<float*>(bop + lb * 4 * GDN_D);     // [lb][3][4]: q.q, k.k, q.k per q/k warp
-    float* gv = part + lb * 12;                                       // e^g per token
-    float* bv = gv + lb;                                              // beta per token
-    // Each warp waits for the stage itself; the barrier below combines the outcomes so that every warp leaves
-    // together on a failure.
-    const bool ok = mbar_wait(&full[s], (i / S) & 1, args.err, ERR_TIMEOUT_TMA);
-    const int len = ok ? meta[s].len : 0;
-    if (len == 0) {
-      if (!named_sync_and<GDNT_CONS>(ok)) break;
-    } else {
-      const int64_t slot = meta[s].slot;
-      // ---- prologue ----
-      const float* ab = x + lb * 4 * GDN_D;
-      const float* hist = ab + lb * GDNT_AB;
-      const __nv_bfloat16* raw = reinterpret_cast<const __nv_bfloat16*>(hist);
-      if (qk_thread) {
-        float q0 = 0.f, q1 = 0.f, q2 = 0.f, k0 = 0.f, k1 = 0.f, k2 = 0.f;
-        if (FUSED) {
-          q0 = hist[0 * GDN_D + c]; q1 = hist[3 * GDN_D + c]; q2 = hist[6 * GDN_D + c];
-          k0 = hist[1 * GDN_D + c]; k1 = hist[4 * GDN_D + c]; k2 = hist[7 * GDN_D + c];
-        }
-        for (int t = 0; t < len; ++t) {
-          float qv, kv;
-          if (FUSED) {
-            const float xq = x[(t * 4 + 0) * GDN_D + c], xk = x[(t * 4 + 1) * GDN_D + c];
-            qv = silu_fast(fmaf(cw.w, xq, fmaf(cw.z, q2, fmaf(cw.y, q1, cw.x * q0))));
-            kv = silu_fast(fmaf(cw2.w, xk, fmaf(cw2.z, k2, fmaf(cw2.y, k1, cw2.x * k0))));
-            q0 = q1; q1 = q2; q2 = xq;
-            k0 = k1; k1 = k2; k2 = xk;
-          } else {
-            qv = __bfloat162float(raw[(t * 3 + 0) * GDN_D + c]);
-            kv = __bfloat162float(raw[(t * 3 + 1) * GDN_D + c]);
-          }
-          x[(t * 4 + 1) * GDN_D + c] = kv;
-          const __half khi = __float2half_rn(kv), qhi = __float2half_rn(qv);
-          __half* bt = bop + t * 4 * GDN_D + c;
-          bt[0 * GDN_D] = khi;
-          bt[1 * GDN_D] = __float2half_rn(kv - __half2float(khi));
-          bt[2 * GDN_D] = qhi;
-          bt[3 * GDN_D] = __float2half_rn(qv - __half2float(qhi));
-          const float sq = warp_sum(qv * qv), sk = warp_sum(kv * kv), sqk = warp_sum(qv * kv);
-          if (lane == 0) {
-            part[(t * 3 + 0) * 4 + warp] = sq;
-            part[(t * 3 + 1) * 4 + warp] = sk;
-            part[(t * 3 + 2) * 4 + warp] = sqk;
-          }
-        }
-        if (FUSED) {
-          float* gp = args.conv_pool + (size_t)slot * CONV_KEEP * CONV_DIM + h * GDN_D + c;
-          gp[0] = q0; gp[CONV_DIM] = q1; gp[2 * CONV_DIM] = q2;
-          gp[KEY_DIM] = k0; gp[CONV_DIM + KEY_DIM] = k1; gp[2 * CONV_DIM + KEY_DIM] = k2;
-        }
-      } else {
-        if (FUSED) {
-          float e0 = hist[2 * GDN_D + c], e1 = hist[5 * GDN_D + c], e2 = hist[8 * GDN_D + c];
-          for (int t = 0; t < len; ++t) {
-            float* xp = x + (t * 4 + 2) * GDN_D + c;
-            const float xv = *xp;
-            *xp = silu_fast(fmaf(cw.w, xv, fmaf(cw.z, e2, fmaf(cw.y, e1, cw.x * e0))));
-            e0 = e1; e1 = e2; e2 = xv;
-          }
-          float* gp = args.conv_pool + (size_t)slot * CONV_KEEP * CONV_DIM + 2 * KEY_DIM + h * GDN_D + c;
-          gp[0] = e0; gp[CONV_DIM] = e1; gp[2 * CONV_DIM] = e2;
-        } else {
-          for (int t = 0; t < len; ++t) x[(t * 4 + 2) * GDN_D + c] = __bfloat162float(raw[(t * 3 + 2) * GDN_D + c]);
-        }
-        if (c < len) {  // g = -exp(A_log) softplus(a + dt_bias) (threshold 20), beta = sigmoid(b)
-          const float xg = ab[c * GDNT_AB + GDN_H + h] + dtb;
-          const float sp = xg > 20.f ? xg : log1pf(expf(xg));
-          gv[c] = expf(negA * sp);
-          bv[c] = sigmoidf_(ab[c * GDNT_AB + h]);
-        }
-      }
+    if (!mbar_wait(&full[s], (i / S) & 1, args.err, ERR_TIMEOUT_TMA)) break;
+    if (!mbar_wait(&pro[s], (i / S) & 1, args.err, ERR_TIMEOUT_TMA)) break;
+    const int len = meta[s].len;
+    if (len > 0) {
+      float* x = x_of(s);
+      const __half* bop = bop_of(i);
+      const float* nrm = nrm_of(i);
+      const float* gv = nrm + lb * 8;
+      const float* bv = gv + lb;
       // this warp's state columns: A = S^T fragments (v 16 w + [0, 16), k 16 kt + [0, 16)), as fp32
-      const uint32_t half_base = smem_u32(st) + (warp >> 2) * GDNT_HALF;
+      const uint32_t half_base = smem_u32(stage_ptr(s)) + (warp >> 2) * GDNT_HALF;
       float sv[8][8];
 #pragma unroll
       for (int kt = 0; kt < 8; ++kt) {
@@ -358,16 +428,11 @@ gdn_tc_kernel(const __grid_constant__ CUtensorMap tm_state, const GdnArgs args) 
           sv[kt][2 * j + 1] = f.y;
         }
       }
-      // conv outputs, operand columns, norm partials, decay and beta are in shared memory
-      if (!named_sync_and<GDNT_CONS>(ok)) break;
-      // ---- recurrence ----
       for (int t = 0; t < len; ++t) {
-        const float4 pq = *reinterpret_cast<const float4*>(part + (t * 3 + 0) * 4);
-        const float4 pk = *reinterpret_cast<const float4*>(part + (t * 3 + 1) * 4);
-        const float4 pqk = *reinterpret_cast<const float4*>(part + (t * 3 + 2) * 4);
-        const float rq = scale * rsqrtf((pq.x + pq.y) + (pq.z + pq.w) + 1e-6f);
-        const float rk = rsqrtf((pk.x + pk.y) + (pk.z + pk.w) + 1e-6f);
-        const float dqk = ((pqk.x + pqk.y) + (pqk.z + pqk.w)) * rq * rk;
+        const float4 na = *reinterpret_cast<const float4*>(nrm + t * 8);
+        const float4 nb = *reinterpret_cast<const float4*>(nrm + t * 8 + 4);
+        const float rq = scale * rsqrtf(na.x + nb.x + 1e-6f), rk = rsqrtf(na.y + nb.y + 1e-6f);
+        const float dqk = (na.z + nb.z) * rq * rk;
         // S^T [k_hi k_lo q_hi q_lo] for this warp's 16 columns (B columns 4..7 repeat 0..3; their results are unused)
         const __half* bcol = bop + (t * 4 + (g & 3)) * GDN_D + 2 * t4;
         float d[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};  // two chains: even and odd k tiles

@@ -87,6 +87,25 @@ static int make_map_2d(CUtensorMap* map, const void* base, CUtensorMapDataType d
   return HSG_OK;
 }
 
+// 3-D tensor map, no swizzle: extents d0 (contiguous) x d1 x d2 with byte strides s1, s2; box b0 x b1 x b2.
+static int make_map_3d(CUtensorMap* map, const void* base, CUtensorMapDataType dtype, int elem_bytes, uint64_t d0,
+                       uint64_t d1, uint64_t d2, uint64_t s1, uint64_t s2, int b0, int b1, int b2) {
+  if (get_encoder() != HSG_OK) return HSG_ERR_CUDA;
+  if ((reinterpret_cast<uintptr_t>(base) & 15) || (s1 & 15) || (s2 & 15) || ((uint64_t)b0 * elem_bytes) % 16 ||
+      b0 < 1 || b1 < 1 || b2 < 1 || b0 > 256 || b1 > 256 || b2 > 256 || d2 < 1)
+    return fail(HSG_ERR_INVALID, "bad 3-D tensor map (base %p, strides %llu %llu, box %d x %d x %d)", base,
+                (unsigned long long)s1, (unsigned long long)s2, b0, b1, b2);
+  cuuint64_t dims[3] = {(cuuint64_t)d0, (cuuint64_t)d1, (cuuint64_t)d2};
+  cuuint64_t strides[2] = {(cuuint64_t)s1, (cuuint64_t)s2};
+  cuuint32_t box[3] = {(cuuint32_t)b0, (cuuint32_t)b1, (cuuint32_t)b2};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = g_encode(map, dtype, 3, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(HSG_ERR_CUDA, "cuTensorMapEncodeTiled (3-D) failed (%d)", (int)r);
+  return HSG_OK;
+}
+
 // GEMM operand: bf16 [rows][k], box [64 k][box_rows], 128-byte swizzle (the tcgen05 K-major SW128 layout).
 static int make_map(CUtensorMap* map, const void* base, int rows, int k, int box_rows) {
   if (k % 64 || box_rows < 16) return fail(HSG_ERR_INVALID, "bad operand map (k %d, box %d)", k, box_rows);
@@ -229,8 +248,10 @@ static int set_kernel_attributes() {
   CU(cudaFuncSetAttribute(gdn_step_kernel<true, __half>, cudaFuncAttributeMaxDynamicSharedMemorySize, GDN_SMEM_LIMIT));
   CU(cudaFuncSetAttribute(gdn_step_kernel<false, __half>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                           GDN_SMEM_LIMIT));
-  CU(cudaFuncSetAttribute(gdn_tc_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, GDN_SMEM_LIMIT));
-  CU(cudaFuncSetAttribute(gdn_tc_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, GDN_SMEM_LIMIT));
+  CU(cudaFuncSetAttribute(gdn_tc_kernel<true, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize, GDN_SMEM_LIMIT));
+  CU(cudaFuncSetAttribute(gdn_tc_kernel<true, 3>, cudaFuncAttributeMaxDynamicSharedMemorySize, GDN_SMEM_LIMIT));
+  CU(cudaFuncSetAttribute(gdn_tc_kernel<false, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize, GDN_SMEM_LIMIT));
+  CU(cudaFuncSetAttribute(gdn_tc_kernel<false, 3>, cudaFuncAttributeMaxDynamicSharedMemorySize, GDN_SMEM_LIMIT));
   CU(cudaFuncSetAttribute(ring_attn_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, attn_smem_bytes(4)));
   CU(cudaFuncSetAttribute(ring_attn_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, attn_smem_bytes(8)));
   CU(cudaFuncSetAttribute(ring_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, rd_smem_bytes()));
@@ -272,6 +293,7 @@ struct hsg_engine {
   CUtensorMap ring_maps[6][2];  // per attention layer: ring K, ring V as 2-D [rows][256] fp16, [64 x 32] SW128 boxes
   CUtensorMap new_maps[2];      // the tick's new K, V ([rows = row*2 + head][256], 1-token ticks)
   CUtensorMap state_maps[18];   // per GDN layer: the fp16 state pool (gdn_tc_kernel)
+  CUtensorMap conv_maps[18];    // per GDN layer: the conv history as [(S+1)*3][3][2048], [3][3][128] boxes
   std::vector<void*> allocations;
   // profiling
   std::vector<cudaEvent_t> events;
@@ -335,6 +357,15 @@ static int enqueue_step(hsg_engine* e, int nb, int lb) {
   const float eps = e->cfg.rms_eps;
   int rc;
   auto lo = [&](__nv_bfloat16* p) { return use_lo ? p : nullptr; };
+  GdntMaps tc_maps;  // the tensor-core GDN kernel's projection maps for this tick shape
+  if (e->rec_elem == 2 && lb <= GDNT_MAX_LB) {
+    if ((rc = make_map_3d(&tc_maps.in1, e->proj, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, KEY_DIM, 4, M, KEY_DIM * 4,
+                          GDN_IN * 4, GDN_D, 4, lb)) != HSG_OK)
+      return rc;
+    if ((rc = make_map_2d(&tc_maps.in2, e->proj + GDN_B_OFF, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, M, GDNT_AB,
+                          GDN_IN * 4, GDNT_AB, lb, CU_TENSOR_MAP_SWIZZLE_NONE)) != HSG_OK)
+      return rc;
+  }
   {
     ProfScope ps(e, HSG_PROF_EMBED);
     embed_norm_kernel<<<M, NORM_THREADS, 0, st>>>(ids, static_cast<const __nv_bfloat16*>(e->w.embed), e->cfg.vocab,
@@ -364,8 +395,14 @@ static int enqueue_step(hsg_engine* e, int nb, int lb) {
         const dim3 grid(GDN_H, std::min(nb, GDN_CTAS_PER_HEAD));
         if (e->rec_elem == 2 && lb <= GDNT_MAX_LB) {
           g.stages = gdnt_stages(lb, true);
-          CU(launch_k(gdn_tc_kernel<true>, grid, dim3(GDNT_THREADS), gdnt_smem_bytes(lb, true), st, e->pdl,
-                      e->state_maps[gi], g));
+          tc_maps.state = e->state_maps[gi];
+          tc_maps.in0 = e->conv_maps[gi];
+          if (lb == 1)
+            CU(launch_k(gdn_tc_kernel<true, 4>, grid, dim3(GDNT_THREADS), gdnt_smem_bytes(lb, true), st, e->pdl,
+                        tc_maps, g));
+          else
+            CU(launch_k(gdn_tc_kernel<true, 3>, grid, dim3(GDNT_THREADS), gdnt_smem_bytes(lb, true), st, e->pdl,
+                        tc_maps, g));
         } else if (e->rec_elem == 2) {
           const int tile = GDN_D * GDN_D * 2;
           g.stages = gdn_stages(lb, tile);
@@ -583,8 +620,11 @@ int hsg_create(const hsg_config* cfg, const hsg_weights* w, int max_slots, int d
     TRY(make_decode_map(&e->ring_maps[a][1], e->ring_v + (size_t)a * S1 * e->ring_slot(), rows));
   }
   if (e->rec_elem == 2)
-    for (int gi = 0; gi < e->n_gdn; ++gi)
+    for (int gi = 0; gi < e->n_gdn; ++gi) {
       TRY(make_state_map(&e->state_maps[gi], e->rec + (size_t)gi * S1 * e->rec_slot() * 2, (int64_t)S1));
+      TRY(make_map_3d(&e->conv_maps[gi], e->conv + (size_t)gi * S1 * e->conv_slot(), CU_TENSOR_MAP_DATA_TYPE_FLOAT32,
+                      4, KEY_DIM, 3, S1 * CONV_KEEP, KEY_DIM * 4, CONV_DIM * 4, GDN_D, 3, CONV_KEEP));
+    }
   TRY(make_decode_map(&e->new_maps[0], e->knew, M * ATT_HKV));
   TRY(make_decode_map(&e->new_maps[1], e->vnew, M * ATT_HKV));
 #undef TRY
@@ -825,10 +865,17 @@ int hsg_gdn_step(const void* packed, const float* a, const float* b, const float
   g.A_log = A_log; g.dt_bias = dt_bias; g.state = state; g.err = err;
   const dim3 grid(GDN_H, std::min(n, GDN_CTAS_PER_HEAD));
   if (state_dtype == HSG_STATE_F16 && lb <= GDNT_MAX_LB) {
-    CUtensorMap tm;
-    if ((rc = make_state_map(&tm, state, (int64_t)max_slots + 1)) != HSG_OK) return rc;
+    GdntMaps maps;
+    if ((rc = make_state_map(&maps.state, state, (int64_t)max_slots + 1)) != HSG_OK) return rc;
+    if ((rc = make_map_3d(&maps.in0, packed, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, KEY_DIM, 3, (uint64_t)n * lb,
+                          KEY_DIM * 2, CONV_DIM * 2, GDN_D, 3, lb)) != HSG_OK)
+      return rc;
+    maps.in1 = maps.in2 = maps.in0;
     g.stages = gdnt_stages(lb, false);
-    gdn_tc_kernel<false><<<grid, GDNT_THREADS, gdnt_smem_bytes(lb, false), (cudaStream_t)stream>>>(tm, g);
+    if (lb == 1)
+      gdn_tc_kernel<false, 4><<<grid, GDNT_THREADS, gdnt_smem_bytes(lb, false), (cudaStream_t)stream>>>(maps, g);
+    else
+      gdn_tc_kernel<false, 3><<<grid, GDNT_THREADS, gdnt_smem_bytes(lb, false), (cudaStream_t)stream>>>(maps, g);
   } else if (state_dtype == HSG_STATE_F16) {
     const int tile = GDN_D * GDN_D * 2;
     g.stages = gdn_stages(lb, tile);
