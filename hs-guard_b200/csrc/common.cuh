@@ -283,8 +283,9 @@ __device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.lau
 
 // ---- math -------------------------------------------------------------------------------------------------------
 __device__ __forceinline__ float silu(float x) { return x / (1.0f + expf(-x)); }
-// SiLU with the hardware exponential and reciprocal (a few ulp): used where it sits on a GEMM epilogue's critical path
-__device__ __forceinline__ float silu_fast(float x) { return x * __frcp_rn(1.0f + __expf(-x)); }
+// SiLU with the approximate exponential and division (a few ulp; used where the result feeds a hi/lo operand split or
+// an fp16 store whose own rounding dominates). For x < -87 the divisor exceeds 2^126 and the quotient is 0, the limit.
+__device__ __forceinline__ float silu_fast(float x) { return __fdividef(x, 1.0f + __expf(-x)); }
 __device__ __forceinline__ float sigmoidf_(float x) { return 1.0f / (1.0f + expf(-x)); }
 
 __device__ __forceinline__ float warp_sum(float v) {

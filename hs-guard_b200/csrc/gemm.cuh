@@ -7,10 +7,11 @@
 // activation operand is given as two bf16 matrices (hi, lo) with hi + lo ~= the fp32 activation; both are
 // accumulated into the same TMEM accumulator, which makes the product accurate to near fp32 against bf16 weights.
 //
-// Roles in a 128-thread CTA: thread 0 issues the TMA loads (a STAGES-deep ring of shared-memory buffers), thread 32
-// issues tcgen05.mma and commits each stage back to the producer, then all four warps drain TMEM (warp w owns
-// accumulator lanes 32w..32w+31 = weight rows) into a shared-memory tile that one TMA bulk store (or bulk
-// reduce-add, for split-K partial sums accumulated into the fp32 residual stream) writes out. Before the dependency
+// Roles in a 256-thread CTA: thread 0 issues the TMA loads (a STAGES-deep ring of shared-memory buffers), thread 32
+// issues tcgen05.mma and commits each stage back to the producer, then all eight warps drain TMEM into a
+// shared-memory tile that one TMA bulk store (or bulk reduce-add, for split-K partial sums accumulated into the fp32
+// residual stream) writes out: warps w and w + 4 share accumulator lanes 32 (w % 4) .. + 31 (= weight rows) and
+// take one half of the token columns each, so every scheduler has two warps to overlap the epilogue's latencies. Before the dependency
 // wait of programmatic dependent launch the CTA sets up its barriers and TMEM, requests its first weight tiles and
 // asks L2 to prefetch the rest of its weight slab. Every wait is bounded and reports through `err`.
 #pragma once
@@ -34,7 +35,7 @@ struct GemmArgs {
   int* err;
 };
 
-constexpr int GEMM_THREADS = 128;
+constexpr int GEMM_THREADS = 256;
 constexpr int GEMM_BK = 64;                       // K elements per stage (128 bytes: one swizzle row)
 constexpr int GEMM_A_BYTES = 128 * GEMM_BK * 2;   // 16 KB weight tile
 
@@ -147,15 +148,18 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__
   const bool have = __syncthreads_and(mbar_wait(done, 0, args.err, ERR_TIMEOUT_MMA));
   tc_fence_after();
   if (have && nk > 0) {
-    const int row = warp * 32 + lane;  // accumulator lane == weight row within the tile
-    const uint32_t lane_base = tmem + ((uint32_t)(warp * 32) << 16);
+    const int quad = warp & 3;          // TMEM lane quadrant this warp may access
+    const int row = quad * 32 + lane;   // accumulator lane == weight row within the tile
+    const uint32_t lane_base = tmem + ((uint32_t)(quad * 32) << 16);
+    const int nch = (tn + 31) / 32, half_ch = (nch + 1) / 2;  // 32-column chunks: warps 0-3 the first half
+    const int c_begin = (warp >> 2) ? half_ch * 32 : 0, c_end = (warp >> 2) ? nch * 32 : half_ch * 32;
     if (args.mode == GEMM_SILU_MUL) {
       // rows (2f, 2f+1) hold (gate, up) of feature f: the pair sits in adjacent lanes
       __nv_bfloat16* sh = reinterpret_cast<__nv_bfloat16*>(smem);  // [tn][64]
       __nv_bfloat16* sl = sh + tn * 64;                              // [tn][64]
       // after the exchange the even lane holds (gate, up) of even tokens, the odd lane of odd tokens
       const int f = row >> 1, odd = lane & 1;
-      for (int c = 0; c < tn; c += 32) {
+      for (int c = c_begin; c < c_end; c += 32) {
         float v[32];
         tmem_ld32(lane_base + c, v);
 #pragma unroll
@@ -170,7 +174,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__
       }
     } else {
       float* tile = reinterpret_cast<float*>(smem);  // [tn][128]
-      for (int c = 0; c < tn; c += 32) {
+      for (int c = c_begin; c < c_end; c += 32) {
         float v[32];
         tmem_ld32(lane_base + c, v);
 #pragma unroll
