@@ -188,11 +188,25 @@ class SlotEngine:
             raise ValueError("a session may appear once per tick")
         return self.run_arrays([c for _, c in requests], slots)
 
+    def fits_one_tick(self, requests):
+        """Whether ``requests`` run as a single tick (<= largest row bucket, every request <= 64 tokens)."""
+        largest = TOKEN_BUCKETS[-1]
+        return len(requests) <= self.session_buckets[-1] and all(len(ids) <= largest for _, ids in requests)
+
+    def tick(self, requests):
+        """One tick for requests that fit one (``fits_one_tick``): ([roles, n, lb, 3] probabilities, lens)."""
+        slots = np.fromiter((s for s, _ in requests), dtype=np.int64, count=len(requests))
+        return self.run_arrays([ids for _, ids in requests], slots)
+
     def step(self, requests):
         """requests [(slot, token_ids)], each slot at most once -> {role: [np.ndarray [L_i, 3]]}
         (reference slot_engine_v7.py:147-167): long requests run as consecutive <=64-token ticks."""
         if len({s for s, _ in requests}) != len(requests):
             raise ValueError("a session may appear once per tick")
+        if requests and self.fits_one_tick(requests):
+            probs, lens = self.tick(requests)
+            return {role: [probs[r, row, :n] for row, n in enumerate(lens.tolist())]
+                    for r, role in enumerate(self.roles)}
         largest, rows = TOKEN_BUCKETS[-1], self.session_buckets[-1]
         results = {role: [[] for _ in requests] for role in self.roles}
         pending = [(i, s, list(ids)) for i, (s, ids) in enumerate(requests)]

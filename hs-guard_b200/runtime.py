@@ -25,8 +25,11 @@ def validate_requests(requests, role, max_slots, vocab_size):
     for slot, ids in requests:
         if not isinstance(slot, int) or not 0 <= slot < max_slots:
             raise ValueError("Slot is outside the allocated range")
-        if not ids or any(not isinstance(i, int) or not 0 <= i < vocab_size for i in ids):
+        if not ids:
             raise ValueError("Each request requires nonempty in-vocabulary integer token IDs")
+        for i in ids:
+            if not isinstance(i, int) or not 0 <= i < vocab_size:
+                raise ValueError("Each request requires nonempty in-vocabulary integer token IDs")
 
 
 class StreamingGuard:
@@ -54,7 +57,16 @@ class StreamingGuard:
 
     def step(self, requests, role="assistant"):
         validate_requests(requests, role, self.max_slots, self.vocab_size)
-        outputs = self.engine.step(requests)[role]
         tau = self.metadata["thresholds"][role]
+        eng = self.engine
+        if eng.fits_one_tick(requests):  # one tick: cut scores for all rows at once
+            probs, lens = eng.tick(requests)
+            cut = 1 - probs[eng.roles.index(role), :, :, 0]  # [n, lb] float32, as the reference's 1 - p[:, 0]
+            if cut.shape[1] == 1:
+                return [{"slot": s, "cut_scores": [c], "threshold": tau}
+                        for (s, _), c in zip(requests, cut[:, 0].tolist())]
+            return [{"slot": s, "cut_scores": row[:n], "threshold": tau}
+                    for (s, _), row, n in zip(requests, cut.tolist(), lens.tolist())]
+        outputs = eng.step(requests)[role]
         return [{"slot": s, "cut_scores": (1 - p[:, 0]).tolist(), "threshold": tau}
                 for (s, _), p in zip(requests, outputs)]

@@ -135,3 +135,45 @@ def test_library_exports_every_header_symbol():
     for s in syms:
         assert hasattr(L, s), s
     assert _lib.lib().hsg_version().startswith(b"hsg-b200")
+
+
+def _fake_engine(max_slots):
+    """A SlotEngine whose device tick is replaced by a deterministic host function of (slot, position, token)."""
+    from hs_guard_b200 import engine as E
+    eng = E.SlotEngine.__new__(E.SlotEngine)
+    eng.max_slots, eng.roles = max_slots, ("user", "assistant")
+    eng.session_buckets = E.default_session_buckets(max_slots)
+    eng.length = np.zeros(max_slots, dtype=np.int64)
+    eng.host, eng.stats, eng._lib, eng._h = {}, {"graph_replays": 0, "ticks": 0}, None, 1
+    eng.cfg = DEFAULT
+
+    def run_arrays(chunks, slots):
+        # deterministic stand-in for the device: p = f(slot, position, token) per role, rows of the tick
+        n = len(chunks)
+        lb = bucket(max(len(c) for c in chunks), (1, 2, 4, 8, 16, 32, 64))
+        probs = np.zeros((2, n, lb, 3), np.float32)
+        lens = np.array([len(c) for c in chunks], np.int64)
+        for row, (c, s) in enumerate(zip(chunks, slots)):
+            for t, tok in enumerate(c):
+                pos = eng.length[s] + t
+                safe = np.float32(((int(s) * 7919 + int(pos) * 31 + tok) % 1000) / 1000.0)
+                probs[:, row, t] = [[safe, 1 - safe, 0], [safe / 2, 1 - safe / 2, 0]]
+        eng.length[np.asarray(slots)] += lens
+        return probs, lens
+    eng.run_arrays = run_arrays
+    return eng
+
+
+def test_streaming_guard_single_tick_path_matches_generic_path():
+    """StreamingGuard.step's one-tick fast path returns exactly what the generic per-request path returns."""
+    from hs_guard_b200.runtime import DEFAULT_METADATA, StreamingGuard
+    rng = np.random.default_rng(3)
+    ticks = [[(s, [int(rng.integers(0, 1000))]) for s in range(40)],                       # one token each
+             [(s, [int(x) for x in rng.integers(0, 1000, rng.integers(1, 9))]) for s in range(0, 40, 3)],
+             [(5, [int(x) for x in rng.integers(0, 1000, 70)])]]                           # > 64 tokens: generic
+    for role in ("user", "assistant"):
+        fast = StreamingGuard.from_engine(_fake_engine(40), DEFAULT_METADATA)
+        slow = StreamingGuard.from_engine(_fake_engine(40), DEFAULT_METADATA)
+        slow.engine.fits_one_tick = lambda requests: False
+        for tick in ticks:
+            assert fast.step(tick, role) == slow.step(tick, role)
