@@ -187,6 +187,19 @@ ring_decode_kernel(const __grid_constant__ CUtensorMap tm_rk, const __grid_const
       mbar_arrive(&meta_free[b]);
       continue;
     }
+    // the output gates of this lane's (row, dim) outputs, loaded now so the latency hides behind both passes
+    float gate[2][2][2] = {};
+    if (!args.out_raw && c4 < 2) {
+#pragma unroll
+      for (int mb = 0; mb < 2; ++mb)
+#pragma unroll
+        for (int half = 0; half < 2; ++half)
+#pragma unroll
+          for (int cc = 0; cc < 2; ++cc) {
+            const int dim = 32 * warp + 16 * mb + g + 8 * half, jq = h * ATT_G + 2 * c4 + cc;
+            gate[mb][half][cc] = args.proj[(size_t)n * ATT_IN + jq * 2 * ATT_D + ATT_D + dim];
+          }
+    }
     // pass-1 B fragments: Q^T for this warp's 64 dims (4 k-steps); query row = fragment column g (rows >= 4 zero)
     uint32_t qb[4][2];
     {
@@ -239,7 +252,7 @@ ring_decode_kernel(const __grid_constant__ CUtensorMap tm_rk, const __grid_const
       const float msafe = mx == -INFINITY ? 0.f : mx;
       float sum = 0.f;
       for (int c = lane; c < nk; c += 32) {
-        const float p = expf(scp[c * 4 + r] - msafe);
+        const float p = __expf(scp[c * 4 + r] - msafe);  // rounded to fp16 below
         pr[r * RD_PSTRIDE + c] = __float2half_rn(p);
         sum += p;
       }
@@ -291,9 +304,8 @@ ring_decode_kernel(const __grid_constant__ CUtensorMap tm_rk, const __grid_const
             if (args.out_raw) {
               args.out_raw[(((size_t)n * ATT_HKV + h) * ATT_G + r) * ATT_D + dim] = val;
             } else {
-              const int jq = h * ATT_G + r;
-              const float gate = args.proj[(size_t)n * ATT_IN + jq * 2 * ATT_D + ATT_D + dim];
-              split_bf16(val * sigmoidf_(gate), ohi[r * ATT_D + dim], olo[r * ATT_D + dim]);
+              const float gt = gate[mb][half][cc];
+              split_bf16(val * __fdividef(1.0f, 1.0f + __expf(-gt)), ohi[r * ATT_D + dim], olo[r * ATT_D + dim]);
             }
           }
         }
