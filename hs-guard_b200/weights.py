@@ -129,15 +129,15 @@ class RandomInitModel:
 
 
 def extract_state_dict(model, head="redline"):
-    """(HsgConfig, state dict) from a reference ``Classifier`` (``.backbone`` + ``.heads``), a
-    RandomInitModel, or a plain dict. ``head='general'`` maps the general heads onto the redline names
+    """(HsgConfig, state dict) from a reference ``Classifier`` (``.backbone`` + ``.heads``), a RandomInitModel or
+    loaded bundle (``.cfg`` + ``.state_dict()``), or a plain dict. ``head='general'`` maps the general heads onto the redline names
     (the swap ``load_model`` performs, reference runtime.py:120-122)."""
     if head not in ("redline", "general"):
         raise ValueError("head must be redline or general")
     if isinstance(model, dict):
         cfg, sd = DEFAULT, model
-    elif isinstance(model, RandomInitModel):
-        cfg, sd = model.cfg, model.state_dict()
+    elif isinstance(getattr(model, "cfg", None), HsgConfig) and callable(getattr(model, "state_dict", None)):
+        cfg, sd = model.cfg, model.state_dict()  # RandomInitModel, bundle.BundleModel
     elif hasattr(model, "backbone") and hasattr(model, "heads"):
         cfg = HsgConfig.from_hf(model.backbone.config)
         sd = {"backbone." + k: v for k, v in model.backbone.state_dict().items()}
