@@ -135,6 +135,25 @@ __device__ __forceinline__ bool named_sync_and(bool pred) {
   return r != 0;
 }
 
+// The same on barrier ID (for a second group of warps that synchronises independently of barrier 1).
+template <int ID, int NTHREADS>
+__device__ __forceinline__ bool named_sync_and_id(bool pred) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.u32 p, %1, 0;\n\t"
+      "bar.red.and.pred q, %2, %3, p;\n\t"
+      "selp.u32 %0, 1, 0, q;\n\t}"
+      : "=r"(r)
+      : "r"((uint32_t)pred), "n"(ID), "n"(NTHREADS)
+      : "memory");
+  return r != 0;
+}
+template <int ID, int NTHREADS>
+__device__ __forceinline__ void named_sync_id() {
+  asm volatile("bar.sync %0, %1;" ::"n"(ID), "n"(NTHREADS) : "memory");
+}
+
 // ---- TMA: 1-D bulk copy and 2-D tiled tensor copy (global -> shared, completion on an mbarrier) ---------------
 __device__ __forceinline__ void bulk_g2s(void* smem_dst, const void* gmem_src, uint32_t bytes, uint64_t* bar) {
   asm volatile(
@@ -324,6 +343,23 @@ __device__ __forceinline__ void mma_f16_16816(float (&d)[4], uint32_t a0, uint32
       : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
+// the same with the accumulator given as four separate registers (e.g. one half of an 8-register fragment row)
+__device__ __forceinline__ void mma_f16_16816_r(float& d0, float& d1, float& d2, float& d3, uint32_t a0, uint32_t a1,
+                                                uint32_t a2, uint32_t a3, uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+      : "+f"(d0), "+f"(d1), "+f"(d2), "+f"(d3)
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+// (hi, lo) fp16 pairs of two fp32 values: hi = fp16(x), lo = fp16(x - hi)
+__device__ __forceinline__ void split_half2x(float a, float b, uint32_t& hi, uint32_t& lo) {
+  const __half2 h = __floats2half2_rn(a, b);
+  const float2 back = __half22float2(h);
+  hi = *reinterpret_cast<const uint32_t*>(&h);
+  const __half2 l = __floats2half2_rn(a - back.x, b - back.y);
+  lo = *reinterpret_cast<const uint32_t*>(&l);
+}
+
 // inverse of ldmatrix_x4_trans: the four 8x8 fragments go back to the same (transposed) places
 __device__ __forceinline__ void stmatrix_x4_trans(uint32_t addr, uint32_t r0, uint32_t r1, uint32_t r2, uint32_t r3) {
   asm volatile("stmatrix.sync.aligned.m8n8.x4.trans.shared.b16 [%0], {%1,%2,%3,%4};" ::"r"(addr), "r"(r0), "r"(r1),

@@ -15,6 +15,7 @@
 #include "common.cuh"
 #include "gdn.cuh"
 #include "gdn_tc.cuh"
+#include "gdn_chunk.cuh"
 #include "gemm.cuh"
 #include "norm.cuh"
 #include "ring_decode.cuh"
@@ -252,6 +253,8 @@ static int set_kernel_attributes() {
   CU(cudaFuncSetAttribute(gdn_tc_kernel<true, 3>, cudaFuncAttributeMaxDynamicSharedMemorySize, GDN_SMEM_LIMIT));
   CU(cudaFuncSetAttribute(gdn_tc_kernel<false, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize, GDN_SMEM_LIMIT));
   CU(cudaFuncSetAttribute(gdn_tc_kernel<false, 3>, cudaFuncAttributeMaxDynamicSharedMemorySize, GDN_SMEM_LIMIT));
+  CU(cudaFuncSetAttribute(gdn_chunk_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, GDN_SMEM_LIMIT));
+  CU(cudaFuncSetAttribute(gdn_chunk_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, GDN_SMEM_LIMIT));
   CU(cudaFuncSetAttribute(ring_attn_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, attn_smem_bytes(4)));
   CU(cudaFuncSetAttribute(ring_attn_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, attn_smem_bytes(8)));
   CU(cudaFuncSetAttribute(ring_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, rd_smem_bytes()));
@@ -366,6 +369,13 @@ static int enqueue_step(hsg_engine* e, int nb, int lb) {
                           GDN_IN * 4, GDNT_AB, lb, CU_TENSOR_MAP_SWIZZLE_NONE)) != HSG_OK)
       return rc;
   }
+  // the chunked kernel (fp16 state, ticks of 32 or 64 tokens): the projection's q|k|v columns, [lb][3][128] boxes
+  const bool chunked = e->rec_elem == 2 && lb > GDNT_MAX_LB && lb % GDNC_SUB == 0 && lb <= GDNC_MAX_LB;
+  GdntMaps ch_maps;
+  if (chunked &&
+      (rc = make_map_3d(&ch_maps.in1, e->proj, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, KEY_DIM, 3, M, KEY_DIM * 4,
+                        GDN_IN * 4, GDN_D, 3, lb)) != HSG_OK)
+    return rc;
   {
     ProfScope ps(e, HSG_PROF_EMBED);
     embed_norm_kernel<<<M, NORM_THREADS, 0, st>>>(ids, static_cast<const __nv_bfloat16*>(e->w.embed), e->cfg.vocab,
@@ -403,6 +413,13 @@ static int enqueue_step(hsg_engine* e, int nb, int lb) {
           else
             CU(launch_k(gdn_tc_kernel<true, 3>, grid, dim3(GDNT_THREADS), gdnt_smem_bytes(lb, true), st, e->pdl,
                         tc_maps, g));
+        } else if (chunked) {
+          g.stages = gdnc_stages(lb, true);
+          ch_maps.state = e->state_maps[gi];
+          ch_maps.in0 = e->conv_maps[gi];
+          ch_maps.in2 = ch_maps.in1;
+          CU(launch_k(gdn_chunk_kernel<true>, grid, dim3(GDNT_THREADS), gdnc_smem_bytes(lb, true), st, e->pdl,
+                      ch_maps, g));
         } else if (e->rec_elem == 2) {
           const int tile = GDN_D * GDN_D * 2;
           g.stages = gdn_stages(lb, tile);
@@ -876,6 +893,15 @@ int hsg_gdn_step(const void* packed, const float* a, const float* b, const float
       gdn_tc_kernel<false, 4><<<grid, GDNT_THREADS, gdnt_smem_bytes(lb, false), (cudaStream_t)stream>>>(maps, g);
     else
       gdn_tc_kernel<false, 3><<<grid, GDNT_THREADS, gdnt_smem_bytes(lb, false), (cudaStream_t)stream>>>(maps, g);
+  } else if (state_dtype == HSG_STATE_F16 && lb % GDNC_SUB == 0) {  // 32 or 64 tokens: the chunked kernel
+    GdntMaps maps;
+    if ((rc = make_state_map(&maps.state, state, (int64_t)max_slots + 1)) != HSG_OK) return rc;
+    if ((rc = make_map_3d(&maps.in0, packed, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, KEY_DIM, 3, (uint64_t)n * lb,
+                          KEY_DIM * 2, CONV_DIM * 2, GDN_D, 3, lb)) != HSG_OK)
+      return rc;
+    maps.in1 = maps.in2 = maps.in0;
+    g.stages = gdnc_stages(lb, false);
+    gdn_chunk_kernel<false><<<grid, GDNT_THREADS, gdnc_smem_bytes(lb, false), (cudaStream_t)stream>>>(maps, g);
   } else if (state_dtype == HSG_STATE_F16) {
     const int tile = GDN_D * GDN_D * 2;
     g.stages = gdn_stages(lb, tile);

@@ -208,6 +208,34 @@ def test_gdn_config2_size_fp16_state(L):
     assert ((pool2.float() - pool.float()).norm() / pool.float().norm()) < 1e-2
 
 
+@pytest.mark.parametrize("lb,lens", [(64, [64, 50, 0, 1, 64]), (32, [32, 17, 0, 31, 2])])
+def test_gdn_chunked_vs_oracle(L, lb, lens):
+    """fp16-state ticks of 32 and 64 tokens run the chunked (WY) kernel: against the token-by-token oracle from the
+    same fp16 initial state, with ragged lengths, a padding row on the scratch slot and permuted slots."""
+    n = len(lens)
+    packed, a, b, state = gdn_raw(n, lb, 70 + lb)
+    S = n + 2
+    slots = np.array([3, 0, S, 5, 1])[:n]
+    g = torch.Generator().manual_seed(lb)
+    pool = (torch.randn(S + 1, 16, 128, 128, generator=g) * 0.05).half()
+    A_log, dt = torch.randn(16, generator=g) * 0.5, torch.randn(16, generator=g)
+    gpu_pool = pool.cuda()
+    o = _gdn_gpu(L, packed, a, b, gpu_pool, slots, np.array(lens), A_log, dt)
+    ref_pool = pool.float().clone()
+    ref = K.gdn_slot_step(packed, a, b, A_log, dt, ref_pool, torch.from_numpy(slots), torch.tensor(lens))
+    got = o.cpu()
+    assert float((got - ref).norm() / ref.norm()) < 5e-3
+    torch.testing.assert_close(got, ref, rtol=2e-2, atol=2e-3)
+    rows = [int(s_) for s_, l_ in zip(slots, lens) if l_ > 0]
+    new = gpu_pool.float().cpu()
+    rel = (new[rows] - ref_pool[rows]).norm() / ref_pool[rows].norm()
+    assert rel < 5e-3, rel
+    untouched = [r for r in range(S + 1) if r not in rows]
+    assert torch.equal(new[untouched], pool.float()[untouched])
+    for row, l_ in enumerate(lens):  # padded positions are zero
+        assert torch.count_nonzero(got[row, l_:]) == 0
+
+
 # ---- ring attention ---------------------------------------------------------------------------------------------
 def _ring_gpu(L, q, ring_k, ring_v, new_k, new_v, ring_pos, slots, starts, lens, write_ring=0):
     n, _, m, _ = q.shape
