@@ -45,6 +45,8 @@ def parse():
     ap.add_argument("--contexts", default=",".join(map(str, CONTEXTS)))
     ap.add_argument("--cpu-slots", type=int, default=32)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--workload", default="c4", choices=("c4", "c5"),
+                    help="c4: single-token steps after prefill (the headline); c5: 64-token ticks with reassignment")
     ap.add_argument("--state-dtype", default="float16", choices=("float16", "float32"),
                     help="recurrent-state storage (float16 = the reference StreamingGuard's)")
     return ap.parse_args()
@@ -314,7 +316,7 @@ def run_ours(args):
                     "d2h_bytes_per_step": 2 * S * 3 * 4 + 4},
             "gpu_launches": launches * K,
             "clocks": clocks,
-            "roofline": {"kernel": "gdn_step_kernel (fused conv + gated delta rule + gated norm)", "bound": "hbm",
+            "roofline": {"kernel": "gdn_tc_kernel (fused conv + gated delta rule + gated norm)", "bound": "hbm",
                          "achieved": achieved, "peak": hbm_peak, "unit": "GB/s", "frac": achieved / hbm_peak,
                          "peak_source": peak_src, "traffic": traffic, "algorithmic_bytes": gdn_bytes,
                          "avg_launch_ms": gdn_avg_ms},
@@ -330,10 +332,183 @@ def run_ours(args):
         torch.distributed.destroy_process_group()
 
 
+def run_c5(args):
+    """C5 per GPU: 352 slots stream 64-token ticks (the chunked delta-rule path); each slot's conversation has a
+    512, 2,048 or 8,000-token context (one third each, seed 5 + 1000 rank) and the slot is reset and reassigned when it
+    ends or after 4,096 tokens, whichever comes first. Starting points are staggered so that reassignments spread over
+    the ticks; the resets (hsg_reset_slot) are inside the timed region. A step is one tick of 352 x 64 tokens."""
+    import torch
+    rank, world, local = dist_env()
+    torch.cuda.set_device(local)
+    if world > 1:
+        import torch.distributed as dist
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=600), device_id=torch.device("cuda", local))
+    from hs_guard_b200 import _lib
+    from hs_guard_b200 import weights as W
+    from hs_guard_b200.build import build
+    from hs_guard_b200.engine import SlotEngine
+    from hs_guard_b200.pack import pack_inputs
+    from hs_guard_b200.runtime import DEFAULT_METADATA, StreamingGuard
+
+    if rank == 0:
+        build()
+    if world > 1:
+        torch.distributed.barrier()
+    S, LB, CAP = args.slots, 64, 4096
+    sd = W.random_state_dict(0)
+    eng = SlotEngine(sd, S, state_dtype=args.state_dtype)
+    state_elem = 2 if args.state_dtype == "float16" else 4
+    guard = StreamingGuard.from_engine(eng, DEFAULT_METADATA)
+    lens = tuple(int(x) for x in args.contexts.split(","))
+    rng = np.random.Generator(np.random.PCG64(5 + 1000 * rank))
+
+    def conversation():
+        return min(int(rng.choice(lens)), CAP) // LB * LB
+
+    left = np.array([conversation() for _ in range(S)], dtype=np.int64)
+    left = rng.integers(1, left // LB + 1) * LB  # staggered: each slot starts somewhere inside its first conversation
+    K, Wm = args.steps, args.warmup
+    slots = np.arange(S, dtype=np.int64)
+
+    def plan(n):
+        """n ticks: (slots reset before the tick, token chunks)."""
+        out = []
+        for _ in range(n):
+            resets = np.nonzero(left == 0)[0]
+            for s in resets:
+                left[s] = conversation()
+            out.append((resets.tolist(), rng.integers(0, 248320, (S, LB))))
+            left[:] -= LB
+        return out
+
+    def barrier():
+        torch.cuda.synchronize()
+        if world > 1:
+            torch.distributed.barrier()
+        torch.cuda.synchronize()
+
+    def max_over_ranks(x):
+        if world == 1:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device="cuda")
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        return float(t.item())
+
+    # ---- device-resident ticks (value) ----
+    eng.reset()
+    L = eng._lib
+    ticks = plan(Wm + K)
+    length = eng.length.copy()
+    staged = []
+    for resets, chunk in ticks:
+        length[resets] = 0
+        buf = np.zeros(S * LB + 3 * S, dtype=np.int64)
+        pack_inputs(chunk.tolist(), slots, S, LB, length, S, buf)
+        length += LB
+        staged.append(torch.from_numpy(buf).cuda())
+
+    def run_tick(k):
+        for s in ticks[k][0]:
+            _lib.check(L.hsg_reset_slot(eng.handle, int(s)))
+        _lib.check(L.hsg_launch(eng.handle, staged[k].data_ptr(), S, LB))
+
+    for k in range(Wm):
+        run_tick(k)
+    _lib.check(L.hsg_synchronize(eng.handle))
+    stream = torch.cuda.ExternalStream(L.hsg_stream(eng.handle))
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    clk = Clocks(local).__enter__()
+    barrier()
+    start.record(stream)
+    for k in range(Wm, Wm + K):
+        run_tick(k)
+    end.record(stream)
+    end.synchronize()
+    _lib.check(L.hsg_fetch(eng.handle, S, LB, None))
+    eng.length[:] = length
+    dev_ms = max_over_ranks(start.elapsed_time(end) / K)
+    n_resets = sum(len(t[0]) for t in ticks[Wm:])
+
+    # ---- end to end: slot resets + StreamingGuard.step with host lists ----
+    lat = []
+    e2e_ticks = plan(Wm + K)
+    for k, (resets, chunk) in enumerate(e2e_ticks):
+        if k == Wm:
+            barrier()
+        t0 = time.perf_counter()
+        for s in resets:
+            eng.reset_slot(s)
+        guard.step([(int(s), row) for s, row in zip(slots, chunk.tolist())], role="assistant")
+        if k >= Wm:
+            lat.append((time.perf_counter() - t0) * 1e3)
+    clk.__exit__(None, None, None)
+    e2e_ms = max_over_ranks(float(np.mean(lat)))
+    p50 = max_over_ranks(float(np.percentile(lat, 50)))
+    p95 = max_over_ranks(float(np.percentile(lat, 95)))
+
+    # ---- per-kernel CUDA events of one eager tick ----
+    _, prof = eng.profile_tick(rng.integers(0, 248320, (S, LB)).tolist(), slots)
+    peaks = {}
+    try:
+        peaks = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))
+    except (OSError, ValueError):
+        pass
+    tflops_peak, tsrc = (peaks["bf16_tflops_sustained"], "measured sustained") if "bf16_tflops_sustained" in peaks \
+        else (1400.0, "fallback sustained")
+    hbm_peak, hsrc = (peaks["hbm_gbs"], "measured") if "hbm_gbs" in peaks else (6650.0, "fallback")
+    gemm_ms = sum(v[0] for k, v in prof.items() if k.startswith("gemm") or k == "head_gemm")
+    gemm_n = sum(v[1] for k, v in prof.items() if k.startswith("gemm") or k == "head_gemm")
+    gemm_flops = 2.0 * 498_113_344 * S * LB  # algorithmic (the hi/lo activation pair executes twice this)
+    gdn_ms, gdn_n = prof["gdn"]
+    gdn_bytes = gdn_bytes_per_launch(S, LB, state_elem)
+    launches = eng.launches_per_step(S, LB)
+    if rank == 0:
+        tokens = S * LB * world
+        value = tokens / (dev_ms * 1e-3)
+        achieved = gemm_flops / (gemm_ms * 1e-3) / 1e12
+        line = {
+            "metric": "scored tokens/s/GPU at 352 slots (C5: 64-token ticks)", "value": value, "unit": "tokens/s",
+            "n_gpus": world, "steps": K, "warmup": Wm, "ms_per_step": dev_ms, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None,
+            "dtype": f"f32 (norms, conv history, accumulation; {args.state_dtype} recurrent state; bf16 hi/lo "
+                     "tensor-core operands; fp16 ring)",
+            "data": "synthetic (uniform random token ids; random-init weights, seed 0)",
+            "config": {"workload": "C5: 64-token ticks over 352 slots per GPU, contexts 512/2048/8000 (seed 5), "
+                                   "slot reset and reassignment at the end of a conversation or after 4096 tokens",
+                       "slots_per_gpu": S, "tokens_per_tick": S * LB, "contexts": list(lens), "reassign_after": CAP,
+                       "resets_in_timed_ticks": n_resets, "parallelism": f"slot-sharded x{world}",
+                       "l2": "no flush: each tick touches > 10 GB (> 126 MB L2)"},
+            "latency_ms": {"p50": p50, "p95": p95, "device_per_step": dev_ms},
+            "e2e": {"value": tokens / (e2e_ms * 1e-3), "unit": "tokens/s",
+                    "h2d_bytes_per_step": (S * LB + 3 * S) * 8, "d2h_bytes_per_step": 2 * S * LB * 3 * 4 + 4},
+            "gpu_launches": launches * K,
+            "clocks": clk.summary(),
+            "roofline": {"kernel": "gemm_tc_kernel (all projections of one tick)", "bound": "tensor",
+                         "achieved": achieved, "peak": tflops_peak, "unit": "TFLOP/s", "frac": achieved / tflops_peak,
+                         "peak_source": tsrc, "traffic": None, "algorithmic_flops": gemm_flops,
+                         "tick_ms": gemm_ms, "launches": gemm_n},
+            "gdn_chunk": {"kernel": "gdn_chunk_kernel", "avg_launch_ms": gdn_ms / max(gdn_n, 1),
+                          "algorithmic_bytes": gdn_bytes,
+                          "achieved_gbs": gdn_bytes / (gdn_ms / max(gdn_n, 1) * 1e-3) / 1e9,
+                          "hbm_frac": gdn_bytes / (gdn_ms / max(gdn_n, 1) * 1e-3) / 1e9 / hbm_peak,
+                          "peak_source": hsrc},
+            "kernel_ms_eager": {k: round(v[0], 4) for k, v in prof.items() if v[1]},
+            "cpu_baseline": None,
+        }
+        print(json.dumps(line), flush=True)
+    eng.close()
+    if world > 1:
+        torch.distributed.barrier()
+        torch.distributed.destroy_process_group()
+
+
 def main():
     args = parse()
     if args.impl == "reference":
         run_reference(args)
+    elif args.workload == "c5":
+        run_c5(args)
     else:
         run_ours(args)
 

@@ -261,7 +261,7 @@ def test_ring_attention_matches_reference_golden(L, golden, name, lb):
     np.testing.assert_allclose(out.cpu().numpy(), golden[name + "_o"], rtol=2e-3, atol=2e-3)
 
 
-@pytest.mark.parametrize("lb", [1, 2, 16, 64])
+@pytest.mark.parametrize("lb", [1, 2, 8, 16, 32, 64])
 def test_ring_attention_vs_oracle(L, lb):
     q, rk, rv, nk, nv, rp, slots, starts, lens = ring_inputs(lb=lb, seed=40 + lb, n=6)
     # use fp16-rounded K/V on both sides (the engine's ring precision)
