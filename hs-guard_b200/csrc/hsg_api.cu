@@ -161,6 +161,17 @@ static GemmPlan plan_gemm(int n_w, int K, int M, int mode, int use_lo) {
   int stages = 4;
   while (stages > 2 && gemm_smem(best.tn, use_lo, stages) > SMEM_MAX) --stages;
   best.stages = std::min(stages, std::max(2, best.kps));
+  const int tb_full = (M + 255) / 256;
+  if ((long)tiles * tb_full >= 4L * SM_COUNT) {
+    // A long-running grid (many waves of full tiles): 128-token tiles with two stages (97 KB of shared memory, 128
+    // TMEM columns) so that two CTAs share each SM and one's epilogue and pipeline fill overlap the other's MMAs.
+    // Measured at 22,528 tokens against 256-token tiles with one CTA per SM: 8-10 % faster for K = 1024.
+    best.tn = 128;
+    best.tb = (M + 127) / 128;
+    best.splits = 1;
+    best.kps = KB;
+    best.stages = 2;
+  }
   best.smem = gemm_smem(best.tn, use_lo, best.stages);
   return best;
 }

@@ -297,3 +297,31 @@ def test_ring_attention_config3_with_ring_write(L):
     for s in range(n):
         col = int(starts[s]) % 512
         assert torch.equal(ring_k[s, :, col], nk[s, :, 0]), s
+
+
+@pytest.mark.parametrize("mode", [0, 1, 2])
+def test_gemm_large_m_two_ctas_per_sm(L, mode):
+    """Long-running grids (>= 4 waves of 256-token tiles) take 128-token, two-stage tiles (two CTAs per SM)."""
+    torch.manual_seed(3)
+    m, n, k = 19000, 1024, 1024
+    w = (torch.randn(n, k, device="cuda") * 0.03).to(torch.bfloat16)
+    x = torch.randn(m, k, device="cuda")
+    hi, lo = _split(x)
+    xin = hi.double() + lo.double()
+    err = _err()
+    if mode == 2:
+        ahi = torch.zeros(m, n // 2, dtype=torch.bfloat16, device="cuda")
+        alo = torch.zeros_like(ahi)
+        L.check(L.lib().hsg_gemm(w.data_ptr(), n, k, hi.data_ptr(), lo.data_ptr(), m, m, None, ahi.data_ptr(),
+                                 alo.data_ptr(), 2, 0, err.data_ptr(), None))
+        _done(L, err)
+        g, u = xin @ w[0::2].double().T, xin @ w[1::2].double().T
+        torch.testing.assert_close(ahi.double() + alo.double(), F.silu(g) * u, rtol=1e-4, atol=1e-5)
+        return
+    base = torch.randn(m, n, device="cuda") if mode == 1 else torch.zeros(m, n, device="cuda")
+    y = base.clone()
+    L.check(L.lib().hsg_gemm(w.data_ptr(), n, k, hi.data_ptr(), lo.data_ptr(), m, m, y.data_ptr(), None, None, mode,
+                             0, err.data_ptr(), None))
+    _done(L, err)
+    ref = ((base.double() if mode == 1 else 0) + xin @ w.double().T).float()
+    torch.testing.assert_close(y, ref, rtol=1e-4, atol=2e-4)
