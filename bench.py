@@ -13,6 +13,8 @@ Reported (rank 0, one JSON line):
   copy, replay, device->host copy of the probabilities, 1 - p(safe)); latency_ms p50/P95 are of these steps.
 - roofline: the dominant kernel (gated-delta-rule step) timed live with CUDA events in an eager tick.
 - cpu_baseline: the CPU oracle port of the same step on this host's cores (bounded sample).
+- complete_message: the reference's complete-message path (C1: one 256-id message) through MessageScorer on the GPU
+  (batch 1 and 64) and through the CPU oracle port of the reference's forward on the host cores.
 --impl reference times the CPU oracle port of the reference's step instead (the reference itself is Triton/CUDA-only
 Python that is not shipped to the GPU host) and prints its own line.
 """
@@ -144,6 +146,44 @@ def cpu_oracle_rate(sd, slots, steps, warmup):
             "sample": f"{slots} slots x {steps} single-token steps (after {warmup} warm-up) of the CPU oracle port "
                       f"(fp32 torch), full 512-column rings, context position {start}",
             "ms_per_step": per_step * 1e3}
+
+
+def cpu_complete_message_rate(sd, n_tokens=256, reps=2):
+    """C1: the CPU oracle port of the reference's complete-message forward (oracle.stream.score_complete, fp32 torch,
+    all host threads) on one message of ``n_tokens`` uniform-random ids (seed 1)."""
+    import torch
+    from hs_guard_b200 import DEFAULT
+    from oracle.stream import Weights, score_complete
+    torch.set_num_threads(os.cpu_count() or 1)
+    w = Weights(sd, DEFAULT)
+    ids = np.random.Generator(np.random.PCG64(1)).integers(0, 248320, n_tokens)
+    score_complete(sd, DEFAULT, ids, w=w)
+    t0 = time.perf_counter()
+    for _ in range(reps):
+        score_complete(sd, DEFAULT, ids, w=w)
+    dt = (time.perf_counter() - t0) / reps
+    return {"value": n_tokens / dt, "unit": "tokens/s", "cores": torch.get_num_threads(), "kind": "port",
+            "sample": f"batch 1, one message of {n_tokens} ids (seed 1), {reps} timed runs after 1 warm-up",
+            "ms_per_message": dt * 1e3}
+
+
+def gpu_complete_message_rate(sd, state_dtype, n_tokens=256, batch=1, reps=10):
+    """The same complete-message scoring on the GPU through MessageScorer (fresh slots, 64-token ticks, probabilities
+    copied to the host): ``batch`` messages of ``n_tokens`` ids scored side by side."""
+    from hs_guard_b200.messages import MessageScorer
+    scorer = MessageScorer(sd, max_slots=batch, state_dtype=state_dtype)
+    rng = np.random.Generator(np.random.PCG64(1))
+    seqs = [[int(x) for x in rng.integers(0, 248320, n_tokens)] for _ in range(batch)]
+    for _ in range(3):
+        scorer.probabilities(seqs)
+    t0 = time.perf_counter()
+    for _ in range(reps):
+        scorer.probabilities(seqs)
+    dt = (time.perf_counter() - t0) / reps
+    scorer.close()
+    return {"value": batch * n_tokens / dt, "unit": "tokens/s", "ms_per_batch": dt * 1e3,
+            "sample": f"batch {batch} x {n_tokens} ids, {reps} timed batches (host wall clock, includes slot resets, "
+                      "H2D of the ids and D2H of the probabilities)"}
 
 
 def run_reference(args):
@@ -294,9 +334,15 @@ def run_ours(args):
     step_bytes = tick_bytes(S, 1, state_elem)
 
     cpu = None
+    complete = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cb = cpu_oracle_rate(sd, args.cpu_slots, 3, 1)
         cpu = {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")}
+        eng.close()
+        eng = None
+        complete = {"gpu_batch1": gpu_complete_message_rate(sd, args.state_dtype),
+                    "gpu_batch64": gpu_complete_message_rate(sd, args.state_dtype, batch=64, reps=5),
+                    "cpu_port_batch1": cpu_complete_message_rate(sd)}
 
     if rank == 0:
         value = S * world / (dev_ms * 1e-3)
@@ -324,9 +370,11 @@ def run_ours(args):
                               "frac": step_bytes / (dev_ms * 1e-3) / 1e9 / hbm_peak},
             "kernel_ms_eager": {k: round(v[0], 4) for k, v in prof.items() if v[1]},
             "cpu_baseline": cpu,
+            "complete_message": complete,
         }
         print(json.dumps(line), flush=True)
-    eng.close()
+    if eng is not None:
+        eng.close()
     if world > 1:
         torch.distributed.barrier()
         torch.distributed.destroy_process_group()

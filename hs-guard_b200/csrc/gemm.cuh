@@ -199,7 +199,9 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__
         tma_reduce_add_2d(&tm_o0, smem, wrow0, tok0);
       }
       bulk_commit();
-      bulk_wait_all();
+      // only the shared-memory source must outlive the CTA; the writes complete with the grid, which is what the
+      // next kernel's dependency wait observes
+      bulk_wait_read_all();
     }
     // Error path only: loads the MMA never consumed may still be in flight; wait for them (bounded) before exit.
     for (int i = progress[1]; i < progress[0]; ++i) mbar_wait(&full[i % S], (i / S) & 1, args.err, ERR_TIMEOUT_TMA);
