@@ -69,6 +69,35 @@ __host__ __device__ inline int gdnc_smem_bytes(int lb, bool fused) {
 
 __device__ __forceinline__ uint32_t ld_u32(const void* p) { return *reinterpret_cast<const uint32_t*>(p); }
 
+// Causal depthwise conv (kernel 4: c.x oldest .. c.w current) + SiLU of one channel over tokens tb..tb+15, in place
+// (xc[t * stride]). w holds the three inputs before the block and afterwards the block's last three; outputs of
+// tokens >= len are 0 and hist receives the three inputs ending at token len - 1 when that token is in the block;
+// sq gets the squared outputs. All loads are issued before the arithmetic so the 16 tokens overlap.
+__device__ __forceinline__ void conv_block16(float* xc, int stride, float4 c, float (&w)[3], int tb, int len,
+                                             float (&hist)[3], float (&sq)[16]) {
+  float in[19];
+  in[0] = w[0];
+  in[1] = w[1];
+  in[2] = w[2];
+#pragma unroll
+  for (int u = 0; u < 16; ++u) in[3 + u] = xc[(tb + u) * stride];
+#pragma unroll
+  for (int u = 0; u < 16; ++u) {
+    const float y = silu_fast(fmaf(c.w, in[u + 3], fmaf(c.z, in[u + 2], fmaf(c.y, in[u + 1], c.x * in[u]))));
+    const float o = tb + u < len ? y : 0.f;
+    xc[(tb + u) * stride] = o;
+    sq[u] = o * o;
+    if (tb + u == len - 1) {
+      hist[0] = in[u + 1];
+      hist[1] = in[u + 2];
+      hist[2] = in[u + 3];
+    }
+  }
+  w[0] = in[16];
+  w[1] = in[17];
+  w[2] = in[18];
+}
+
 // Sum of v[i] over the 32 lanes for 16 values at once (a transposing butterfly: 8 + 4 + 2 + 1 + 1 shuffles instead
 // of 16 x 5). Lane l ends with the total of value ((l >> 4) & 1) * 8 + ((l >> 3) & 1) * 4 + ((l >> 2) & 1) * 2
 // + ((l >> 1) & 1); lanes l and l ^ 1 hold the same total.
@@ -496,45 +525,35 @@ gdn_chunk_kernel(const __grid_constant__ GdntMaps maps, const GdnArgs args) {
       const float* hist = tail_of(s);
       const __nv_bfloat16* raw = reinterpret_cast<const __nv_bfloat16*>(tail_of(s));
       // ---- conv + SiLU (or widening) of all tokens, in place; per-token norm partial sums; gates ----
-      if (qk_thread) {
-        float q0 = 0.f, q1 = 0.f, q2 = 0.f, k0 = 0.f, k1 = 0.f, k2 = 0.f;
-        if (FUSED) {
-          q0 = hist[0 * GDN_D + cc]; q1 = hist[3 * GDN_D + cc]; q2 = hist[6 * GDN_D + cc];
-          k0 = hist[1 * GDN_D + cc]; k1 = hist[4 * GDN_D + cc]; k2 = hist[7 * GDN_D + cc];
+      if (qk_thread && FUSED) {
+        float wq[3] = {hist[0 * GDN_D + cc], hist[3 * GDN_D + cc], hist[6 * GDN_D + cc]};
+        float wk[3] = {hist[1 * GDN_D + cc], hist[4 * GDN_D + cc], hist[7 * GDN_D + cc]};
+        float hq[3] = {0.f, 0.f, 0.f}, hk[3] = {0.f, 0.f, 0.f};
+        for (int tb = 0; tb < lb; tb += GDNC_SUB) {
+          float psq[GDNC_SUB], psk[GDNC_SUB];
+          conv_block16(x + 0 * GDN_D + cc, XS * GDN_D, cq, wq, tb, len, hq, psq);
+          conv_block16(x + 1 * GDN_D + cc, XS * GDN_D, ck, wk, tb, len, hk, psk);
+          const float tq = reduce16(psq, lane), tk = reduce16(psk, lane);
+          if (!(lane & 1))
+            *reinterpret_cast<float2*>(ipart + ((tb + reduce16_index(lane)) * 4 + warp) * 2) = make_float2(tq, tk);
         }
+        float* gp = args.conv_pool + (size_t)meta[s].slot * CONV_KEEP * CONV_DIM + h * GDN_D + cc;
+        gp[0] = hq[0]; gp[CONV_DIM] = hq[1]; gp[2 * CONV_DIM] = hq[2];
+        gp[KEY_DIM] = hk[0]; gp[CONV_DIM + KEY_DIM] = hk[1]; gp[2 * CONV_DIM + KEY_DIM] = hk[2];
+      } else if (qk_thread) {  // the isolated kernel's q, k: widened from bf16
         for (int tb = 0; tb < lb; tb += GDNC_SUB) {
           float psq[GDNC_SUB], psk[GDNC_SUB];
 #pragma unroll
           for (int u = 0; u < GDNC_SUB; ++u) {
             const int t = tb + u;
-            float qv = 0.f, kv = 0.f;
-            if (t < len) {
-              if (FUSED) {
-                const float xq = x[(t * XS + 0) * GDN_D + cc], xk = x[(t * XS + 1) * GDN_D + cc];
-                qv = silu_fast(fmaf(cq.w, xq, fmaf(cq.z, q2, fmaf(cq.y, q1, cq.x * q0))));
-                kv = silu_fast(fmaf(ck.w, xk, fmaf(ck.z, k2, fmaf(ck.y, k1, ck.x * k0))));
-                q0 = q1; q1 = q2; q2 = xq;
-                k0 = k1; k1 = k2; k2 = xk;
-              } else {
-                qv = __bfloat162float(raw[(t * 3 + 0) * GDN_D + cc]);
-                kv = __bfloat162float(raw[(t * 3 + 1) * GDN_D + cc]);
-              }
-            }
-            if (FUSED) {
-              x[(t * XS + 0) * GDN_D + cc] = qv;
-              x[(t * XS + 1) * GDN_D + cc] = kv;
-            }
+            const float qv = t < len ? __bfloat162float(raw[(t * 3 + 0) * GDN_D + cc]) : 0.f;
+            const float kv = t < len ? __bfloat162float(raw[(t * 3 + 1) * GDN_D + cc]) : 0.f;
             psq[u] = qv * qv;
             psk[u] = kv * kv;
           }
           const float tq = reduce16(psq, lane), tk = reduce16(psk, lane);
           if (!(lane & 1))
             *reinterpret_cast<float2*>(ipart + ((tb + reduce16_index(lane)) * 4 + warp) * 2) = make_float2(tq, tk);
-        }
-        if (FUSED) {
-          float* gp = args.conv_pool + (size_t)meta[s].slot * CONV_KEEP * CONV_DIM + h * GDN_D + cc;
-          gp[0] = q0; gp[CONV_DIM] = q1; gp[2 * CONV_DIM] = q2;
-          gp[KEY_DIM] = k0; gp[CONV_DIM + KEY_DIM] = k1; gp[2 * CONV_DIM + KEY_DIM] = k2;
         }
       } else {
         if (cc < lb) {  // gates of token cc: log decay g = -exp(A_log) softplus(a + dt_bias) (threshold 20), beta
@@ -550,26 +569,19 @@ gdn_chunk_kernel(const __grid_constant__ GdntMaps maps, const GdnArgs args) {
           igl[cc] = gl;
           ibe[cc] = be;
         }
-        float e0 = 0.f, e1 = 0.f, e2 = 0.f;
         if (FUSED) {
-          e0 = hist[2 * GDN_D + cc]; e1 = hist[5 * GDN_D + cc]; e2 = hist[8 * GDN_D + cc];
-        }
-        for (int t = 0; t < lb; ++t) {
-          float vv = 0.f;
-          if (t < len) {
-            if (FUSED) {
-              const float xv = x[(t * XS + SV) * GDN_D + cc];
-              vv = silu_fast(fmaf(cq.w, xv, fmaf(cq.z, e2, fmaf(cq.y, e1, cq.x * e0))));
-              e0 = e1; e1 = e2; e2 = xv;
-            } else {
-              vv = __bfloat162float(raw[(t * 3 + 2) * GDN_D + cc]);
-            }
+          float wv[3] = {hist[2 * GDN_D + cc], hist[5 * GDN_D + cc], hist[8 * GDN_D + cc]};
+          float hv[3] = {0.f, 0.f, 0.f};
+          for (int tb = 0; tb < lb; tb += GDNC_SUB) {
+            float sq[GDNC_SUB];
+            conv_block16(x + SV * GDN_D + cc, XS * GDN_D, cq, wv, tb, len, hv, sq);
           }
-          x[(t * XS + SV) * GDN_D + cc] = vv;
-        }
-        if (FUSED) {
           float* gp = args.conv_pool + (size_t)meta[s].slot * CONV_KEEP * CONV_DIM + 2 * KEY_DIM + h * GDN_D + cc;
-          gp[0] = e0; gp[CONV_DIM] = e1; gp[2 * CONV_DIM] = e2;
+          gp[0] = hv[0]; gp[CONV_DIM] = hv[1]; gp[2 * CONV_DIM] = hv[2];
+        }
+        if (!FUSED) {  // the isolated kernel's v: widened from bf16
+          for (int t = 0; t < lb; ++t)
+            x[(t * XS + SV) * GDN_D + cc] = t < len ? __bfloat162float(raw[(t * 3 + 2) * GDN_D + cc]) : 0.f;
         }
       }
       mbar_arrive(cdone);  // the prologue may build this item's tables
