@@ -156,3 +156,32 @@ def test_score_messages_matches_complete_message_reference(golden, weights_seed0
             assert d < P_TOL, d
     finally:
         scorer.close()
+
+
+@pytest.mark.parametrize("state_dtype", ["float16", "float32"])
+def test_engine_32_token_ticks_vs_oracle(weights_seed0, state_dtype):
+    """Ticks in the 32-token bucket (ragged 17..32-token rows: the chunked delta rule and the tensor-core window
+    attention with conv history carried across partial sub-chunks), then 3- and 1-token ticks, against the CPU oracle
+    of the reference's streaming engine."""
+    from hs_guard_b200 import DEFAULT
+    from hs_guard_b200.engine import SlotEngine
+    from oracle.stream import StreamOracle
+    r = np.random.default_rng(11)
+    ids = lambda n: [int(x) for x in r.integers(0, 248320, n)]
+    ticks = [[(0, ids(20)), (1, ids(31))], [(1, ids(17)), (0, ids(32))], [(0, ids(3)), (1, ids(25))],
+             [(1, ids(1)), (0, ids(1))]]
+    eng = SlotEngine(weights_seed0, 2, state_dtype=state_dtype)
+    orc = StreamOracle(weights_seed0, DEFAULT, 2)
+    try:
+        worst = 0.0
+        for tick in ticks:
+            got, want = eng.step(tick), orc.step(tick)
+            for role in ("user", "assistant"):
+                for g_, w_ in zip(got[role], want[role]):
+                    worst = max(worst, float(np.abs(g_ - w_).max()))
+        print(f"max |dp| {worst:.3g}")
+        assert worst < P_TOL, worst
+        np.testing.assert_array_equal(eng.length, orc.length)
+        np.testing.assert_array_equal(eng.pools()["ring_pos"][:2].cpu().numpy(), orc.ring_pos[:2].numpy())
+    finally:
+        eng.close()
