@@ -371,7 +371,10 @@ gdn_chunk_kernel(const __grid_constant__ GdntMaps maps, const GdnArgs args) {
         {
           const int g = lane >> 2, t4 = lane & 3;
           const int va = w10 ? 2 : 0;  // A operand rows: q (warp 10) or k (warp 11)
+          // three independent accumulator chains per 8-token tile (hi.hi, hi.lo, lo.hi), summed at the end
           float d[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+          float dx[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+          float dy[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
 #pragma unroll
           for (int kt = 0; kt < 8; ++kt) {
             const int ko = (16 * kt + 2 * t4) * 2;
@@ -390,15 +393,57 @@ gdn_chunk_kernel(const __grid_constant__ GdntMaps maps, const GdnArgs args) {
               const uint32_t bh0 = ld_u32(br), bh1 = ld_u32(br + 16);
               const uint32_t bl0 = ld_u32(br + GDN_D * 2), bl1 = ld_u32(br + GDN_D * 2 + 16);
               mma_f16_16816(d[nt], a[0][0], a[0][1], a[0][2], a[0][3], bh0, bh1);
-              mma_f16_16816(d[nt], a[0][0], a[0][1], a[0][2], a[0][3], bl0, bl1);
-              mma_f16_16816(d[nt], a[1][0], a[1][1], a[1][2], a[1][3], bh0, bh1);
+              mma_f16_16816(dx[nt], a[0][0], a[0][1], a[0][2], a[0][3], bl0, bl1);
+              mma_f16_16816(dy[nt], a[1][0], a[1][1], a[1][2], a[1][3], bh0, bh1);
             }
           }
+#pragma unroll
+          for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) d[nt][e] += dx[nt][e] + dy[nt][e];
           // D: rows t = g, g + 8; cols s = 8 nt + 2 t4 + e
           const float* gamv = vec;
           const float* bev = vec + 1 * GDNC_SUB;
           const float* rkv = vec + 3 * GDNC_SUB;
           const float* rqv = vec + 4 * GDNC_SUB;
+          // K~^T[k][s] = e^(gam_C - gam_s) rk_s k_s[k] as hi/lo for the tokens s of one half (warp 10: 0-7, warp 11:
+          // 8-15); the exponent is <= 0, so strong decay underflows to 0, never 0/0. Lane owns k = 4 lane .. 4 lane + 3.
+          // The 4-byte column (s pair) of row k is stored XOR-ed with (k >> 3) & 7, which spreads a warp's stores over
+          // 16 banks (rows are 48 bytes apart) and keeps the consumers' fragment loads conflict-free.
+          auto kt_half = [&](int half) {
+            const float gC = gamv[GDNC_SUB - 1];
+            uint8_t* ktb = sb + GDNC_OFF_KT;
+            const int f = (lane >> 1) & 7;
+#pragma unroll
+            for (int s2 = 0; s2 < GDNC_SUB / 2; s2 += 2) {
+              const int s = 8 * half + s2;
+              const float f0 = expf(gC - gamv[s]) * rkv[s], f1 = expf(gC - gamv[s + 1]) * rkv[s + 1];
+              float4 ka, kb;
+              if (FUSED) {
+                ka = reinterpret_cast<const float4*>(x + ((t0 + s) * XS + 1) * GDN_D)[lane];
+                kb = reinterpret_cast<const float4*>(x + ((t0 + s + 1) * XS + 1) * GDN_D)[lane];
+              } else {
+                auto rawk = [&](int t) {
+                  if (t >= len) return make_float4(0.f, 0.f, 0.f, 0.f);
+                  const __nv_bfloat162* r2 = reinterpret_cast<const __nv_bfloat162*>(raw + (t * 3 + 1) * GDN_D) + 2 * lane;
+                  const float2 u0 = __bfloat1622float2(r2[0]), u1 = __bfloat1622float2(r2[1]);
+                  return make_float4(u0.x, u0.y, u1.x, u1.y);
+                };
+                ka = rawk(t0 + s);
+                kb = rawk(t0 + s + 1);
+              }
+              const float kav[4] = {ka.x, ka.y, ka.z, ka.w}, kbv[4] = {kb.x, kb.y, kb.z, kb.w};
+              const int col = ((s >> 1) ^ f) * 4;
+#pragma unroll
+              for (int c = 0; c < 4; ++c) {
+                uint32_t hi, lo;
+                split_half2x(kav[c] * f0, kbv[c] * f1, hi, lo);
+                const int k = 4 * lane + c;
+                *reinterpret_cast<uint32_t*>(ktb + k * GDNC_KT_ROW + col) = hi;
+                *reinterpret_cast<uint32_t*>(ktb + (GDN_D + k) * GDNC_KT_ROW + col) = lo;
+              }
+            }
+          };
           if (w10) {  // Mqk[t][s] = rq_t rk_s e^(gam_t - gam_s) q.k for s <= t, as hi/lo
             uint8_t* mq = sb + GDNC_OFF_MQ;
 #pragma unroll
@@ -418,37 +463,7 @@ gdn_chunk_kernel(const __grid_constant__ GdntMaps maps, const GdnArgs args) {
                 *reinterpret_cast<uint32_t*>(mq + off) = hi;
                 *reinterpret_cast<uint32_t*>(mq + GDNC_SUB * GDNC_T_ROW + off) = lo;
               }
-            // K~^T[k][s] = e^(gam_C - gam_s) rk_s k_s[k] as hi/lo (the exponent is <= 0: strong decay underflows to
-            // 0, never 0/0); lane owns k = 4 lane .. 4 lane + 3
-            const float gC = gamv[GDNC_SUB - 1];
-            uint8_t* ktb = sb + GDNC_OFF_KT;
-#pragma unroll
-            for (int s2 = 0; s2 < GDNC_SUB; s2 += 2) {
-              const float f0 = expf(gC - gamv[s2]) * rkv[s2], f1 = expf(gC - gamv[s2 + 1]) * rkv[s2 + 1];
-              float4 ka, kb;
-              if (FUSED) {
-                ka = reinterpret_cast<const float4*>(x + ((t0 + s2) * XS + 1) * GDN_D)[lane];
-                kb = reinterpret_cast<const float4*>(x + ((t0 + s2 + 1) * XS + 1) * GDN_D)[lane];
-              } else {
-                auto rawk = [&](int t) {
-                  if (t >= len) return make_float4(0.f, 0.f, 0.f, 0.f);
-                  const __nv_bfloat162* r2 = reinterpret_cast<const __nv_bfloat162*>(raw + (t * 3 + 1) * GDN_D) + 2 * lane;
-                  const float2 u0 = __bfloat1622float2(r2[0]), u1 = __bfloat1622float2(r2[1]);
-                  return make_float4(u0.x, u0.y, u1.x, u1.y);
-                };
-                ka = rawk(t0 + s2);
-                kb = rawk(t0 + s2 + 1);
-              }
-              const float kav[4] = {ka.x, ka.y, ka.z, ka.w}, kbv[4] = {kb.x, kb.y, kb.z, kb.w};
-#pragma unroll
-              for (int c = 0; c < 4; ++c) {
-                uint32_t hi, lo;
-                split_half2x(kav[c] * f0, kbv[c] * f1, hi, lo);
-                const int k = 4 * lane + c;
-                *reinterpret_cast<uint32_t*>(ktb + k * GDNC_KT_ROW + s2 * 2) = hi;
-                *reinterpret_cast<uint32_t*>(ktb + (GDN_D + k) * GDNC_KT_ROW + s2 * 2) = lo;
-              }
-            }
+            kt_half(0);
           } else {  // A[t][s] = beta_t rk_t rk_s e^(gam_t - gam_s) k.k for s < t; T = (I + A)^-1
             float* am = reinterpret_cast<float*>(sb + GDNC_OFF_TM);
 #pragma unroll
@@ -484,6 +499,7 @@ gdn_chunk_kernel(const __grid_constant__ GdntMaps maps, const GdnArgs args) {
                 tm[(GDNC_SUB * GDNC_T_ROW + t * GDNC_T_ROW) / 2 + lane] = __float2half_rn(tc[t] - __half2float(hi));
               }
             }
+            kt_half(1);
           }
         }
         mbar_arrive(&sfull[jsub & 1]);
@@ -704,9 +720,11 @@ gdn_chunk_kernel(const __grid_constant__ GdntMaps maps, const GdnArgs args) {
           const uint8_t* ktb = sb + GDNC_OFF_KT;
 #pragma unroll
           for (int j = 0; j < 16; ++j) {
-            const uint8_t* kh = ktb + (8 * j + g) * GDNC_KT_ROW + 4 * t4;
+            // row 8 j + g, s pairs t4 and t4 + 4, columns XOR-ed with (row >> 3) & 7 = j & 7
+            const uint8_t* kh = ktb + (8 * j + g) * GDNC_KT_ROW;
             const uint8_t* kl = kh + GDN_D * GDNC_KT_ROW;
-            const uint32_t bh0 = ld_u32(kh), bh1 = ld_u32(kh + 16), bl0 = ld_u32(kl), bl1 = ld_u32(kl + 16);
+            const int c0 = (t4 ^ (j & 7)) * 4, c1 = ((t4 + 4) ^ (j & 7)) * 4;
+            const uint32_t bh0 = ld_u32(kh + c0), bh1 = ld_u32(kh + c1), bl0 = ld_u32(kl + c0), bl1 = ld_u32(kl + c1);
             float* dd = &sv[j >> 1][4 * (j & 1)];
             mma_f16_16816_r(dd[0], dd[1], dd[2], dd[3], uh[0], uh[1], uh[2], uh[3], bh0, bh1);
             mma_f16_16816_r(dd[0], dd[1], dd[2], dd[3], uh[0], uh[1], uh[2], uh[3], bl0, bl1);
