@@ -59,10 +59,9 @@ __host__ __device__ inline int gdnc_stage_bytes(int lb, bool fused) {
 __host__ __device__ inline int gdnc_fixed_bytes() {
   return 2 * GDNC_SCRATCH + GDNC_ITEM + GDN_MAX_STAGES * (16 + 3 * 8) + 2 * 2 * 8 + 8 + 1024;
 }
-__host__ __device__ inline int gdnc_stages(int lb, bool fused) {
-  int s = (GDN_SMEM_LIMIT - gdnc_fixed_bytes()) / gdnc_stage_bytes(lb, fused);
-  return s > GDN_MAX_STAGES ? GDN_MAX_STAGES : (s < 1 ? 1 : s);
-}
+// One stage: the per-item arrays (partial sums, gates) and the team conv keep exactly one item in flight (a 64-token
+// item's stage is 133 KB, so a second would not fit beside the scratch anyway).
+__host__ __device__ inline int gdnc_stages(int, bool) { return 1; }
 __host__ __device__ inline int gdnc_smem_bytes(int lb, bool fused) {
   return gdnc_stages(lb, fused) * gdnc_stage_bytes(lb, fused) + gdnc_fixed_bytes();
 }
@@ -179,13 +178,63 @@ gdn_chunk_kernel(const __grid_constant__ GdntMaps maps, const GdnArgs args) {
       mbar_init(&sfull[b], 64);
       mbar_init(&sdone[b], GDNT_CONS);
     }
-    mbar_init(cdone, GDNT_CONS);
+    mbar_init(cdone, FUSED ? GDNT_THREADS : GDNT_CONS);
     fence_barrier_init();
     prefetch_tmap(&maps.state);
     prefetch_tmap(&maps.in0);
     if (FUSED) prefetch_tmap(&maps.in1);
   }
   __syncthreads();
+
+  // FUSED: the causal conv of an item is shared by all twelve warps, one channel a thread: thread t owns channel
+  // t & 127 of part t >> 7 (q, k, v) and runs conv + SiLU over the item's tokens in place, writes the per-token
+  // partial sums of the squared q / k outputs (one per warp) and the new conv history; v threads with channel c < lb
+  // also compute token c's gates. Every thread then arrives on cdone. Callers have passed pdl_wait (gates read proj).
+  const int cpart = tid >> 7, cch = tid & (GDN_D - 1);
+  float4 cw = make_float4(0.f, 0.f, 0.f, 0.f);
+  if (FUSED) cw = (reinterpret_cast<const float4*>(args.conv_w) + h * GDN_D)[cpart * KEY_DIM + cch];
+  const float negA = -expf(args.A_log[h]), dtb = args.dt_bias[h];
+  auto team_conv = [&](int s, int n, int len) {
+    float* x = x_of(s);
+    const float* hist = tail_of(s);
+    float w[3] = {hist[(0 * 3 + cpart) * GDN_D + cch], hist[(1 * 3 + cpart) * GDN_D + cch],
+                  hist[(2 * 3 + cpart) * GDN_D + cch]};
+    float hh[3] = {0.f, 0.f, 0.f};
+    for (int tb = 0; tb < lb; tb += GDNC_SUB) {
+      float sq[GDNC_SUB];
+      conv_block16(x + cpart * GDN_D + cch, XS * GDN_D, cw, w, tb, len, hh, sq);
+      if (cpart < 2) {  // warp-uniform
+        const float tot = reduce16(sq, lane);
+        if (!(lane & 1)) ipart[((tb + reduce16_index(lane)) * 4 + (warp & 3)) * 2 + cpart] = tot;
+      }
+    }
+    float* gp = args.conv_pool + (size_t)meta[s].slot * CONV_KEEP * CONV_DIM + cpart * KEY_DIM + h * GDN_D + cch;
+    gp[0] = hh[0];
+    gp[CONV_DIM] = hh[1];
+    gp[2 * CONV_DIM] = hh[2];
+    if (cpart == 2 && cch < lb) {  // gates of token cch: log decay -exp(A_log) softplus(a + dt_bias), beta
+      float gl = 0.f, be = 0.f;
+      if (cch < len) {
+        const size_t rt = (size_t)n * lb + cch;
+        const float xg = args.proj[rt * GDN_IN + GDN_A_OFF + h] + dtb;
+        gl = negA * (xg > 20.f ? xg : log1pf(expf(xg)));
+        be = sigmoidf_(args.proj[rt * GDN_IN + GDN_B_OFF + h]);
+      }
+      igl[cch] = gl;
+      ibe[cch] = be;
+    }
+  };
+  // FUSED roles other than the consumers: wait for item i's stage, take part in its conv
+  auto join_conv = [&](int i) {
+    const int s = i % S;
+    if (!mbar_wait(&full[s], (i / S) & 1, args.err, ERR_TIMEOUT_TMA)) return false;
+    const int len = meta[s].len;
+    if (len > 0) {
+      team_conv(s, row_of(i), len);
+      mbar_arrive(cdone);
+    }
+    return true;
+  };
 
   if (warp == GDNT_PROD_WARP) {
     // ===================================== producer =====================================
@@ -238,14 +287,17 @@ gdn_chunk_kernel(const __grid_constant__ GdntMaps maps, const GdnArgs args) {
     }
     pdl_wait();
     for (int i = 0; i < pre; ++i) issue_inputs(i);
-    for (int i = pre; i < n_items; ++i) {
-      if (!mbar_wait(&empty[i % S], ((i / S) - 1) & 1, args.err, ERR_TIMEOUT_TMA)) break;
-      issue_state(i, nxt_len, nxt_slot);
-      if (i + 1 < n_items) {
-        nxt_len = args.lens[row_of(i + 1)];
-        nxt_slot = args.slots[row_of(i + 1)];
+    for (int i = 0; i < n_items; ++i) {
+      if (i >= pre) {
+        if (!mbar_wait(&empty[i % S], ((i / S) - 1) & 1, args.err, ERR_TIMEOUT_TMA)) break;
+        issue_state(i, nxt_len, nxt_slot);
+        if (i + 1 < n_items) {
+          nxt_len = args.lens[row_of(i + 1)];
+          nxt_slot = args.slots[row_of(i + 1)];
+        }
+        issue_inputs(i);
       }
-      issue_inputs(i);
+      if (FUSED && !join_conv(i)) break;
     }
     return;
   }
@@ -255,6 +307,7 @@ gdn_chunk_kernel(const __grid_constant__ GdntMaps maps, const GdnArgs args) {
     pdl_wait();  // the outputs may still be read by an earlier kernel
     for (int i = 0; i < n_items; ++i) {
       const int s = i % S, n = row_of(i);
+      if (FUSED && !join_conv(i)) break;
       if (!mbar_wait(&done[s], (i / S) & 1, args.err, ERR_TIMEOUT_TMA)) break;
       const int len = meta[s].len;
       if (len == 0) {  // a padding row: zero outputs (the consumers write the outputs of real rows)
@@ -291,10 +344,11 @@ gdn_chunk_kernel(const __grid_constant__ GdntMaps maps, const GdnArgs args) {
     // barrier 2.
     const bool w10 = warp == GDNT_QK_WARP;
     const float scale = 0.08838834764831845f;  // 128^-1/2, correctly rounded
+    if (FUSED) pdl_wait();  // the conv history written below may still be read by an earlier kernel
     int jsub = 0, item_seq = 0;
     for (int i = 0; i < n_items; ++i) {
       const int s = i % S;
-      bool ok = mbar_wait(&full[s], (i / S) & 1, args.err, ERR_TIMEOUT_TMA);
+      bool ok = FUSED ? join_conv(i) : mbar_wait(&full[s], (i / S) & 1, args.err, ERR_TIMEOUT_TMA);
       const int len = ok ? meta[s].len : 1;
       if (ok && len > 0) ok = mbar_wait(cdone, item_seq & 1, args.err, ERR_TIMEOUT_TMA);
       if (!named_sync_and_id<2, 64>(ok)) return;
@@ -514,20 +568,10 @@ gdn_chunk_kernel(const __grid_constant__ GdntMaps maps, const GdnArgs args) {
   const int frag_c = 2 * (warp & 3) + ((lane >> 3) & 1);
   const int v0 = 16 * warp + g;  // this lane's state columns: v0 (fragment rows g) and v0 + 8
   const float gw0 = FUSED ? args.gnorm_w[v0] : 0.f, gw1 = FUSED ? args.gnorm_w[v0 + 8] : 0.f;
-  // the conv: thread c < 128 owns q and k channel c, thread 128 + c owns v channel c and (c < lb) token c's gates
+  // the isolated kernel's widening: thread c < 128 owns q and k channel c, thread 128 + c owns v channel c and
+  // (c < lb) token c's gates
   const bool qk_thread = tid < GDN_D;
   const int cc = tid & (GDN_D - 1);
-  float4 cq = make_float4(0.f, 0.f, 0.f, 0.f), ck = cq;
-  if (FUSED) {
-    const float4* w4 = reinterpret_cast<const float4*>(args.conv_w) + h * GDN_D;
-    if (qk_thread) {
-      cq = w4[cc];
-      ck = w4[KEY_DIM + cc];
-    } else {
-      cq = w4[2 * KEY_DIM + cc];
-    }
-  }
-  const float negA = -expf(args.A_log[h]), dtb = args.dt_bias[h];
   pdl_wait();  // z comes from the preceding GEMM's output; the outputs may still be read by an earlier kernel
   if (tid == 0) pdl_trigger();
   int jsub = 0;
@@ -540,22 +584,9 @@ gdn_chunk_kernel(const __grid_constant__ GdntMaps maps, const GdnArgs args) {
       float* x = x_of(s);
       const float* hist = tail_of(s);
       const __nv_bfloat16* raw = reinterpret_cast<const __nv_bfloat16*>(tail_of(s));
-      // ---- conv + SiLU (or widening) of all tokens, in place; per-token norm partial sums; gates ----
-      if (qk_thread && FUSED) {
-        float wq[3] = {hist[0 * GDN_D + cc], hist[3 * GDN_D + cc], hist[6 * GDN_D + cc]};
-        float wk[3] = {hist[1 * GDN_D + cc], hist[4 * GDN_D + cc], hist[7 * GDN_D + cc]};
-        float hq[3] = {0.f, 0.f, 0.f}, hk[3] = {0.f, 0.f, 0.f};
-        for (int tb = 0; tb < lb; tb += GDNC_SUB) {
-          float psq[GDNC_SUB], psk[GDNC_SUB];
-          conv_block16(x + 0 * GDN_D + cc, XS * GDN_D, cq, wq, tb, len, hq, psq);
-          conv_block16(x + 1 * GDN_D + cc, XS * GDN_D, ck, wk, tb, len, hk, psk);
-          const float tq = reduce16(psq, lane), tk = reduce16(psk, lane);
-          if (!(lane & 1))
-            *reinterpret_cast<float2*>(ipart + ((tb + reduce16_index(lane)) * 4 + warp) * 2) = make_float2(tq, tk);
-        }
-        float* gp = args.conv_pool + (size_t)meta[s].slot * CONV_KEEP * CONV_DIM + h * GDN_D + cc;
-        gp[0] = hq[0]; gp[CONV_DIM] = hq[1]; gp[2 * CONV_DIM] = hq[2];
-        gp[KEY_DIM] = hk[0]; gp[CONV_DIM + KEY_DIM] = hk[1]; gp[2 * CONV_DIM + KEY_DIM] = hk[2];
+      // ---- conv + SiLU (FUSED, shared with the other warps) or widening of all tokens; partial sums; gates ----
+      if (FUSED) {
+        team_conv(s, n, len);
       } else if (qk_thread) {  // the isolated kernel's q, k: widened from bf16
         for (int tb = 0; tb < lb; tb += GDNC_SUB) {
           float psq[GDNC_SUB], psk[GDNC_SUB];
@@ -576,29 +607,15 @@ gdn_chunk_kernel(const __grid_constant__ GdntMaps maps, const GdnArgs args) {
           float gl = 0.f, be = 0.f;
           if (cc < len) {
             const size_t rt = (size_t)n * lb + cc;
-            const float a = FUSED ? args.proj[rt * GDN_IN + GDN_A_OFF + h] : args.a_raw[rt * GDN_H + h];
-            const float b = FUSED ? args.proj[rt * GDN_IN + GDN_B_OFF + h] : args.b_raw[rt * GDN_H + h];
-            const float xg = a + dtb;
+            const float xg = args.a_raw[rt * GDN_H + h] + dtb;
             gl = negA * (xg > 20.f ? xg : log1pf(expf(xg)));
-            be = sigmoidf_(b);
+            be = sigmoidf_(args.b_raw[rt * GDN_H + h]);
           }
           igl[cc] = gl;
           ibe[cc] = be;
         }
-        if (FUSED) {
-          float wv[3] = {hist[2 * GDN_D + cc], hist[5 * GDN_D + cc], hist[8 * GDN_D + cc]};
-          float hv[3] = {0.f, 0.f, 0.f};
-          for (int tb = 0; tb < lb; tb += GDNC_SUB) {
-            float sq[GDNC_SUB];
-            conv_block16(x + SV * GDN_D + cc, XS * GDN_D, cq, wv, tb, len, hv, sq);
-          }
-          float* gp = args.conv_pool + (size_t)meta[s].slot * CONV_KEEP * CONV_DIM + 2 * KEY_DIM + h * GDN_D + cc;
-          gp[0] = hv[0]; gp[CONV_DIM] = hv[1]; gp[2 * CONV_DIM] = hv[2];
-        }
-        if (!FUSED) {  // the isolated kernel's v: widened from bf16
-          for (int t = 0; t < lb; ++t)
-            x[(t * XS + SV) * GDN_D + cc] = t < len ? __bfloat162float(raw[(t * 3 + 2) * GDN_D + cc]) : 0.f;
-        }
+        for (int t = 0; t < lb; ++t)  // the isolated kernel's v: widened from bf16
+          x[(t * XS + SV) * GDN_D + cc] = t < len ? __bfloat162float(raw[(t * 3 + 2) * GDN_D + cc]) : 0.f;
       }
       mbar_arrive(cdone);  // the prologue may build this item's tables
       const uint32_t half_base = smem_u32(stage_ptr(s)) + (warp >> 2) * GDNT_HALF;
