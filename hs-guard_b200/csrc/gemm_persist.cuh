@@ -1,0 +1,222 @@
+// Persistent weight-streaming GEMM for long-running grids (many 128 x tn tiles, e.g. 64-token ticks of 352 rows):
+// the contract, operand layout and epilogue modes of gemm_tc_kernel, but one CTA per SM loops over tiles with the
+// accumulator double-buffered in TMEM, so that draining tile i (TMEM -> registers -> shared -> TMA store, in
+// 32-token chunks) overlaps the loads and MMAs of tile i + 1, and the load ring runs on across tiles.
+//
+// Roles in a 192-thread CTA: warp 0 lane 0 issues the TMA loads (a STAGES-deep ring of [A | B_hi | B_lo] stages
+// shared by all of the CTA's tiles); warp 1 owns TMEM and its lane 0 issues tcgen05.mma, committing each stage back to
+// the producer and each finished accumulator to the epilogue; warps 2-5 are the epilogue, warp w reading accumulator
+// lanes 32 (w % 4) .. + 31 (= weight rows), and hand each accumulator back once drained. Tiles are numbered weight
+// tile fastest, then token block, then K split, so the CTAs that run at the same time share activation blocks in L2.
+// Every wait is bounded and reports through `err`.
+#pragma once
+#include "gemm.cuh"
+
+namespace hsg {
+
+constexpr int GPC_THREADS = 192;
+constexpr int GPC_CHUNK = 32;  // tokens per epilogue chunk (one TMA store)
+
+struct GemmPcArgs {
+  int tiles_w, tb, splits, kps, k_blocks_total;
+  int tn;       // tokens per tile: 128 or 256
+  int m;        // valid tokens (chunks wholly beyond are not stored)
+  int use_lo, stages, mode;
+  int* err;
+};
+
+__host__ __device__ inline int gpc_chunk_bytes(int mode) {
+  return mode == GEMM_SILU_MUL ? 2 * GPC_CHUNK * 64 * 2 : GPC_CHUNK * 128 * 4;
+}
+__host__ __device__ inline int gpc_smem(int tn, int use_lo, int stages, int mode) {
+  return stages * gemm_stage_bytes(tn, use_lo) + 2 * gpc_chunk_bytes(mode) + (2 * stages + 5) * 8 + 16 + 1024;
+}
+
+__device__ __forceinline__ void bulk_wait_read_1() { asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory"); }
+
+// Output maps: STORE / ATOMIC: tm_o0 = fp32 Y [tokens][N] with a [128 x 32] box; SILU_MUL: tm_o0 / tm_o1 = bf16
+// act_hi / act_lo [tokens][N/2] with [64 x 32] boxes.
+__global__ void __launch_bounds__(GPC_THREADS, 1)
+gemm_pc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_xhi,
+               const __grid_constant__ CUtensorMap tm_xlo, const __grid_constant__ CUtensorMap tm_o0,
+               const __grid_constant__ CUtensorMap tm_o1, const GemmPcArgs args) {
+  extern __shared__ __align__(1024) uint8_t gpc_smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(gpc_smem_raw) + 1023) & ~uintptr_t(1023));
+  const int S = args.stages, tn = args.tn;
+  const int stage_bytes = gemm_stage_bytes(tn, args.use_lo);
+  const int chunk_bytes = gpc_chunk_bytes(args.mode);
+  uint8_t* outbuf = smem + S * stage_bytes;                                   // [2] epilogue chunks
+  uint64_t* full = reinterpret_cast<uint64_t*>(outbuf + 2 * chunk_bytes);
+  uint64_t* empty = full + S;
+  uint64_t* acc_full = empty + S;   // [2] MMA -> epilogue
+  uint64_t* acc_empty = acc_full + 2;  // [2] epilogue -> MMA
+  uint64_t* mma_done = acc_empty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
+  int* progress = reinterpret_cast<int*>(tmem_slot + 1);  // [0] loads issued, [1] stages consumed by the MMA
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int total = args.tiles_w * args.tb * args.splits;
+  uint32_t ncols = 32;
+  while (ncols < (uint32_t)(2 * tn)) ncols <<= 1;
+  auto decode = [&](int j, int& wrow0, int& tok0, int& kb0, int& nk) {
+    const int wt = j % args.tiles_w, r = j / args.tiles_w;
+    wrow0 = wt * 128;
+    tok0 = (r % args.tb) * tn;
+    kb0 = (r / args.tb) * args.kps;
+    nk = min(args.kps, args.k_blocks_total - kb0);
+  };
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], 128);
+    }
+    mbar_init(mma_done, 1);
+    progress[0] = progress[1] = 0;
+    fence_barrier_init();
+    prefetch_tmap(&tm_w);
+    prefetch_tmap(&tm_xhi);
+    if (args.use_lo) prefetch_tmap(&tm_xlo);
+    prefetch_tmap(&tm_o0);
+    if (args.mode == GEMM_SILU_MUL) prefetch_tmap(&tm_o1);
+  }
+  if (warp == 1) tmem_alloc(tmem_slot, ncols);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  pdl_wait();  // activations come from the previous kernel; the outputs may still be read by it
+  if (threadIdx.x == 0) pdl_trigger();
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---- TMA producer: one ring of stages across all of this CTA's tiles ----
+      int cnt = 0;
+      bool ok = true;
+      for (int j = blockIdx.x; j < total && ok; j += gridDim.x) {
+        int wrow0, tok0, kb0, nk;
+        decode(j, wrow0, tok0, kb0, nk);
+        for (int i = 0; i < nk; ++i, ++cnt) {
+          const int s = cnt % S, r = cnt / S;
+          if (r > 0 && !mbar_wait(&empty[s], (r - 1) & 1, args.err, ERR_TIMEOUT_MMA)) { ok = false; break; }
+          uint8_t* a = smem + s * stage_bytes;
+          uint8_t* bh = a + GEMM_A_BYTES;
+          uint8_t* bl = bh + tn * GEMM_BK * 2;
+          const int kx = (kb0 + i) * GEMM_BK;
+          mbar_arrive_expect_tx(&full[s], stage_bytes);
+          tma_load_2d(a, &tm_w, kx, wrow0, &full[s]);
+          tma_load_2d(bh, &tm_xhi, kx, tok0, &full[s]);
+          if (args.use_lo) tma_load_2d(bl, &tm_xlo, kx, tok0, &full[s]);
+          progress[0] = cnt + 1;
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ---- MMA issuer ----
+      const uint32_t idesc = idesc_bf16(128, tn);
+      int cnt = 0, lt = 0;
+      bool ok = true;
+      for (int j = blockIdx.x; j < total && ok; j += gridDim.x, ++lt) {
+        int wrow0, tok0, kb0, nk;
+        decode(j, wrow0, tok0, kb0, nk);
+        const int buf = lt & 1;
+        if (lt >= 2 && !mbar_wait(&acc_empty[buf], ((lt >> 1) - 1) & 1, args.err, ERR_TIMEOUT_MMA)) break;
+        tc_fence_after();
+        const uint32_t d = tmem + (uint32_t)(buf * tn);
+        for (int i = 0; i < nk; ++i, ++cnt) {
+          const int s = cnt % S, r = cnt / S;
+          if (!mbar_wait(&full[s], r & 1, args.err, ERR_TIMEOUT_TMA)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t a = smem_u32(smem + s * stage_bytes);
+          const uint32_t bh = a + GEMM_A_BYTES;
+          const uint32_t bl = bh + tn * GEMM_BK * 2;
+#pragma unroll
+          for (int kk = 0; kk < GEMM_BK / 16; ++kk) {
+            const uint64_t da = sw128_desc(a + kk * 32);
+            mma_bf16(d, da, sw128_desc(bh + kk * 32), idesc, (i > 0 || kk > 0) ? 1u : 0u);
+            if (args.use_lo) mma_bf16(d, da, sw128_desc(bl + kk * 32), idesc, 1u);
+          }
+          mma_commit(&empty[s]);
+          progress[1] = cnt + 1;
+        }
+        if (ok) mma_commit(&acc_full[buf]);
+      }
+      mma_commit(mma_done);  // arrives once every MMA issued above has completed
+    }
+  } else {
+    // ---- epilogue: per tile, 32-token chunks TMEM -> shared -> one TMA store each, two chunk buffers ----
+    const int quad = warp & 3;
+    const int row = quad * 32 + lane;  // accumulator lane == weight row within the tile
+    const uint32_t lane_base = tmem + ((uint32_t)(quad * 32) << 16);
+    const bool issuer = warp == 2 && lane == 0;
+    int lt = 0, seq = 0;
+    for (int j = blockIdx.x; j < total; j += gridDim.x, ++lt) {
+      int wrow0, tok0, kb0, nk;
+      decode(j, wrow0, tok0, kb0, nk);
+      const int buf = lt & 1;
+      if (!named_sync_and_id<3, 128>(mbar_wait(&acc_full[buf], (lt >> 1) & 1, args.err, ERR_TIMEOUT_MMA))) break;
+      tc_fence_after();
+      for (int c = 0; c < tn; c += GPC_CHUNK, ++seq) {
+        uint8_t* cb = outbuf + (seq & 1) * chunk_bytes;
+        if (issuer) bulk_wait_read_1();  // the store issued from this buffer two chunks ago has read it
+        named_sync_id<3, 128>();
+        float v[32];
+        tmem_ld32(lane_base + (uint32_t)(buf * tn + c), v);
+        if (args.mode == GEMM_SILU_MUL) {
+          // rows (2f, 2f+1) hold (gate, up) of feature f: the even lane keeps even tokens, the odd lane odd ones
+          __nv_bfloat16* sh = reinterpret_cast<__nv_bfloat16*>(cb);  // [32][64]
+          __nv_bfloat16* sl = sh + GPC_CHUNK * 64;
+          const int f = row >> 1, odd = lane & 1;
+#pragma unroll
+          for (int t = 0; t < 32; t += 2) {
+            const float other = __shfl_xor_sync(0xffffffffu, odd ? v[t] : v[t + 1], 1);
+            const float gate = odd ? other : v[t];
+            const float up = odd ? v[t + 1] : other;
+            const int tok = t + odd;
+            split_bf16(silu_fast(gate) * up, sh[tok * 64 + f], sl[tok * 64 + f]);
+          }
+        } else {
+          float* tile = reinterpret_cast<float*>(cb);  // [32][128]
+#pragma unroll
+          for (int t = 0; t < 32; ++t) tile[t * 128 + row] = v[t];
+        }
+        fence_proxy_async();
+        named_sync_id<3, 128>();
+        if (issuer) {
+          if (tok0 + c < args.m) {
+            if (args.mode == GEMM_SILU_MUL) {
+              tma_store_2d(&tm_o0, cb, wrow0 / 2, tok0 + c);
+              tma_store_2d(&tm_o1, cb + GPC_CHUNK * 64 * 2, wrow0 / 2, tok0 + c);
+            } else if (args.mode == GEMM_STORE) {
+              tma_store_2d(&tm_o0, cb, wrow0, tok0 + c);
+            } else {
+              tma_reduce_add_2d(&tm_o0, cb, wrow0, tok0 + c);
+            }
+          }
+          bulk_commit();
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&acc_empty[buf]);  // this accumulator may be overwritten by the tile after next
+    }
+    if (issuer) bulk_wait_read_all();  // the shared-memory sources of the last stores have been read
+  }
+
+  // ---- teardown: every MMA done, every issued load landed (error paths), then release TMEM ----
+  if (threadIdx.x == 32) mbar_wait(mma_done, 0, args.err, ERR_TIMEOUT_MMA);
+  tc_fence_before();
+  __syncthreads();
+  if (threadIdx.x == 0)
+    for (int i = progress[1]; i < progress[0]; ++i) mbar_wait(&full[i % S], (i / S) & 1, args.err, ERR_TIMEOUT_TMA);
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, ncols);
+  }
+}
+
+}  // namespace hsg

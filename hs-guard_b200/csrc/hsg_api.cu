@@ -17,6 +17,7 @@
 #include "gdn_tc.cuh"
 #include "gdn_chunk.cuh"
 #include "gemm.cuh"
+#include "gemm_persist.cuh"
 #include "norm.cuh"
 #include "ring_decode.cuh"
 #include "ring_prefill.cuh"
@@ -118,6 +119,7 @@ static int make_map(CUtensorMap* map, const void* base, int rows, int k, int box
 // ---- GEMM planning ----------------------------------------------------------------------------------------------
 struct GemmPlan {
   int tb, tn, splits, kps, stages, smem;
+  int persist;  // 1: gemm_pc_kernel (persistent, double-buffered accumulator), one CTA per SM
 };
 
 static constexpr int SM_COUNT = 148;
@@ -140,7 +142,7 @@ static long gemm_cost(int tiles, int KB, int tb, int tn, int splits, int kps, in
 
 static GemmPlan plan_gemm(int n_w, int K, int M, int mode, int use_lo) {
   const int tiles = n_w / 128, KB = K / 64;
-  GemmPlan best{0, 0, 0, 0, 0, 0};
+  GemmPlan best{0, 0, 0, 0, 0, 0, 0};
   long best_cost = -1;
   const int max_tb = (M + 15) / 16;
   for (int tb = 1; tb <= max_tb; ++tb) {
@@ -154,7 +156,7 @@ static GemmPlan plan_gemm(int n_w, int K, int M, int mode, int use_lo) {
       const long cost = gemm_cost(tiles, KB, tb, tn, splits, kps, mode, use_lo);
       if (best_cost < 0 || cost < best_cost) {
         best_cost = cost;
-        best = {tb, tn, splits, kps, 0, 0};
+        best = {tb, tn, splits, kps, 0, 0, 0};
       }
     }
   }
@@ -163,14 +165,19 @@ static GemmPlan plan_gemm(int n_w, int K, int M, int mode, int use_lo) {
   best.stages = std::min(stages, std::max(2, best.kps));
   const int tb_full = (M + 255) / 256;
   if ((long)tiles * tb_full >= 4L * SM_COUNT) {
-    // A long-running grid (many waves of full tiles): 128-token tiles with two stages (97 KB of shared memory, 128
-    // TMEM columns) so that two CTAs share each SM and one's epilogue and pipeline fill overlap the other's MMAs.
-    // Measured at 22,528 tokens against 256-token tiles with one CTA per SM: 8-10 % faster for K = 1024.
+    // A long-running grid (many waves of full tiles): the persistent kernel, one CTA per SM looping over 128-token
+    // tiles with the accumulator double-buffered in TMEM (each tile's epilogue overlaps the next tile's MMAs) and
+    // as many load stages as fit beside the two epilogue chunk buffers.
+    best.persist = 1;
     best.tn = 128;
     best.tb = (M + 127) / 128;
     best.splits = 1;
     best.kps = KB;
-    best.stages = 2;
+    int st = 6;
+    while (st > 2 && gpc_smem(best.tn, use_lo, st, mode) > SMEM_MAX) --st;
+    best.stages = st;
+    best.smem = gpc_smem(best.tn, use_lo, st, mode);
+    return best;
   }
   best.smem = gemm_smem(best.tn, use_lo, best.stages);
   return best;
@@ -203,7 +210,7 @@ static int launch_gemm(cudaStream_t st, const void* w, int n_w, int K, const voi
                        bool pdl = false) {
   const int use_lo = xlo != nullptr;
   GemmPlan p = plan_gemm(n_w, K, M, mode, use_lo);
-  if (force_splits > 0 && mode == GEMM_ATOMIC) {
+  if (force_splits > 0 && mode == GEMM_ATOMIC && !p.persist) {
     const int KB = K / 64;
     p.kps = (KB + force_splits - 1) / force_splits;
     p.splits = (KB + p.kps - 1) / p.kps;
@@ -213,18 +220,39 @@ static int launch_gemm(cudaStream_t st, const void* w, int n_w, int K, const voi
   if ((rc = make_map(&tw, w, n_w, K, 128)) != HSG_OK) return rc;
   if ((rc = make_map(&th, xhi, m_alloc, K, p.tn)) != HSG_OK) return rc;
   if ((rc = make_map(&tl, use_lo ? xlo : xhi, m_alloc, K, p.tn)) != HSG_OK) return rc;
+  const int out_rows = p.persist ? GPC_CHUNK : p.tn;  // the persistent kernel stores 32-token chunks
   if (mode == GEMM_SILU_MUL) {
-    if ((rc = make_map_2d(&t0, ahi, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, M, n_w / 2, (uint64_t)ld_act * 2, 64, p.tn,
-                          CU_TENSOR_MAP_SWIZZLE_NONE)) != HSG_OK)
+    if ((rc = make_map_2d(&t0, ahi, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, M, n_w / 2, (uint64_t)ld_act * 2, 64,
+                          out_rows, CU_TENSOR_MAP_SWIZZLE_NONE)) != HSG_OK)
       return rc;
-    if ((rc = make_map_2d(&t1, alo, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, M, n_w / 2, (uint64_t)ld_act * 2, 64, p.tn,
-                          CU_TENSOR_MAP_SWIZZLE_NONE)) != HSG_OK)
+    if ((rc = make_map_2d(&t1, alo, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, M, n_w / 2, (uint64_t)ld_act * 2, 64,
+                          out_rows, CU_TENSOR_MAP_SWIZZLE_NONE)) != HSG_OK)
       return rc;
   } else {
-    if ((rc = make_map_2d(&t0, y, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, M, n_w, (uint64_t)ldy * 4, 128, p.tn,
+    if ((rc = make_map_2d(&t0, y, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, M, n_w, (uint64_t)ldy * 4, 128, out_rows,
                           CU_TENSOR_MAP_SWIZZLE_NONE)) != HSG_OK)
       return rc;
     t1 = t0;
+  }
+  if (p.persist) {
+    GemmPcArgs a;
+    a.tiles_w = n_w / 128;
+    a.tb = p.tb;
+    a.splits = 1;
+    a.kps = K / 64;
+    a.k_blocks_total = K / 64;
+    a.tn = p.tn;
+    a.m = M;
+    a.use_lo = use_lo;
+    a.stages = p.stages;
+    a.mode = mode;
+    a.err = err;
+    const int total = a.tiles_w * a.tb;
+    if (prof) prof_mark(prof, prof_cls);
+    CU(launch_k(gemm_pc_kernel, dim3(std::min(total, SM_COUNT)), dim3(GPC_THREADS), p.smem, st, pdl, tw, th, tl, t0,
+                t1, a));
+    if (prof) prof_mark(prof, -1);
+    return HSG_OK;
   }
   GemmArgs a;
   a.k_blocks_per_split = p.kps;
@@ -256,6 +284,7 @@ static int make_decode_map(CUtensorMap* map, const void* base, uint64_t rows) {
 
 static int set_kernel_attributes() {
   CU(cudaFuncSetAttribute(gemm_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_MAX));
+  CU(cudaFuncSetAttribute(gemm_pc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_MAX));
   CU(cudaFuncSetAttribute(gdn_step_kernel<true, float>, cudaFuncAttributeMaxDynamicSharedMemorySize, GDN_SMEM_LIMIT));
   CU(cudaFuncSetAttribute(gdn_step_kernel<false, float>, cudaFuncAttributeMaxDynamicSharedMemorySize, GDN_SMEM_LIMIT));
   CU(cudaFuncSetAttribute(gdn_step_kernel<true, __half>, cudaFuncAttributeMaxDynamicSharedMemorySize, GDN_SMEM_LIMIT));
