@@ -532,7 +532,7 @@ def run_c5(args):
                     "h2d_bytes_per_step": (S * LB + 3 * S) * 8, "d2h_bytes_per_step": 2 * S * LB * 3 * 4 + 4},
             "gpu_launches": launches * K,
             "clocks": clk.summary(),
-            "roofline": {"kernel": "gemm_tc_kernel (all projections of one tick)", "bound": "tensor",
+            "roofline": {"kernel": "gemm_pc_kernel + gemm_tc_kernel (all projections of one tick)", "bound": "tensor",
                          "achieved": achieved, "peak": tflops_peak, "unit": "TFLOP/s", "frac": achieved / tflops_peak,
                          "peak_source": tsrc, "traffic": None, "algorithmic_flops": gemm_flops,
                          "tick_ms": gemm_ms, "launches": gemm_n},
