@@ -60,16 +60,14 @@ static PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
 
 static int get_encoder() {
   static std::once_flag once;
-  static int status = 0;
   std::call_once(once, [] {
     void* fn = nullptr;
     cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) != cudaSuccess ||
-        q != cudaDriverEntryPointSuccess || !fn)
-      status = fail(HSG_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
-    g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess && fn)
+      g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
   });
-  return g_encode ? HSG_OK : HSG_ERR_CUDA;
+  return g_encode ? HSG_OK : fail(HSG_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
 }
 
 // 2-D row-major tensor map: `rows` x `cols` elements of `dtype`, rows `row_bytes` apart, box `box_cols` x `box_rows`.
