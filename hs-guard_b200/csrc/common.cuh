@@ -92,21 +92,25 @@ __device__ __forceinline__ uint64_t global_ns() {
 
 constexpr uint64_t WAIT_LIMIT_NS = 2000000000ull;  // 2 s: far above any legitimate wait in these kernels
 
-// Bounded wait on an mbarrier phase. Gives up after WAIT_LIMIT_NS of wall time (recording `code` in *err), or at
-// once when another CTA has already recorded a timeout (the pipeline is broken; waiting longer only delays the
-// error). Returns false when it gave up; the caller skips the dependent work.
+// Bounded wait on an mbarrier phase. Gives up after WAIT_LIMIT_NS of wall time (recording `code` in *err), or soon
+// after another CTA has recorded a timeout (the pipeline is broken; waiting longer only delays the error). Returns
+// false when it gave up; the caller skips the dependent work. The two slow checks (a global load of the error word,
+// the clock) run every 64th poll only: polled each time, the load's latency sat between consecutive try_waits and
+// delayed every wait that did not succeed at once by up to a global-memory round trip.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err, int code) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = global_ns();
-  while (true) {
+  for (uint32_t it = 1;; ++it) {
     if (mbar_try_wait(bar, parity)) return true;
-    if (err) {
-      const int e = *reinterpret_cast<volatile int*>(err);
-      if (e == ERR_TIMEOUT_TMA || e == ERR_TIMEOUT_MMA) return false;
-    }
-    if (global_ns() - t0 > WAIT_LIMIT_NS) {
-      set_error(err, code);
-      return false;
+    if ((it & 63) == 0) {
+      if (err) {
+        const int e = *reinterpret_cast<volatile int*>(err);
+        if (e == ERR_TIMEOUT_TMA || e == ERR_TIMEOUT_MMA) return false;
+      }
+      if (global_ns() - t0 > WAIT_LIMIT_NS) {
+        set_error(err, code);
+        return false;
+      }
     }
   }
 }
