@@ -118,15 +118,37 @@ ring_prefill_kernel(const __grid_constant__ CUtensorMap tm_rk, const __grid_cons
   if (warp < nact) {
     // ---- this warp's 16 query rows -> fp16, swizzled like the K tiles (rows beyond M are zero) ----
     uint8_t* qw = qsm + warp * PF_QWARP;
-    for (int e = lane; e < 16 * 32; e += 32) {  // (row, 8-dim chunk)
-      const int r = e >> 5, ch = e & 31, row = rb0 + 16 * warp + r;
-      uint4 v = make_uint4(0u, 0u, 0u, 0u);
-      if (row < M) {
-        const float4* src = reinterpret_cast<const float4*>(args.qbuf + (head * M + row) * ATT_D + ch * 8);
-        const float4 a = src[0], b = src[1];
-        v = make_uint4(pack_half2(a.x, a.y), pack_half2(a.z, a.w), pack_half2(b.x, b.y), pack_half2(b.z, b.w));
+    const int ch = lane;  // this lane's 8-dim chunk of each row
+    for (int r0 = 0; r0 < 16; r0 += 4) {  // four rows' loads in flight before any conversion
+      float4 a[4], b[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int row = rb0 + 16 * warp + r0 + u;
+        a[u] = b[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (row < M) {
+          const float4* src = reinterpret_cast<const float4*>(args.qbuf + (head * M + row) * ATT_D + ch * 8);
+          a[u] = src[0];
+          b[u] = src[1];
+        }
       }
-      *reinterpret_cast<uint4*>(qw + (ch >> 3) * PF_QBOX + sw128_off(r, ch & 7)) = v;
+#pragma unroll
+      for (int u = 0; u < 4; ++u)
+        *reinterpret_cast<uint4*>(qw + (ch >> 3) * PF_QBOX + sw128_off(r0 + u, ch & 7)) =
+            make_uint4(pack_half2(a[u].x, a[u].y), pack_half2(a[u].z, a[u].w), pack_half2(b[u].x, b[u].y),
+                       pack_half2(b[u].z, b[u].w));
+    }
+    if (!args.out_raw) {
+      // the output gates of these rows into L2 now (read in the epilogue): 16 rows x 1 KB, four lines a lane
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int e = lane * 4 + u, r = e >> 3, row = rb0 + 16 * warp + r;
+        if (row < M) {
+          const int grp = row / lb, tok = row % lb;
+          const float* gp = args.proj + ((size_t)n * lb + tok) * ATT_IN + (h * ATT_G + grp) * 2 * ATT_D + ATT_D +
+                            (e & 7) * 32;
+          asm volatile("prefetch.global.L2 [%0];" ::"l"(gp));
+        }
+      }
     }
   }
   __syncthreads();
@@ -287,18 +309,27 @@ ring_prefill_kernel(const __grid_constant__ CUtensorMap tm_rk, const __grid_cons
     const float* gate = args.proj + ((size_t)n * lb + tok) * ATT_IN + jq * 2 * ATT_D + ATT_D + 2 * c4;
     const bool live = inv != 0.f;
 #pragma unroll
-    for (int d = 0; d < 32; ++d) {
-      float y0 = 0.f, y1 = 0.f;
-      if (live) {
-        const float2 gt = *reinterpret_cast<const float2*>(gate + 8 * d);
-        y0 = o[d][2 * hr] * inv * __fdividef(1.0f, 1.0f + __expf(-gt.x));
-        y1 = o[d][2 * hr + 1] * inv * __fdividef(1.0f, 1.0f + __expf(-gt.y));
+    for (int d0 = 0; d0 < 32; d0 += 8) {
+      // eight gate pairs loaded before this batch's stores (a store may alias a later load as far as the compiler
+      // knows, which would otherwise serialise one memory round trip per pair)
+      float2 gt[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u)
+        gt[u] = live ? *reinterpret_cast<const float2*>(gate + 8 * (d0 + u)) : make_float2(0.f, 0.f);
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int d = d0 + u;
+        float y0 = 0.f, y1 = 0.f;
+        if (live) {
+          y0 = o[d][2 * hr] * inv * __fdividef(1.0f, 1.0f + __expf(-gt[u].x));
+          y1 = o[d][2 * hr + 1] * inv * __fdividef(1.0f, 1.0f + __expf(-gt[u].y));
+        }
+        __nv_bfloat16 h0, h1, lo0, lo1;
+        split_bf16(y0, h0, lo0);
+        split_bf16(y1, h1, lo1);
+        *reinterpret_cast<__nv_bfloat162*>(args.out_hi + ob + 8 * d) = __halves2bfloat162(h0, h1);
+        *reinterpret_cast<__nv_bfloat162*>(args.out_lo + ob + 8 * d) = __halves2bfloat162(lo0, lo1);
       }
-      __nv_bfloat16 h0, h1, lo0, lo1;
-      split_bf16(y0, h0, lo0);
-      split_bf16(y1, h1, lo1);
-      *reinterpret_cast<__nv_bfloat162*>(args.out_hi + ob + 8 * d) = __halves2bfloat162(h0, h1);
-      *reinterpret_cast<__nv_bfloat162*>(args.out_lo + ob + 8 * d) = __halves2bfloat162(lo0, lo1);
     }
   }
 }
