@@ -390,6 +390,13 @@ __device__ __forceinline__ void split_bf16(float x, __nv_bfloat16& hi, __nv_bflo
   hi = __float2bfloat16_rn(x);
   lo = __float2bfloat16_rn(x - __bfloat162float(hi));
 }
+// The same for two values with paired conversions (two instructions instead of four): hi = (hi(a), hi(b)),
+// lo = (lo(a), lo(b)); identical results to split_bf16 on each.
+__device__ __forceinline__ void split_bf16x2(float a, float b, __nv_bfloat162& hi, __nv_bfloat162& lo) {
+  hi = __floats2bfloat162_rn(a, b);
+  const float2 h = __bfloat1622float2(hi);
+  lo = __floats2bfloat162_rn(a - h.x, b - h.y);
+}
 
 // Sum over a thread block of `nthreads` (multiple of 32) using `scratch` (>= nthreads/32 floats).
 __device__ __forceinline__ float block_sum(float v, float* scratch, int nthreads) {

@@ -163,13 +163,26 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__
         float v[32];
         tmem_ld32(lane_base + c, v);
 #pragma unroll
-        for (int j = 0; j < 32; j += 2) {
-          // even lane sends v[j+1] (gate of token j+1), odd lane sends v[j] (up of token j)
-          const float other = __shfl_xor_sync(0xffffffffu, odd ? v[j] : v[j + 1], 1);
-          const float gate = odd ? other : v[j];
-          const float up = odd ? v[j + 1] : other;
-          const int tok = c + j + odd;
-          if (tok < tn) split_bf16(silu_fast(gate) * up, sh[tok * 64 + f], sl[tok * 64 + f]);
+        for (int j0 = 0; j0 < 32; j0 += 4) {  // two tokens of this lane per paired hi/lo conversion
+          float y[2];
+#pragma unroll
+          for (int q = 0; q < 2; ++q) {
+            const int j = j0 + 2 * q;
+            // even lane sends v[j+1] (gate of token j+1), odd lane sends v[j] (up of token j)
+            const float other = __shfl_xor_sync(0xffffffffu, odd ? v[j] : v[j + 1], 1);
+            const float gate = odd ? other : v[j];
+            const float up = odd ? v[j + 1] : other;
+            y[q] = silu_fast(gate) * up;
+          }
+          __nv_bfloat162 h2, l2;
+          split_bf16x2(y[0], y[1], h2, l2);
+          const int tok = c + j0 + odd;  // tn is a multiple of 16, so tok < tn implies tok + 2 < tn
+          if (tok < tn) {
+            sh[tok * 64 + f] = h2.x;
+            sl[tok * 64 + f] = l2.x;
+            sh[(tok + 2) * 64 + f] = h2.y;
+            sl[(tok + 2) * 64 + f] = l2.y;
+          }
         }
       }
     } else {

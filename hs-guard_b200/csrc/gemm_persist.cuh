@@ -173,12 +173,23 @@ gemm_pc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__
           __nv_bfloat16* sl = sh + GPC_CHUNK * 64;
           const int f = row >> 1, odd = lane & 1;
 #pragma unroll
-          for (int t = 0; t < 32; t += 2) {
-            const float other = __shfl_xor_sync(0xffffffffu, odd ? v[t] : v[t + 1], 1);
-            const float gate = odd ? other : v[t];
-            const float up = odd ? v[t + 1] : other;
+          for (int t = 0; t < 32; t += 4) {  // two tokens of this lane per paired hi/lo conversion
+            float y[2];
+#pragma unroll
+            for (int q = 0; q < 2; ++q) {
+              const int j = t + 2 * q;
+              const float other = __shfl_xor_sync(0xffffffffu, odd ? v[j] : v[j + 1], 1);
+              const float gate = odd ? other : v[j];
+              const float up = odd ? v[j + 1] : other;
+              y[q] = silu_fast(gate) * up;
+            }
+            __nv_bfloat162 h2, l2;
+            split_bf16x2(y[0], y[1], h2, l2);
             const int tok = t + odd;
-            split_bf16(silu_fast(gate) * up, sh[tok * 64 + f], sl[tok * 64 + f]);
+            sh[tok * 64 + f] = h2.x;
+            sl[tok * 64 + f] = l2.x;
+            sh[(tok + 2) * 64 + f] = h2.y;
+            sl[(tok + 2) * 64 + f] = l2.y;
           }
         } else {
           float* tile = reinterpret_cast<float*>(cb);  // [32][128]
