@@ -417,12 +417,31 @@ __global__ void __launch_bounds__(256) ring_append_kernel(const AttnArgs args) {
   const int64_t slot = args.slots[n], start = args.starts[n];
   if (len <= 0 || slot < 0 || slot > args.max_slots) return;
   const size_t head = (size_t)n * ATT_HKV + kvh;
-  for (int t = 0; t < len; ++t) {
-    const size_t col = (size_t)((start + t) % WIN);
-    const size_t dst = (((size_t)slot * ATT_HKV + kvh) * RING_COLS + col) * ATT_D + threadIdx.x;
-    const size_t src = (head * args.lb + t) * ATT_D + threadIdx.x;
-    args.ring_k[dst] = args.knew[src];
-    args.ring_v[dst] = args.vnew[src];
+  // thread = (16-byte chunk c of a 256-dim row, token t0 + 8 i): every load is issued before any store (a store
+  // could alias a later load as far as the compiler knows, which would serialise one round trip per token)
+  static_assert(MAX_LB <= 64 && ATT_D * 2 / 16 == 32, "eight tokens of 32 chunks per pass, at most 64 tokens");
+  const int c = threadIdx.x & 31, t0 = threadIdx.x >> 5;
+  const uint4* nk = reinterpret_cast<const uint4*>(args.knew) + head * args.lb * 32;
+  const uint4* nv = reinterpret_cast<const uint4*>(args.vnew) + head * args.lb * 32;
+  uint4 kr[8], vr[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int t = t0 + 8 * i;
+    if (t < len) {
+      kr[i] = nk[t * 32 + c];
+      vr[i] = nv[t * 32 + c];
+    }
+  }
+  uint4* rk = reinterpret_cast<uint4*>(args.ring_k) + ((size_t)slot * ATT_HKV + kvh) * RING_COLS * 32;
+  uint4* rv = reinterpret_cast<uint4*>(args.ring_v) + ((size_t)slot * ATT_HKV + kvh) * RING_COLS * 32;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int t = t0 + 8 * i;
+    if (t < len) {
+      const size_t col = (size_t)((start + t) % WIN);
+      rk[col * 32 + c] = kr[i];
+      rv[col * 32 + c] = vr[i];
+    }
   }
 }
 
