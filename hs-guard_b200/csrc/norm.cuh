@@ -54,13 +54,12 @@ __global__ void __launch_bounds__(NORM_THREADS) resid_norm_kernel(const float* h
   const int m = blockIdx.x, d = threadIdx.x * 4;
   float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
   if (m < m_valid) x = *reinterpret_cast<const float4*>(hidden + (size_t)m * HIDDEN + d);
+  const float4 w = *reinterpret_cast<const float4*>(w1 + d);  // requested before the reduction's barriers
   const float ss = block_sum(x.x * x.x + x.y * x.y + x.z * x.z + x.w * x.w, scratch, NORM_THREADS);
-  const float r = 1.0f / sqrtf(ss * (1.0f / HIDDEN) + eps);
-  const float4 w = *reinterpret_cast<const float4*>(w1 + d);
-  const float y[4] = {x.x * r * w.x, x.y * r * w.y, x.z * r * w.z, x.w * r * w.w};
-  __nv_bfloat16 hi[4], lo[4];
-#pragma unroll
-  for (int j = 0; j < 4; ++j) split_bf16(m < m_valid ? y[j] : 0.f, hi[j], lo[j]);
+  const float r = m < m_valid ? 1.0f / sqrtf(ss * (1.0f / HIDDEN) + eps) : 0.f;
+  __nv_bfloat162 hi[2], lo[2];
+  split_bf16x2(x.x * r * w.x, x.y * r * w.y, hi[0], lo[0]);
+  split_bf16x2(x.z * r * w.z, x.w * r * w.w, hi[1], lo[1]);
   *reinterpret_cast<uint2*>(x_hi + (size_t)m * HIDDEN + d) = *reinterpret_cast<uint2*>(hi);
   *reinterpret_cast<uint2*>(x_lo + (size_t)m * HIDDEN + d) = *reinterpret_cast<uint2*>(lo);
 }
