@@ -36,6 +36,7 @@ constexpr int RD_PSTRIDE = RD_MAXK + 8;          // fp16 probabilities row strid
 
 struct alignas(16) RdMeta {
   int64_t qpos;
+  int64_t slot;
   int len, ntile;
   int tile[RD_MAXT];      // ring tile index, or -1 for the new-key tile
   int kpos[RD_MAXK];      // key position per listed tile column (-1: not visible)
@@ -131,6 +132,7 @@ ring_decode_kernel(const __grid_constant__ CUtensorMap tm_rk, const __grid_const
       __syncwarp();  // every lane's metadata writes are ordered before lane 0's releasing arrive
       if (lane == 0) {
         m.qpos = start;
+        m.slot = slot;
         m.len = len;
         m.ntile = nt;
         mbar_arrive(&meta_full[b]);
@@ -188,6 +190,14 @@ ring_decode_kernel(const __grid_constant__ CUtensorMap tm_rk, const __grid_const
       continue;
     }
     // the output gates of this lane's (row, dim) outputs, loaded now so the latency hides behind both passes
+    // this item's new key / value pair for the ring write at its end, loaded now (a load issued after the output
+    // stores could not be moved ahead of them and would add a memory round trip to every item)
+    __half2 nk2 = __floats2half2_rn(0.f, 0.f), nv2 = nk2;
+    if (args.write_ring && tid < ATT_D / 2) {
+      const size_t src = ((size_t)n * ATT_HKV + h) * ATT_D + 2 * tid;
+      nk2 = *reinterpret_cast<const __half2*>(args.knew + src);
+      nv2 = *reinterpret_cast<const __half2*>(args.vnew + src);
+    }
     float gate[2][2][2] = {};
     if (!args.out_raw && c4 < 2) {
 #pragma unroll
@@ -313,12 +323,10 @@ ring_decode_kernel(const __grid_constant__ CUtensorMap tm_rk, const __grid_const
     }
     if (args.write_ring && tid < ATT_D / 2) {
       // the new key/value go into ring column start % 512 (every copy of this item has landed)
-      const int64_t slot = args.slots[n];
       const size_t col = (size_t)(qpos % WIN);
-      const size_t dst = (((size_t)slot * ATT_HKV + h) * RING_COLS + col) * ATT_D + 2 * tid;
-      const size_t src = ((size_t)n * ATT_HKV + h) * ATT_D + 2 * tid;
-      *reinterpret_cast<__half2*>(args.ring_k + dst) = *reinterpret_cast<const __half2*>(args.knew + src);
-      *reinterpret_cast<__half2*>(args.ring_v + dst) = *reinterpret_cast<const __half2*>(args.vnew + src);
+      const size_t dst = (((size_t)m.slot * ATT_HKV + h) * RING_COLS + col) * ATT_D + 2 * tid;
+      *reinterpret_cast<__half2*>(args.ring_k + dst) = nk2;
+      *reinterpret_cast<__half2*>(args.ring_v + dst) = nv2;
     }
     mbar_arrive(&meta_free[b]);
     named_sync<RD_CONS>();  // scores and probabilities are reused by the next item
