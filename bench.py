@@ -33,7 +33,7 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 METRIC = "scored tokens/s/GPU at 352 slots; p50/P95 single-token step latency (ms)"
-PUBLISHED_TOKENS_PER_S = 15075.6   # reference, 1x L20, 352 streams
+PUBLISHED_TOKENS_PER_S = 15075.6   # the reference's published minimum throughput, 1x L20, 352 streams
 CONTEXTS = (512, 2048, 8000)
 
 

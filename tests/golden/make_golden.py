@@ -1,8 +1,8 @@
 """Generate the golden vectors in tests/golden/golden.npz by running the REFERENCE implementation on the CPU.
 
-Run once in a container that has the reference checkout (path in $HSG_REFERENCE, default /root/reference):
+Run once in a container that has the reference checkout (its root directory in $HSG_REFERENCE):
 
-    python tests/golden/make_golden.py
+    HSG_REFERENCE=<reference checkout> python tests/golden/make_golden.py
 
 What it runs (all fp32 on bf16-valued random-init weights from hs_guard_b200.weights, seed 0):
 - ``pack_inputs`` from the reference (src/hs_guard/engine/slot_engine_v7.py:7-25) on fixed cases;
@@ -28,7 +28,9 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 REPO = os.path.dirname(os.path.dirname(HERE))
 sys.path.insert(0, REPO)
 sys.path.insert(0, HERE)
-REF = os.environ.get("HSG_REFERENCE", "/root/reference")
+REF = os.environ.get("HSG_REFERENCE")
+if not REF:
+    raise SystemExit("set HSG_REFERENCE to the root of the reference checkout")
 sys.path.insert(0, os.path.join(REF, "src"))
 
 from golden_inputs import (STREAM_MAX_SLOTS, gdn_inputs, ring_inputs, sample_index, stream_script)  # noqa: E402

@@ -1,7 +1,7 @@
 """Golden vectors for the decision rules, produced by the reference demo's own functions.
 
-Run in a container that has the reference checkout (read-only) at $HSG_REFERENCE (default /root/reference):
-    python tests/golden/make_rules_golden.py
+Run in a container that has the reference checkout (read-only), its root directory in $HSG_REFERENCE:
+    HSG_REFERENCE=<reference checkout> python tests/golden/make_rules_golden.py
 It imports examples/demo/server.py and records, for seeded logits sequences and a grid of rules, the reference's
 first_fire index and its RuleTracker state (fired_k, best_k, best) after every token, into rules_golden.json.
 """
@@ -38,7 +38,9 @@ def sequences():
 
 
 def main():
-    ref = os.environ.get("HSG_REFERENCE", "/root/reference")
+    ref = os.environ.get("HSG_REFERENCE")
+    if not ref:
+        raise SystemExit("set HSG_REFERENCE to the root of the reference checkout")
     sys.path.insert(0, os.path.join(ref, "examples", "demo"))
     sys.path.insert(0, os.path.join(ref, "src"))
     import server
