@@ -8,7 +8,7 @@ N > 1); each rank owns its own 352 slots and full weight replica, no collective 
 
 Reported (rank 0, one JSON line):
 - value: scored tokens/s of the whole job with the packed ticks already resident in HBM (graph replays timed with
-  CUDA events, max over ranks); the per-tick working set (~17 GB) exceeds the 126 MB L2, so no flush is needed.
+  CUDA events, max over ranks); the per-tick working set (~10.8 GB) exceeds the 126 MB L2, so no flush is needed.
 - e2e: the same metric through the public API (StreamingGuard.step with host lists: validation, packing, host->device
   copy, replay, device->host copy of the probabilities, 1 - p(safe)); latency_ms p50/P95 are of these steps.
 - roofline: the dominant kernel (gated-delta-rule step) timed live with CUDA events in an eager tick.
@@ -356,7 +356,7 @@ def run_ours(args):
             "config": {"workload": "C4: full-model streaming, 352 slots per GPU prefilled with 512/2048/8000 "
                                    "random tokens (1/3 each, seed 4), then single-token role=assistant steps",
                        "slots_per_gpu": S, "contexts": list(lens), "parallelism": f"slot-sharded x{world}",
-                       "l2": "no flush: each tick touches ~17 GB (> 126 MB L2)", "prefill_s": round(prefill_s, 2)},
+                       "l2": "no flush: each tick touches ~10.8 GB (> 126 MB L2)", "prefill_s": round(prefill_s, 2)},
             "latency_ms": {"p50": p50, "p95": p95, "device_per_step": dev_ms},
             "e2e": {"value": S * world / (e2e_ms * 1e-3), "unit": "tokens/s", "h2d_bytes_per_step": (S + 3 * S) * 8,
                     "d2h_bytes_per_step": 2 * S * 3 * 4 + 4},
