@@ -188,6 +188,28 @@ class SlotEngine:
             raise ValueError("a session may appear once per tick")
         return self.run_arrays([c for _, c in requests], slots)
 
+    def run_tokens(self, slots, ids):
+        """One tick of one token per row (``slots`` and ``ids`` as lists, already validated): the packed layout of
+        pack_inputs with lb = 1, filled without per-row lists. Returns ([roles, n, 1, 3] numpy copy, lens)."""
+        n = len(slots)
+        nb = bucket(n, self.session_buckets)
+        hin, hin_np, hout, out_np = self._buffers(nb, 1)
+        sl = np.asarray(slots, dtype=np.int64)
+        hin_np[:nb] = 0
+        hin_np[:n] = ids
+        tail = hin_np[nb:4 * nb].reshape(3, nb)
+        tail[0].fill(0)
+        tail[0, :n] = 1
+        tail[1].fill(self.max_slots)
+        tail[1, :n] = sl
+        tail[2].fill(0)
+        tail[2, :n] = self.length[sl]
+        check(self._lib.hsg_step(self.handle, ptr(hin), nb, 1, ptr(hout)))
+        self.stats["graph_replays"] += 1
+        self.stats["ticks"] += 1
+        self.length[sl] += 1
+        return out_np[:, :n].copy(), np.ones(n, dtype=np.int64)
+
     def fits_one_tick(self, requests):
         """Whether ``requests`` run as a single tick (<= largest row bucket, every request <= 64 tokens)."""
         largest = TOKEN_BUCKETS[-1]

@@ -6,7 +6,7 @@ behind it is the B200 slot engine (hs_guard_b200.engine.SlotEngine -> libhsg.so)
 """
 from __future__ import annotations
 
-from .config import ROLES, SESSION_BUCKETS
+from .config import ROLES, SESSION_BUCKETS, TOKEN_BUCKETS
 from .engine import SlotEngine
 
 # Red-line thresholds of the released model's metadata (reference docs/ENGINE.md:14); used when a caller has
@@ -30,6 +30,35 @@ def validate_requests(requests, role, max_slots, vocab_size):
         for i in ids:
             if not isinstance(i, int) or not 0 <= i < vocab_size:
                 raise ValueError("Each request requires nonempty in-vocabulary integer token IDs")
+
+
+def validate_collect(requests, role, max_slots, vocab_size):
+    """validate_requests (the same checks in the same order, the same errors) in one pass that also returns
+    (slots, the single id of every request or None when some request has more than one, longest request)."""
+    if role not in ROLES:
+        raise ValueError("role must be user or assistant")
+    slots = [s for s, _ in requests]
+    if not requests or len(set(slots)) != len(slots):
+        raise ValueError("Each tick requires nonempty requests and unique slots")
+    singles = []
+    longest = 0
+    for slot, ids in requests:
+        if not isinstance(slot, int) or not 0 <= slot < max_slots:
+            raise ValueError("Slot is outside the allocated range")
+        if not ids:
+            raise ValueError("Each request requires nonempty in-vocabulary integer token IDs")
+        for i in ids:
+            if not isinstance(i, int) or not 0 <= i < vocab_size:
+                raise ValueError("Each request requires nonempty in-vocabulary integer token IDs")
+        n = len(ids)
+        if n > longest:
+            longest = n
+        if singles is not None:
+            if n == 1:
+                singles.append(ids[0])
+            else:
+                singles = None
+    return slots, singles, longest
 
 
 class StreamingGuard:
@@ -56,15 +85,18 @@ class StreamingGuard:
         self.engine.reset()
 
     def step(self, requests, role="assistant"):
-        validate_requests(requests, role, self.max_slots, self.vocab_size)
+        slots, singles, longest = validate_collect(requests, role, self.max_slots, self.vocab_size)
         tau = self.metadata["thresholds"][role]
         eng = self.engine
-        if eng.fits_one_tick(requests):  # one tick: cut scores for all rows at once
-            probs, lens = eng.tick(requests)
+        if len(slots) <= eng.session_buckets[-1] and longest <= TOKEN_BUCKETS[-1]:
+            # one tick: cut scores for all rows at once
+            if singles is not None:
+                probs, lens = eng.run_tokens(slots, singles)
+            else:
+                probs, lens = eng.tick(requests)
             cut = 1 - probs[eng.roles.index(role), :, :, 0]  # [n, lb] float32, as the reference's 1 - p[:, 0]
             if cut.shape[1] == 1:
-                return [{"slot": s, "cut_scores": [c], "threshold": tau}
-                        for (s, _), c in zip(requests, cut[:, 0].tolist())]
+                return [{"slot": s, "cut_scores": [c], "threshold": tau} for s, c in zip(slots, cut[:, 0].tolist())]
             return [{"slot": s, "cut_scores": row[:n], "threshold": tau}
                     for (s, _), row, n in zip(requests, cut.tolist(), lens.tolist())]
         outputs = eng.step(requests)[role]

@@ -61,6 +61,57 @@ def test_validation_matches_reference():
             validate_requests(req, role, 2, 100)
 
 
+def test_validate_collect_matches_validate_requests():
+    """The one-pass validation raises exactly what validate_requests raises and returns the tick's columns."""
+    from hs_guard_b200.runtime import validate_collect
+    assert validate_collect([(0, [5]), (2, [7])], "user", 3, 100) == ([0, 2], [5, 7], 1)
+    assert validate_collect([(0, [5]), (2, [7, 8])], "user", 3, 100) == ([0, 2], None, 2)
+    cases = [([], "user"), ([(0, [1])], "system"), ([(0, [1]), (0, [2])], "user"), ([(3, [1])], "user"),
+             ([(0, [])], "user"), ([(0, [100])], "user"), ([(0, [-1])], "user"), ([(0, [1.0])], "user"),
+             ([(0.5, [1])], "user"), ([(0, [1]), (5, [1]), (1, [])], "user"), ([(0, [200]), (7, [1])], "user"),
+             ([(0, [np.int64(1)])], "user")]
+    for req, role in cases:
+        want = got = None
+        try:
+            validate_requests(req, role, 3, 100)
+        except ValueError as e:
+            want = str(e)
+        try:
+            validate_collect(req, role, 3, 100)
+        except ValueError as e:
+            got = str(e)
+        assert want is not None and got == want, (req, got, want)
+
+
+def test_run_tokens_packs_like_pack_inputs():
+    """SlotEngine.run_tokens (one token per row, no per-row lists) fills the same tick buffer as pack_inputs."""
+    from hs_guard_b200 import engine as E
+    seen = {}
+
+    class FakeLib:
+        def hsg_step(self, handle, hin, nb, lb, hout):
+            seen["buf"] = np.ctypeslib.as_array(ctypes.cast(hin, ctypes.POINTER(ctypes.c_int64)),
+                                                shape=(nb * lb + 3 * nb,)).copy()
+            return 0
+
+    eng = E.SlotEngine.__new__(E.SlotEngine)
+    eng.max_slots, eng.roles = 40, ("user", "assistant")
+    eng.session_buckets = E.default_session_buckets(40)
+    eng.length = np.arange(40, dtype=np.int64) * 3
+    eng.host, eng.stats, eng._lib, eng._h = {}, {"graph_replays": 0, "ticks": 0}, FakeLib(), 1
+    slots, ids = [7, 0, 31, 12, 5], [11, 22, 33, 44, 55]
+    nb = bucket(len(slots), eng.session_buckets)
+    hin = torch.full((4 * nb,), -7, dtype=torch.int64)  # pageable stand-ins for the engine's pinned buffers
+    hout = torch.zeros(2, nb, 1, 3)
+    eng.host[(nb, 1)] = (hin, hin.numpy(), hout, hout.numpy())
+    length_before = eng.length.copy()
+    eng.run_tokens(slots, ids)
+    want = np.full(nb + 3 * nb, -1, dtype=np.int64)
+    pack_inputs([[i] for i in ids], np.array(slots), nb, 1, length_before, 40, want)
+    np.testing.assert_array_equal(seen["buf"], want)
+    np.testing.assert_array_equal(eng.length - length_before, np.isin(np.arange(40), slots).astype(np.int64))
+
+
 def test_config_and_parameter_count():
     assert DEFAULT.check() is DEFAULT
     assert sum(int(np.prod(s)) for _, s, _ in W.parameter_specs()) == 754_519_918
@@ -161,6 +212,7 @@ def _fake_engine(max_slots):
         eng.length[np.asarray(slots)] += lens
         return probs, lens
     eng.run_arrays = run_arrays
+    eng.run_tokens = lambda slots, ids: run_arrays([[i] for i in ids], slots)
     return eng
 
 
