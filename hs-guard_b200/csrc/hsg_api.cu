@@ -21,6 +21,7 @@
 #include "norm.cuh"
 #include "ring_decode.cuh"
 #include "ring_prefill.cuh"
+#include "ring_prefill_tc.cuh"
 
 using namespace hsg;
 
@@ -302,6 +303,7 @@ static int set_kernel_attributes() {
   CU(cudaFuncSetAttribute(ring_attn_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, attn_smem_bytes(8)));
   CU(cudaFuncSetAttribute(ring_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, rd_smem_bytes()));
   CU(cudaFuncSetAttribute(ring_prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, pf_smem_bytes()));
+  CU(cudaFuncSetAttribute(ring_prefill_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, pt_smem_bytes()));
   return HSG_OK;
 }
 
@@ -503,6 +505,10 @@ static int enqueue_step(hsg_engine* e, int nb, int lb) {
         if (lb == 1)
           CU(launch_k(ring_decode_kernel, dim3(std::min(SM_COUNT, nb * ATT_HKV)), dim3(RD_THREADS), rd_smem_bytes(),
                       st, e->pdl, e->ring_maps[ai][0], e->ring_maps[ai][1], e->new_maps[0], e->new_maps[1], a));
+        else if (lb >= 32)
+          CU(launch_k(ring_prefill_tc_kernel, dim3(nb, ATT_HKV, ATT_G * lb / PT_ROWS), dim3(PT_THREADS),
+                      pt_smem_bytes(), st, e->pdl, e->ring_maps[ai][0], e->ring_maps[ai][1], e->new_maps[0],
+                      e->new_maps[1], a));
         else if (lb >= 16)
           CU(launch_k(ring_prefill_kernel, dim3(nb, ATT_HKV, (ATT_G * lb + PF_ROWS - 1) / PF_ROWS), dim3(PF_THREADS),
                       pf_smem_bytes(), st, e->pdl, e->ring_maps[ai][0], e->ring_maps[ai][1], e->new_maps[0],
@@ -1002,8 +1008,12 @@ int hsg_ring_attention(const float* q, void* ring_k, void* ring_v, const void* n
         (rc = make_decode_map(&nk, new_k, (uint64_t)n * ATT_HKV * lb)) ||
         (rc = make_decode_map(&nv, new_v, (uint64_t)n * ATT_HKV * lb)))
       return rc;
-    ring_prefill_kernel<<<dim3(n, ATT_HKV, (ATT_G * lb + PF_ROWS - 1) / PF_ROWS), PF_THREADS, pf_smem_bytes(), st>>>(
-        rk, rv, nk, nv, a);
+    if (lb >= 32)
+      ring_prefill_tc_kernel<<<dim3(n, ATT_HKV, ATT_G * lb / PT_ROWS), PT_THREADS, pt_smem_bytes(), st>>>(rk, rv, nk,
+                                                                                                        nv, a);
+    else
+      ring_prefill_kernel<<<dim3(n, ATT_HKV, (ATT_G * lb + PF_ROWS - 1) / PF_ROWS), PF_THREADS, pf_smem_bytes(),
+                            st>>>(rk, rv, nk, nv, a);
   }
   else ring_attn_kernel<8><<<dim3(n, ATT_HKV, (ATT_G * lb + 7) / 8), ATT_THREADS, attn_smem_bytes(8), st>>>(a);
   CU(cudaGetLastError());
