@@ -1,16 +1,17 @@
 // Multi-token ring-window attention for ticks of 32 or 64 tokens on the 5th-generation tensor cores (tcgen05, TMEM).
 //
-// CTA = (session row n, kv head h, block of 128 query rows: row r = group * lb + token), 128 threads; thread r owns
-// query row r, which is TMEM lane r of both accumulators: S (32 columns, the scores of one 32-key tile) and O (256
-// columns, the output). Thread 0 also issues the TMA loads and the MMAs. Per listed 32-key tile (the slot's filled
-// ring tiles, then this tick's own keys; K and V in a 4-stage shared-memory ring filled by TMA, 128-byte swizzle):
+// CTA = (session row n, kv head h, block of 128 query rows: row r = group * lb + token), 256 threads; thread r < 128
+// owns query row r, which is TMEM lane r of both accumulators: S (32 columns, the scores of one 32-key tile) and O
+// (256 columns, the output); threads 128-255 transpose each V tile while the row threads run the softmax. Thread 0
+// also issues the TMA loads and the MMAs. Per listed 32-key tile (the slot's filled ring tiles, then this tick's own
+// keys; K and V in a 4-stage shared-memory ring filled by TMA, 128-byte swizzle):
 //   S = Q K^T        tcgen05.mma kind::f16, M = 128, N = 32, K = 256 (A = Q staged once as fp16, B = the K tile)
 //   softmax          each thread loads its row of S, masks it (key position kp visible to query position qp iff
 //                    0 <= kp <= qp and kp > qp - 512), and forms P = 2^(s log2e / 16 - m) against a running maximum m
 //                    that is raised only when a tile's maximum exceeds it by more than 8 (log2 units): then the
 //                    row's O and sum are rescaled once (tcgen05.ld / st), otherwise P stays below 2^8 and fp16 holds
-//                    it; P goes to shared memory as fp16 (64-byte swizzle, K-major), and the V tile is transposed
-//                    into V^T [256 dims][32 keys] the same way;
+//                    it; P goes to shared memory as fp16 (64-byte swizzle, K-major); meanwhile the other four
+//                    warps transpose the V tile into V^T [256 dims][32 keys] the same way;
 //   O += P V         tcgen05.mma, M = 128, N = 256, K = 32 (A = P, B = V^T), accumulating in TMEM.
 // A tcgen05.commit after each tile's S MMA also covers the previous tile's PV MMA, so one wait per tile orders the
 // reuse of S, P and V^T. Epilogue: O / l times sigmoid(gate) as the o_proj operand (bf16 hi/lo) or the ungated fp32
@@ -21,7 +22,7 @@
 
 namespace hsg {
 
-constexpr int PT_THREADS = 128;
+constexpr int PT_THREADS = 256;  // warps 0-3: one query row a thread (TMEM lanes); warps 4-7: the V^T transpose
 constexpr int PT_ROWS = 128;
 constexpr int PT_QBOX = PT_ROWS * 128;         // one [128 rows x 64 dims] fp16 box of Q (16 KB)
 constexpr int PT_Q = 4 * PT_QBOX;              // 64 KB
@@ -34,6 +35,13 @@ constexpr uint32_t PT_O_COL = 256;
 
 __host__ __device__ inline int pt_smem_bytes() {
   return PT_Q + PT_STAGES * PT_KVSTAGE + PT_P + PT_VT + (int)sizeof(PfMeta) + (PT_STAGES + 2) * 8 + 16 + 1024;
+}
+
+// 2^x by the PTX fast approximation (a few ulp of fp32: far below the fp16 rounding the softmax weights then get).
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
 }
 
 __global__ void __launch_bounds__(PT_THREADS, 1)
@@ -109,12 +117,12 @@ ring_prefill_tc_kernel(const __grid_constant__ CUtensorMap tm_rk, const __grid_c
     }
     if (lane == 0) meta->ntile = nt;
   }
-  // ---- Q -> fp16, SW128 boxes; warp w stages rows 32 w .. 32 w + 31, lane = 8-dim chunk ----
-  for (int r0 = 0; r0 < 32; r0 += 4) {
+  // ---- Q -> fp16, SW128 boxes; warp w stages rows 16 w .. 16 w + 15, lane = 8-dim chunk ----
+  for (int r0 = 0; r0 < 16; r0 += 4) {
     float4 a[4], b[4];
 #pragma unroll
     for (int u = 0; u < 4; ++u) {
-      const int row = rb0 + 32 * warp + r0 + u;
+      const int row = rb0 + 16 * warp + r0 + u;
       a[u] = b[u] = make_float4(0.f, 0.f, 0.f, 0.f);
       if (row < M) {
         const float4* src = reinterpret_cast<const float4*>(args.qbuf + (head * M + row) * ATT_D + lane * 8);
@@ -124,19 +132,20 @@ ring_prefill_tc_kernel(const __grid_constant__ CUtensorMap tm_rk, const __grid_c
     }
 #pragma unroll
     for (int u = 0; u < 4; ++u) {
-      const int r = 32 * warp + r0 + u;
+      const int r = 16 * warp + r0 + u;
       *reinterpret_cast<uint4*>(qsm + (lane >> 3) * PT_QBOX + sw128_off(r, lane & 7)) =
           make_uint4(pack_half2(a[u].x, a[u].y), pack_half2(a[u].z, a[u].w), pack_half2(b[u].x, b[u].y),
                      pack_half2(b[u].z, b[u].w));
     }
   }
-  // this thread's query row, and its output gates into L2 (read in the epilogue)
-  const int row = rb0 + tid;
+  // this thread's query row (threads 0-127), and its output gates into L2 (read in the epilogue)
+  const bool rowt = tid < PT_ROWS;
+  const int row = rb0 + (tid & (PT_ROWS - 1));
   const int tok = row % lb, grp = row / lb;
-  const bool valid = row < M && tok < len;
+  const bool valid = rowt && row < M && tok < len;
   const int64_t qp = start + tok;
   const float* gate = args.proj + ((size_t)n * lb + tok) * ATT_IN + (h * ATT_G + grp) * 2 * ATT_D + ATT_D;
-  if (!args.out_raw && row < M) {
+  if (!args.out_raw && rowt && row < M) {
 #pragma unroll
     for (int c = 0; c < 8; ++c) asm volatile("prefetch.global.L2 [%0];" ::"l"(gate + 32 * c));
   }
@@ -192,9 +201,10 @@ ring_prefill_tc_kernel(const __grid_constant__ CUtensorMap tm_rk, const __grid_c
     ++commits;
     tc_fence_after();
     const int s = t % PT_STAGES;
-    // ---- V_t -> V^T [256 dims][32 keys], 64-byte swizzle: thread owns dims 2 tid, 2 tid + 1 ----
-    {
-      const uint8_t* vb = kvs + s * PT_KVSTAGE + PF_KV_BYTES + warp * PF_BOX;  // the box of dims 64 w .. 64 w + 63
+    if (!rowt) {
+      // ---- V_t -> V^T [256 dims][32 keys], 64-byte swizzle: thread 128 + i owns dims 2 i, 2 i + 1 ----
+      const int tw = warp - 4;
+      const uint8_t* vb = kvs + s * PT_KVSTAGE + PF_KV_BYTES + tw * PF_BOX;  // the box of dims 64 tw .. 64 tw + 63
       const int ch = lane >> 2, sub = (lane & 3) * 4;                         // 16-byte chunk, byte within it
       uint32_t lo[16], hi[16];
 #pragma unroll
@@ -204,14 +214,14 @@ ring_prefill_tc_kernel(const __grid_constant__ CUtensorMap tm_rk, const __grid_c
         lo[k >> 1] = __byte_perm(a, b, 0x5410);  // (dim d, key k) | (dim d, key k + 1)
         hi[k >> 1] = __byte_perm(a, b, 0x7632);  // (dim d + 1, key k) | (dim d + 1, key k + 1)
       }
-      const int d = 2 * tid;
+      const int d = 2 * (tid - PT_ROWS);
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
         *reinterpret_cast<uint4*>(vts + sw64_off(d, c)) = make_uint4(lo[4 * c], lo[4 * c + 1], lo[4 * c + 2], lo[4 * c + 3]);
         *reinterpret_cast<uint4*>(vts + sw64_off(d + 1, c)) =
             make_uint4(hi[4 * c], hi[4 * c + 1], hi[4 * c + 2], hi[4 * c + 3]);
       }
-    }
+    } else {
     // ---- this row's scores, mask, running maximum (lazily raised), P ----
     float sc[32];
     tmem_ld32(lane_base, sc);
@@ -225,7 +235,7 @@ ring_prefill_tc_kernel(const __grid_constant__ CUtensorMap tm_rk, const __grid_c
       mt = fmaxf(mt, sc[j]);
     }
     const bool raise = mt > m + 8.f || (m == -INFINITY && mt > -INFINITY);
-    const float alpha = raise ? (m == -INFINITY ? 0.f : exp2f(m - mt)) : 1.f;
+    const float alpha = raise ? (m == -INFINITY ? 0.f : ex2_approx(m - mt)) : 1.f;
     if (raise) {
       m = mt;
       l *= alpha;
@@ -244,14 +254,15 @@ ring_prefill_tc_kernel(const __grid_constant__ CUtensorMap tm_rk, const __grid_c
     uint32_t pp[16];
 #pragma unroll
     for (int j = 0; j < 32; j += 2) {
-      const float p0 = sc[j] == -INFINITY ? 0.f : exp2f(sc[j] - m);
-      const float p1 = sc[j + 1] == -INFINITY ? 0.f : exp2f(sc[j + 1] - m);
+      const float p0 = sc[j] == -INFINITY ? 0.f : ex2_approx(sc[j] - m);
+      const float p1 = sc[j + 1] == -INFINITY ? 0.f : ex2_approx(sc[j + 1] - m);
       l += p0 + p1;
       pp[j >> 1] = pack_half2(p0, p1);
     }
 #pragma unroll
     for (int c = 0; c < 4; ++c)
       *reinterpret_cast<uint4*>(psm + sw64_off(tid, c)) = make_uint4(pp[4 * c], pp[4 * c + 1], pp[4 * c + 2], pp[4 * c + 3]);
+    }
     fence_proxy_async();  // P and V^T (generic writes) are read by the tensor cores
     tc_fence_before();
     __syncthreads();
@@ -281,7 +292,7 @@ ring_prefill_tc_kernel(const __grid_constant__ CUtensorMap tm_rk, const __grid_c
   if (ok && nt > 0) ok = __syncthreads_and(mbar_wait(mmab, commits & 1, args.err, ERR_TIMEOUT_MMA));
   tc_fence_after();
   const float inv = (ok && valid && l > 0.f) ? 1.0f / l : 0.f;
-  if (row < M) {
+  if (rowt && row < M) {
 #pragma unroll 1
     for (int c = 0; c < ATT_D; c += 32) {
       float ov[32];
