@@ -6,7 +6,7 @@
 //
 // Producer warp: per item it reads the slot's ring positions, lists the 32-column tiles holding any filled column
 // plus the new-key tile, publishes the list (with every key's position) in a double-buffered metadata block, then
-// streams the K tiles and after them the V tiles through an 8-stage ring. A tile is 32 keys x 256 dims fp16 (16 KB),
+// streams the K tiles and after them the V tiles through an 11-stage ring. A tile is 32 keys x 256 dims fp16 (16 KB),
 // loaded as four [32 x 64] boxes by 2-D TMA with 128-byte swizzle, so the tensor-core fragment loads below are free
 // of shared-memory bank conflicts.
 // Consumer warps (8) -- warp-level MMA (mma.sync m16n8k16, fp16 in, fp32 accumulate); the 4 query rows sit in an
@@ -29,7 +29,7 @@ constexpr int RD_THREADS = RD_CONS + 32;         // + producer warp
 constexpr int RD_TILE = 32;                      // keys per tile
 constexpr int RD_TILE_BYTES = RD_TILE * ATT_D * 2;
 constexpr int RD_SUB_BYTES = RD_TILE * 64 * 2;   // one [32 keys x 64 dims] swizzled box
-constexpr int RD_STAGES = 8;
+constexpr int RD_STAGES = 11;                   // 176 KB in flight per SM (the most that fits)
 constexpr int RD_MAXT = WIN / RD_TILE + 1;       // 16 ring tiles + the new-key tile
 constexpr int RD_MAXK = RD_MAXT * RD_TILE;
 constexpr int RD_PSTRIDE = RD_MAXK + 8;          // fp16 probabilities row stride (bank-spread)
@@ -60,8 +60,8 @@ ring_decode_kernel(const __grid_constant__ CUtensorMap tm_rk, const __grid_const
   float* scp = reinterpret_cast<float*>(meta + 2);             // [4 dim ranges][MAXK][4 rows] partial scores
   __half* pr = reinterpret_cast<__half*>(scp + 4 * RD_MAXK * 4);  // [4 rows][PSTRIDE] probabilities
   float* lsum = reinterpret_cast<float*>(pr + 4 * RD_PSTRIDE);    // [4]
-  uint64_t* full = reinterpret_cast<uint64_t*>(lsum + 4);       // [8]
-  uint64_t* empty = full + RD_STAGES;                           // [8]
+  uint64_t* full = reinterpret_cast<uint64_t*>(lsum + 4);       // [RD_STAGES]
+  uint64_t* empty = full + RD_STAGES;                           // [RD_STAGES]
   uint64_t* meta_full = empty + RD_STAGES;                      // [2]
   uint64_t* meta_free = meta_full + 2;                          // [2]
 
