@@ -15,6 +15,7 @@ import torch
 
 from . import _lib
 from ._lib import check, ptr
+from .build import host
 from .config import DEFAULT, ROLES, SESSION_BUCKETS, TOKEN_BUCKETS, HsgConfig
 from .pack import pack_inputs
 from .weights import engine_layout, extract_state_dict
@@ -209,6 +210,30 @@ class SlotEngine:
         self.stats["ticks"] += 1
         self.length[sl] += 1
         return out_np[:, :n].copy(), np.ones(n, dtype=np.int64)
+
+    def run_single_requests(self, requests):
+        """A one-token tick straight from the request list when every request is (int slot, [one int id]): the
+        reference's validation (runtime.py:161-171), the lb = 1 packing and the length update run in C
+        (``_hsg_host``). Returns (probs [roles, nb, 1, 3] host view, valid until the next tick; n; nb), or None
+        when the requests need the general path -- which is also where every invalid input gets its error."""
+        if type(requests) is not list:
+            return None
+        n = len(requests)
+        if not 0 < n <= self.session_buckets[-1]:
+            return None
+        nb = bucket(n, self.session_buckets)
+        hin, hin_np, hout, out_np = self._buffers(nb, 1)
+        sl = self.__dict__.get("_slot_rows")
+        if sl is None or len(sl) < n:
+            sl = self._slot_rows = np.empty(max(n, self.session_buckets[-1]), dtype=np.int64)
+        h = host()
+        if h.pack_tokens(requests, self.max_slots, self.cfg.vocab, hin_np, nb, self.length, sl) < 0:
+            return None
+        check(self._lib.hsg_step(self.handle, ptr(hin), nb, 1, ptr(hout)))
+        self.stats["graph_replays"] += 1
+        self.stats["ticks"] += 1
+        h.advance(self.length, sl, n)
+        return out_np, n, nb
 
     def fits_one_tick(self, requests):
         """Whether ``requests`` run as a single tick (<= largest row bucket, every request <= 64 tokens)."""

@@ -6,6 +6,7 @@ behind it is the B200 slot engine (hs_guard_b200.engine.SlotEngine -> libhsg.so)
 """
 from __future__ import annotations
 
+from .build import host
 from .config import ROLES, SESSION_BUCKETS, TOKEN_BUCKETS
 from .engine import SlotEngine
 
@@ -85,9 +86,16 @@ class StreamingGuard:
         self.engine.reset()
 
     def step(self, requests, role="assistant"):
+        eng = self.engine
+        if role in ROLES:
+            # one token per request: validation, packing and the result list in C
+            hit = eng.run_single_requests(requests)
+            if hit is not None:
+                probs, n, nb = hit
+                return host().results_single(requests, probs, eng.roles.index(role), n, nb,
+                                             self.metadata["thresholds"][role])
         slots, singles, longest = validate_collect(requests, role, self.max_slots, self.vocab_size)
         tau = self.metadata["thresholds"][role]
-        eng = self.engine
         if len(slots) <= eng.session_buckets[-1] and longest <= TOKEN_BUCKETS[-1]:
             # one tick: cut scores for all rows at once
             if singles is not None:

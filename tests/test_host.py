@@ -188,15 +188,48 @@ def test_library_exports_every_header_symbol():
     assert _lib.lib().hsg_version().startswith(b"hsg-b200")
 
 
+def _fake_safe(slot, pos, tok):
+    return np.float32(((int(slot) * 7919 + int(pos) * 31 + int(tok)) % 1000) / 1000.0)
+
+
+class _FakeStepLib:
+    """hsg_step stand-in: reads the packed tick (ids | lens | slots | starts) and writes p = f(slot, position, token)
+    per role into the output buffer, as the device would; counts its calls."""
+
+    def __init__(self):
+        self.calls = 0
+
+    def hsg_step(self, handle, hin, nb, lb, hout):
+        self.calls += 1
+        buf = np.ctypeslib.as_array(ctypes.cast(hin, ctypes.POINTER(ctypes.c_int64)), shape=(nb * lb + 3 * nb,))
+        out = np.ctypeslib.as_array(ctypes.cast(hout, ctypes.POINTER(ctypes.c_float)), shape=(2, nb, lb, 3))
+        ids, lens = buf[:nb * lb].reshape(nb, lb), buf[nb * lb:nb * lb + nb]
+        slots, starts = buf[nb * lb + nb:nb * lb + 2 * nb], buf[nb * lb + 2 * nb:]
+        out[:] = 0
+        for row in range(nb):
+            for t in range(int(lens[row])):
+                safe = _fake_safe(slots[row], starts[row] + t, ids[row, t])
+                out[:, row, t] = [[safe, 1 - safe, 0], [safe / 2, 1 - safe / 2, 0]]
+        return 0
+
+
 def _fake_engine(max_slots):
-    """A SlotEngine whose device tick is replaced by a deterministic host function of (slot, position, token)."""
+    """A SlotEngine whose device tick is replaced by a deterministic host function of (slot, position, token):
+    run_arrays / run_tokens in Python, hsg_step (the C fast path's call) by _FakeStepLib."""
     from hs_guard_b200 import engine as E
     eng = E.SlotEngine.__new__(E.SlotEngine)
     eng.max_slots, eng.roles = max_slots, ("user", "assistant")
     eng.session_buckets = E.default_session_buckets(max_slots)
     eng.length = np.zeros(max_slots, dtype=np.int64)
-    eng.host, eng.stats, eng._lib, eng._h = {}, {"graph_replays": 0, "ticks": 0}, None, 1
+    eng.host, eng.stats, eng._lib, eng._h = {}, {"graph_replays": 0, "ticks": 0}, _FakeStepLib(), 1
     eng.cfg = DEFAULT
+
+    def buffers(nb, lb):  # pageable stand-ins for the engine's pinned buffers (no CUDA here)
+        if (nb, lb) not in eng.host:
+            hin, hout = torch.zeros(nb * lb + 3 * nb, dtype=torch.int64), torch.zeros(2, nb, lb, 3)
+            eng.host[(nb, lb)] = (hin, hin.numpy(), hout, hout.numpy())
+        return eng.host[(nb, lb)]
+    eng._buffers = buffers
 
     def run_arrays(chunks, slots):
         # deterministic stand-in for the device: p = f(slot, position, token) per role, rows of the tick
@@ -206,10 +239,9 @@ def _fake_engine(max_slots):
         lens = np.array([len(c) for c in chunks], np.int64)
         for row, (c, s) in enumerate(zip(chunks, slots)):
             for t, tok in enumerate(c):
-                pos = eng.length[s] + t
-                safe = np.float32(((int(s) * 7919 + int(pos) * 31 + tok) % 1000) / 1000.0)
+                safe = _fake_safe(s, eng.length[int(s)] + t, tok)
                 probs[:, row, t] = [[safe, 1 - safe, 0], [safe / 2, 1 - safe / 2, 0]]
-        eng.length[np.asarray(slots)] += lens
+        eng.length[np.asarray(slots, dtype=np.int64)] += lens
         return probs, lens
     eng.run_arrays = run_arrays
     eng.run_tokens = lambda slots, ids: run_arrays([[i] for i in ids], slots)
@@ -227,5 +259,62 @@ def test_streaming_guard_single_tick_path_matches_generic_path():
         fast = StreamingGuard.from_engine(_fake_engine(40), DEFAULT_METADATA)
         slow = StreamingGuard.from_engine(_fake_engine(40), DEFAULT_METADATA)
         slow.engine.fits_one_tick = lambda requests: False
-        for tick in ticks:
+        slow.engine.run_single_requests = lambda requests: None
+        for tick in ticks + ticks[:1]:
             assert fast.step(tick, role) == slow.step(tick, role)
+        assert fast.engine._lib.calls == 2 and slow.engine._lib.calls == 0  # the one-token ticks took the C path
+        np.testing.assert_array_equal(fast.engine.length, slow.engine.length)
+
+
+def test_host_pack_tokens_layout_and_fallbacks():
+    """_hsg_host.pack_tokens writes pack_inputs' lb = 1 layout for (int slot, [int id]) requests and declines
+    (-1) everything else; advance adds one position per row."""
+    from hs_guard_b200.build import host
+    h = host()
+    S, V = 40, DEFAULT.vocab
+    length = np.arange(S, dtype=np.int64) * 5
+    req = [(7, [11]), [0, [22]], (31, [V - 1]), (12, [0]), (5, [55])]
+    slots = [7, 0, 31, 12, 5]
+    nb = bucket(len(req), default_session_buckets(S))
+    hin, out = np.full(4 * nb, -9, np.int64), np.zeros(S, np.int64)
+    assert h.pack_tokens(req, S, V, hin, nb, length, out) == len(req)
+    want = np.full(4 * nb, -1, np.int64)
+    pack_inputs([ids for _, ids in req], np.array(slots), nb, 1, length, S, want)
+    np.testing.assert_array_equal(hin, want)
+    np.testing.assert_array_equal(out[:len(req)], slots)
+    before = length.copy()
+    h.advance(length, out, len(req))
+    np.testing.assert_array_equal(length - before, np.isin(np.arange(S), slots).astype(np.int64))
+    declined = [
+        [(1, [2, 3])],                          # more than one token: the general path
+        [(1, (2,))],                            # ids not a list
+        [(True, [2])],                          # int subclass (valid for the reference; the general path takes it)
+        [(1, [np.int64(2)])],                   # not an int (the general path raises)
+        [(1, [2]), (1, [3])],                   # duplicate slot
+        [(S, [2])], [(-1, [2])], [(1, [V])], [(1, [-2])], [(2 ** 70, [1])], [(1, [2 ** 70])],
+        [(1, [])], [(1, [2], 3)], [1], [("1", [2])],
+        [(s, [1]) for s in range(nb + 1)],      # more rows than the bucket
+    ]
+    for bad in declined:
+        assert h.pack_tokens(bad, S, V, np.zeros(4 * nb, np.int64), nb, length, out) == -1, bad
+    assert h.pack_tokens(tuple(req), S, V, hin, nb, length, out) == -1  # requests not a list
+
+
+def test_streaming_guard_fast_path_errors_match_reference():
+    """Invalid one-token ticks get the reference's ValueError through StreamingGuard.step, with no device call
+    and no state change; valid unusual ones (bool slot) run through the general path."""
+    from hs_guard_b200.runtime import DEFAULT_METADATA, StreamingGuard
+    g = StreamingGuard.from_engine(_fake_engine(40), DEFAULT_METADATA)
+    V = DEFAULT.vocab
+    bad_ticks = [[], [(1, [2]), (1, [3])], [(40, [2])], [(-1, [2])], [(1, [V])], [(1, [])], [(1, [2.0])],
+                 [(1.0, [2])], [(1, [np.int64(2)])], [(2, [3]), (1, [-1])]]
+    for role in ("user", "assistant", "system"):
+        for tick in bad_ticks + ([[(1, [2])]] if role == "system" else []):
+            with pytest.raises(ValueError) as got:
+                g.step(tick, role)
+            with pytest.raises(ValueError) as want:
+                validate_requests(tick, role, 40, V)
+            assert str(got.value) == str(want.value), (tick, role)
+    assert g.engine._lib.calls == 0 and not g.engine.length.any()
+    out = g.step([(True, [3]), (2, [4])], "user")
+    assert [r["slot"] for r in out] == [True, 2] and g.engine.length[1] == 1 and g.engine.length[2] == 1
