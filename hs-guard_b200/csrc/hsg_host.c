@@ -1,21 +1,24 @@
-/* Host fast path of StreamingGuard.step for one-token ticks (CPython extension module _hsg_host).
+/* Host fast path of StreamingGuard.step for ticks that fit one launch (CPython extension module _hsg_host).
  *
  * The reference's step (src/hs_guard/runtime.py:161-174) validates every request in Python, packs the tick
- * (engine/slot_engine_v7.py:117-136, pack_inputs) and builds one result dict per request. For the serving shape
- * in which every request is (int slot, [one int token id]) these three loops are the host's share of a step;
- * here they run in C over the request list:
+ * (engine/slot_engine_v7.py:7-25 pack_inputs, :117-136) and builds one result dict per request. For the shapes a
+ * server sends -- a list of (int slot, [int token ids]) with unique slots and at most 64 ids each -- these loops are
+ * the host's share of a step; here they run in C over the request list:
  *
- *   pack_tokens(requests, max_slots, vocab, hin, nb, length, slots_out) -> n or -1
- *       checks every request against the reference's rules (slot an int in [0, max_slots), unique, ids a
- *       one-element list of an int in [0, vocab)) and writes the lb = 1 packed layout of pack_inputs into hin
- *       (int64 [4 * nb]: ids | lens | slots (padding rows: the scratch slot max_slots) | starts = length[slot]),
- *       and the slots into slots_out. Anything else -- a multi-token request, an int subclass, a tuple of ids,
- *       and every invalid input -- returns -1 before any state changes, and the caller takes the general path,
- *       whose Python validation raises the reference's own error for invalid input.
- *   advance(length, slots, n)              length[slots[i]] += 1 for the n rows of a finished tick
- *   results_single(requests, probs, role, n, nb, tau) -> [{'slot', 'cut_scores', 'threshold'}]
- *       cut score = 1 - p(safe) in float32 (as the reference's 1 - p[:, 0] on a float32 tensor), from the
- *       engine's host output probs (float32 [roles][nb][1][3]); 'slot' is the request's own slot object and
+ *   scan(requests, max_slots, vocab) -> longest request, or -1
+ *       the reference's rules (slot an int in [0, max_slots), slots unique, ids a nonempty list of ints in
+ *       [0, vocab)) for requests that are exactly that: a list of 2-tuples / 2-lists of exact ints and lists of
+ *       exact ints. Anything else -- an int subclass such as bool, a tuple of ids, and every invalid input --
+ *       gives -1, and the caller takes the general path, whose Python validation accepts what the reference
+ *       accepts and raises the reference's own error otherwise. Nothing is written.
+ *   fill(requests, hin, nb, lb, length, max_slots)
+ *       pack_inputs' layout into hin (int64 [nb * lb + 3 * nb]): ids [nb][lb] right-padded with 0 | lens |
+ *       slots (padding rows: the scratch slot max_slots) | starts = length[slot] (padding rows 0), for requests
+ *       that scan accepted with longest <= lb and len(requests) <= nb.
+ *   advance(length, hin, nb, lb, n)   length[slot] += len for the n rows of the packed tick (after it ran)
+ *   results(requests, probs, role, n, nb, lb, tau) -> [{'slot', 'cut_scores', 'threshold'}]
+ *       cut score = 1 - p(safe) per token in float32 (the reference's 1 - p[:, 0] on a float32 tensor) from the
+ *       engine's host output probs (float32 [roles][nb][lb][3]); 'slot' is the request's own slot object and
  *       'threshold' the caller's tau object, as in the reference's list.
  *
  * Host code only: no CUDA, no device state.
@@ -62,99 +65,128 @@ static long long small_int(PyObject* o, long long bound) {
   return v;
 }
 
-static PyObject* pack_tokens(PyObject* self, PyObject* args) {
-  PyObject *requests, *hin_o, *len_o, *slots_o;
+static PyObject* scan(PyObject* self, PyObject* args) {
+  PyObject* requests;
   long long max_slots, vocab;
-  Py_ssize_t nb;
-  if (!PyArg_ParseTuple(args, "OLLOnOO", &requests, &max_slots, &vocab, &hin_o, &nb, &len_o, &slots_o)) return NULL;
+  if (!PyArg_ParseTuple(args, "OLL", &requests, &max_slots, &vocab)) return NULL;
   if (!PyList_CheckExact(requests) || max_slots < 1 || vocab < 1) return PyLong_FromLong(-1);
   const Py_ssize_t n = PyList_GET_SIZE(requests);
-  if (n == 0 || n > nb) return PyLong_FromLong(-1);
-  Py_buffer hb, lb, sb;
-  if (get_buf(hin_o, &hb, 1, 8, 4 * nb, "hin") < 0) return NULL;
-  if (get_buf(len_o, &lb, 0, 8, max_slots, "length") < 0) {
-    PyBuffer_Release(&hb);
-    return NULL;
-  }
-  if (get_buf(slots_o, &sb, 1, 8, n, "slots_out") < 0) {
-    PyBuffer_Release(&hb);
-    PyBuffer_Release(&lb);
-    return NULL;
-  }
+  if (n == 0) return PyLong_FromLong(-1);
   unsigned char* seen = (unsigned char*)PyMem_Calloc((size_t)max_slots, 1);
-  if (!seen) {
+  if (!seen) return PyErr_NoMemory();
+  Py_ssize_t longest = 0;
+  for (Py_ssize_t i = 0; i < n && longest >= 0; ++i) {
+    PyObject *s, *ids;
+    if (!unpack_pair(PyList_GET_ITEM(requests, i), &s, &ids) || !PyList_CheckExact(ids)) {
+      longest = -1;
+      break;
+    }
+    const long long sv = small_int(s, max_slots);
+    const Py_ssize_t m = PyList_GET_SIZE(ids);
+    if (sv < 0 || seen[sv] || m == 0) {
+      longest = -1;
+      break;
+    }
+    seen[sv] = 1;
+    for (Py_ssize_t t = 0; t < m; ++t) {
+      if (small_int(PyList_GET_ITEM(ids, t), vocab) < 0) {
+        longest = -1;
+        break;
+      }
+    }
+    if (m > longest && longest >= 0) longest = m;
+  }
+  PyMem_Free(seen);
+  return PyLong_FromSsize_t(longest);
+}
+
+static PyObject* fill(PyObject* self, PyObject* args) {
+  PyObject *requests, *hin_o, *len_o;
+  Py_ssize_t nb, lb;
+  long long max_slots;
+  if (!PyArg_ParseTuple(args, "OOnnOL", &requests, &hin_o, &nb, &lb, &len_o, &max_slots)) return NULL;
+  if (!PyList_CheckExact(requests) || nb < 1 || lb < 1 || PyList_GET_SIZE(requests) > nb) {
+    PyErr_SetString(PyExc_ValueError, "fill: the tick does not fit its bucket");
+    return NULL;
+  }
+  const Py_ssize_t n = PyList_GET_SIZE(requests);
+  Py_buffer hb, lenb;
+  if (get_buf(hin_o, &hb, 1, 8, nb * lb + 3 * nb, "hin") < 0) return NULL;
+  if (get_buf(len_o, &lenb, 0, 8, max_slots, "length") < 0) {
     PyBuffer_Release(&hb);
-    PyBuffer_Release(&lb);
-    PyBuffer_Release(&sb);
-    return PyErr_NoMemory();
+    return NULL;
   }
   int64_t* ids = (int64_t*)hb.buf;
-  int64_t* lens = ids + nb;
-  int64_t* sl = ids + 2 * nb;
-  int64_t* st = ids + 3 * nb;
-  const int64_t* length = (const int64_t*)lb.buf;
-  int64_t* out = (int64_t*)sb.buf;
-  Py_ssize_t i;
-  for (i = 0; i < n; ++i) {
+  int64_t* lens = ids + nb * lb;
+  int64_t* sl = lens + nb;
+  int64_t* st = sl + nb;
+  const int64_t* length = (const int64_t*)lenb.buf;
+  int bad = 0;
+  for (Py_ssize_t i = 0; i < n && !bad; ++i) {
     PyObject *s, *tok;
-    if (!unpack_pair(PyList_GET_ITEM(requests, i), &s, &tok)) break;
+    if (!unpack_pair(PyList_GET_ITEM(requests, i), &s, &tok) || !PyList_CheckExact(tok)) {
+      bad = 1;
+      break;
+    }
     const long long sv = small_int(s, max_slots);
-    if (sv < 0 || seen[sv]) break;
-    seen[sv] = 1;
-    if (!PyList_CheckExact(tok) || PyList_GET_SIZE(tok) != 1) break;
-    const long long tv = small_int(PyList_GET_ITEM(tok, 0), vocab);
-    if (tv < 0) break;
-    ids[i] = tv;
-    lens[i] = 1;
+    const Py_ssize_t m = PyList_GET_SIZE(tok);
+    if (sv < 0 || m < 1 || m > lb) {
+      bad = 1;
+      break;
+    }
+    int64_t* row = ids + i * lb;
+    for (Py_ssize_t t = 0; t < m; ++t) row[t] = PyLong_AsLongLong(PyList_GET_ITEM(tok, t));
+    for (Py_ssize_t t = m; t < lb; ++t) row[t] = 0;
+    lens[i] = m;
     sl[i] = sv;
     st[i] = length[sv];
-    out[i] = sv;
   }
-  const int fast = i == n;
-  if (fast) {
-    for (; i < nb; ++i) {
-      ids[i] = 0;
+  if (!bad) {
+    memset(ids + n * lb, 0, (size_t)((nb - n) * lb) * sizeof(int64_t));
+    for (Py_ssize_t i = n; i < nb; ++i) {
       lens[i] = 0;
       sl[i] = max_slots;
       st[i] = 0;
     }
   }
-  PyMem_Free(seen);
   PyBuffer_Release(&hb);
-  PyBuffer_Release(&lb);
-  PyBuffer_Release(&sb);
-  return PyLong_FromSsize_t(fast ? n : -1);
+  PyBuffer_Release(&lenb);
+  if (bad || PyErr_Occurred()) {
+    if (!PyErr_Occurred()) PyErr_SetString(PyExc_ValueError, "fill: requests that scan did not accept");
+    return NULL;
+  }
+  Py_RETURN_NONE;
 }
 
 static PyObject* advance(PyObject* self, PyObject* args) {
-  PyObject *len_o, *slots_o;
-  Py_ssize_t n;
-  if (!PyArg_ParseTuple(args, "OOn", &len_o, &slots_o, &n)) return NULL;
-  Py_buffer lb, sb;
-  if (PyObject_GetBuffer(len_o, &lb, PyBUF_C_CONTIGUOUS | PyBUF_FORMAT | PyBUF_WRITABLE) < 0) return NULL;
-  if (lb.itemsize != 8) {
-    PyBuffer_Release(&lb);
+  PyObject *len_o, *hin_o;
+  Py_ssize_t nb, lb, n;
+  if (!PyArg_ParseTuple(args, "OOnnn", &len_o, &hin_o, &nb, &lb, &n)) return NULL;
+  if (n < 0 || n > nb || lb < 1) {
+    PyErr_SetString(PyExc_ValueError, "advance: bad sizes");
+    return NULL;
+  }
+  Py_buffer lenb, hb;
+  if (PyObject_GetBuffer(len_o, &lenb, PyBUF_C_CONTIGUOUS | PyBUF_FORMAT | PyBUF_WRITABLE) < 0) return NULL;
+  if (lenb.itemsize != 8) {
+    PyBuffer_Release(&lenb);
     PyErr_SetString(PyExc_ValueError, "length: need int64");
     return NULL;
   }
-  if (get_buf(slots_o, &sb, 0, 8, n, "slots") < 0) {
-    PyBuffer_Release(&lb);
+  if (get_buf(hin_o, &hb, 0, 8, nb * lb + 3 * nb, "hin") < 0) {
+    PyBuffer_Release(&lenb);
     return NULL;
   }
-  int64_t* length = (int64_t*)lb.buf;
-  const int64_t* sl = (const int64_t*)sb.buf;
-  const Py_ssize_t m = lb.len / 8;
+  int64_t* length = (int64_t*)lenb.buf;
+  const int64_t* lens = (const int64_t*)hb.buf + nb * lb;
+  const int64_t* sl = lens + nb;
+  const Py_ssize_t m = lenb.len / 8;
   int bad = 0;
-  for (Py_ssize_t i = 0; i < n; ++i) {
-    if (sl[i] < 0 || sl[i] >= m) {
-      bad = 1;
-      break;
-    }
-  }
+  for (Py_ssize_t i = 0; i < n; ++i) bad |= sl[i] < 0 || sl[i] >= m;
   if (!bad)
-    for (Py_ssize_t i = 0; i < n; ++i) length[sl[i]] += 1;
-  PyBuffer_Release(&lb);
-  PyBuffer_Release(&sb);
+    for (Py_ssize_t i = 0; i < n; ++i) length[sl[i]] += lens[i];
+  PyBuffer_Release(&lenb);
+  PyBuffer_Release(&hb);
   if (bad) {
     PyErr_SetString(PyExc_IndexError, "slot outside the length array");
     return NULL;
@@ -162,18 +194,18 @@ static PyObject* advance(PyObject* self, PyObject* args) {
   Py_RETURN_NONE;
 }
 
-static PyObject* results_single(PyObject* self, PyObject* args) {
+static PyObject* results(PyObject* self, PyObject* args) {
   PyObject *requests, *probs_o, *tau;
   int role;
-  Py_ssize_t n, nb;
-  if (!PyArg_ParseTuple(args, "OOinnO", &requests, &probs_o, &role, &n, &nb, &tau)) return NULL;
-  if (!PyList_CheckExact(requests) || PyList_GET_SIZE(requests) < n || role < 0) {
-    PyErr_SetString(PyExc_ValueError, "results_single: bad arguments");
+  Py_ssize_t n, nb, lb;
+  if (!PyArg_ParseTuple(args, "OOinnnO", &requests, &probs_o, &role, &n, &nb, &lb, &tau)) return NULL;
+  if (!PyList_CheckExact(requests) || PyList_GET_SIZE(requests) < n || n > nb || role < 0 || lb < 1) {
+    PyErr_SetString(PyExc_ValueError, "results: bad arguments");
     return NULL;
   }
   Py_buffer pb;
-  if (get_buf(probs_o, &pb, 0, 4, ((Py_ssize_t)role + 1) * nb * 3, "probs") < 0) return NULL;
-  const float* p = (const float*)pb.buf + (Py_ssize_t)role * nb * 3;
+  if (get_buf(probs_o, &pb, 0, 4, ((Py_ssize_t)role + 1) * nb * lb * 3, "probs") < 0) return NULL;
+  const float* p = (const float*)pb.buf + (Py_ssize_t)role * nb * lb * 3;
   PyObject* list = PyList_New(n);
   if (!list) {
     PyBuffer_Release(&pb);
@@ -181,19 +213,23 @@ static PyObject* results_single(PyObject* self, PyObject* args) {
   }
   for (Py_ssize_t i = 0; i < n; ++i) {
     PyObject *s, *ids;
-    if (!unpack_pair(PyList_GET_ITEM(requests, i), &s, &ids)) {
-      PyErr_SetString(PyExc_ValueError, "results_single: request is not a (slot, ids) pair");
+    if (!unpack_pair(PyList_GET_ITEM(requests, i), &s, &ids) || !PyList_CheckExact(ids) ||
+        PyList_GET_SIZE(ids) > lb) {
+      PyErr_SetString(PyExc_ValueError, "results: request is not a (slot, ids) pair of the tick");
       goto fail;
     }
-    const float cut = 1.0f - p[i * 3];
-    PyObject* c = PyFloat_FromDouble((double)cut);
-    if (!c) goto fail;
-    PyObject* cl = PyList_New(1);
-    if (!cl) {
-      Py_DECREF(c);
-      goto fail;
+    const Py_ssize_t m = PyList_GET_SIZE(ids);
+    PyObject* cl = PyList_New(m);
+    if (!cl) goto fail;
+    for (Py_ssize_t t = 0; t < m; ++t) {
+      const float cut = 1.0f - p[(i * lb + t) * 3];
+      PyObject* c = PyFloat_FromDouble((double)cut);
+      if (!c) {
+        Py_DECREF(cl);
+        goto fail;
+      }
+      PyList_SET_ITEM(cl, t, c);
     }
-    PyList_SET_ITEM(cl, 0, c);
     PyObject* d = PyDict_New();
     if (!d || PyDict_SetItem(d, k_slot, s) < 0 || PyDict_SetItem(d, k_cut, cl) < 0 ||
         PyDict_SetItem(d, k_thr, tau) < 0) {
@@ -213,9 +249,10 @@ fail:
 }
 
 static PyMethodDef methods[] = {
-    {"pack_tokens", pack_tokens, METH_VARARGS, "Validate one-token requests and write the lb = 1 packed tick."},
-    {"advance", advance, METH_VARARGS, "length[slots[i]] += 1 for i < n."},
-    {"results_single", results_single, METH_VARARGS, "The reference's result list for a one-token tick."},
+    {"scan", scan, METH_VARARGS, "Validate a tick's requests (the reference's rules); longest request or -1."},
+    {"fill", fill, METH_VARARGS, "Write pack_inputs' layout of a scanned tick."},
+    {"advance", advance, METH_VARARGS, "length[slot] += len for the rows of a packed tick."},
+    {"results", results, METH_VARARGS, "The reference's result list of a tick."},
     {NULL, NULL, 0, NULL}};
 
 static struct PyModuleDef module = {PyModuleDef_HEAD_INIT, "_hsg_host", NULL, -1, methods, NULL, NULL, NULL, NULL};

@@ -211,29 +211,29 @@ class SlotEngine:
         self.length[sl] += 1
         return out_np[:, :n].copy(), np.ones(n, dtype=np.int64)
 
-    def run_single_requests(self, requests):
-        """A one-token tick straight from the request list when every request is (int slot, [one int id]): the
-        reference's validation (runtime.py:161-171), the lb = 1 packing and the length update run in C
-        (``_hsg_host``). Returns (probs [roles, nb, 1, 3] host view, valid until the next tick; n; nb), or None
-        when the requests need the general path -- which is also where every invalid input gets its error."""
+    def run_requests(self, requests):
+        """One tick straight from the request list when it is a list of (int slot, [int ids]) that fits one
+        launch (<= largest row bucket, <= 64 ids each): the reference's validation (runtime.py:161-171), the
+        packing and the length update run in C (``_hsg_host``). Returns (probs [roles, nb, lb, 3] host view,
+        valid until the next tick; n; nb; lb), or None when the requests need the general path -- which is also
+        where every invalid input gets its error."""
         if type(requests) is not list:
             return None
         n = len(requests)
         if not 0 < n <= self.session_buckets[-1]:
             return None
-        nb = bucket(n, self.session_buckets)
-        hin, hin_np, hout, out_np = self._buffers(nb, 1)
-        sl = self.__dict__.get("_slot_rows")
-        if sl is None or len(sl) < n:
-            sl = self._slot_rows = np.empty(max(n, self.session_buckets[-1]), dtype=np.int64)
         h = host()
-        if h.pack_tokens(requests, self.max_slots, self.cfg.vocab, hin_np, nb, self.length, sl) < 0:
+        longest = h.scan(requests, self.max_slots, self.cfg.vocab)
+        if not 0 < longest <= TOKEN_BUCKETS[-1]:
             return None
-        check(self._lib.hsg_step(self.handle, ptr(hin), nb, 1, ptr(hout)))
+        nb, lb = bucket(n, self.session_buckets), bucket(longest, TOKEN_BUCKETS)
+        hin, hin_np, hout, out_np = self._buffers(nb, lb)
+        h.fill(requests, hin_np, nb, lb, self.length, self.max_slots)
+        check(self._lib.hsg_step(self.handle, ptr(hin), nb, lb, ptr(hout)))
         self.stats["graph_replays"] += 1
         self.stats["ticks"] += 1
-        h.advance(self.length, sl, n)
-        return out_np, n, nb
+        h.advance(self.length, hin_np, nb, lb, n)
+        return out_np, n, nb, lb
 
     def fits_one_tick(self, requests):
         """Whether ``requests`` run as a single tick (<= largest row bucket, every request <= 64 tokens)."""

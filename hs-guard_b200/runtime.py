@@ -88,12 +88,12 @@ class StreamingGuard:
     def step(self, requests, role="assistant"):
         eng = self.engine
         if role in ROLES:
-            # one token per request: validation, packing and the result list in C
-            hit = eng.run_single_requests(requests)
+            # a tick that fits one launch: validation, packing and the result list in C
+            hit = eng.run_requests(requests)
             if hit is not None:
-                probs, n, nb = hit
-                return host().results_single(requests, probs, eng.roles.index(role), n, nb,
-                                             self.metadata["thresholds"][role])
+                probs, n, nb, lb = hit
+                return host().results(requests, probs, eng.roles.index(role), n, nb, lb,
+                                      self.metadata["thresholds"][role])
         slots, singles, longest = validate_collect(requests, role, self.max_slots, self.vocab_size)
         tau = self.metadata["thresholds"][role]
         if len(slots) <= eng.session_buckets[-1] and longest <= TOKEN_BUCKETS[-1]:

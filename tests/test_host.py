@@ -249,55 +249,60 @@ def _fake_engine(max_slots):
 
 
 def test_streaming_guard_single_tick_path_matches_generic_path():
-    """StreamingGuard.step's one-tick fast path returns exactly what the generic per-request path returns."""
+    """StreamingGuard.step's one-tick fast paths (C, then Python) return exactly what the generic per-request path
+    returns, and advance the same lengths."""
     from hs_guard_b200.runtime import DEFAULT_METADATA, StreamingGuard
     rng = np.random.default_rng(3)
     ticks = [[(s, [int(rng.integers(0, 1000))]) for s in range(40)],                       # one token each
              [(s, [int(x) for x in rng.integers(0, 1000, rng.integers(1, 9))]) for s in range(0, 40, 3)],
-             [(5, [int(x) for x in rng.integers(0, 1000, 70)])]]                           # > 64 tokens: generic
+             [[s, [int(x) for x in rng.integers(0, 1000, 64)]] for s in (3, 9, 1)],          # 64 ids, list pairs
+             [(5, [int(x) for x in rng.integers(0, 1000, 70)])],                           # > 64 tokens: generic
+             [(7, tuple(int(x) for x in rng.integers(0, 1000, 3)))]]                       # tuple ids: Python path
     for role in ("user", "assistant"):
         fast = StreamingGuard.from_engine(_fake_engine(40), DEFAULT_METADATA)
         slow = StreamingGuard.from_engine(_fake_engine(40), DEFAULT_METADATA)
         slow.engine.fits_one_tick = lambda requests: False
-        slow.engine.run_single_requests = lambda requests: None
+        slow.engine.run_requests = lambda requests: None
         for tick in ticks + ticks[:1]:
             assert fast.step(tick, role) == slow.step(tick, role)
-        assert fast.engine._lib.calls == 2 and slow.engine._lib.calls == 0  # the one-token ticks took the C path
+        assert fast.engine._lib.calls == 4 and slow.engine._lib.calls == 0  # the C path took ticks 0, 1, 2, 0
         np.testing.assert_array_equal(fast.engine.length, slow.engine.length)
 
 
-def test_host_pack_tokens_layout_and_fallbacks():
-    """_hsg_host.pack_tokens writes pack_inputs' lb = 1 layout for (int slot, [int id]) requests and declines
-    (-1) everything else; advance adds one position per row."""
+def test_host_scan_fill_layout_and_fallbacks():
+    """_hsg_host.scan accepts exactly (int slot, [int ids]) lists under the reference's rules; fill writes
+    pack_inputs' layout; advance adds each row's length."""
     from hs_guard_b200.build import host
     h = host()
     S, V = 40, DEFAULT.vocab
     length = np.arange(S, dtype=np.int64) * 5
-    req = [(7, [11]), [0, [22]], (31, [V - 1]), (12, [0]), (5, [55])]
-    slots = [7, 0, 31, 12, 5]
-    nb = bucket(len(req), default_session_buckets(S))
-    hin, out = np.full(4 * nb, -9, np.int64), np.zeros(S, np.int64)
-    assert h.pack_tokens(req, S, V, hin, nb, length, out) == len(req)
-    want = np.full(4 * nb, -1, np.int64)
-    pack_inputs([ids for _, ids in req], np.array(slots), nb, 1, length, S, want)
-    np.testing.assert_array_equal(hin, want)
-    np.testing.assert_array_equal(out[:len(req)], slots)
-    before = length.copy()
-    h.advance(length, out, len(req))
-    np.testing.assert_array_equal(length - before, np.isin(np.arange(S), slots).astype(np.int64))
+    for req in ([(7, [11]), [0, [22]], (31, [V - 1]), (12, [0]), (5, [55])],
+                [(7, [11, 12, 13]), [0, [22]], (31, list(range(64))), (12, [0, V - 1])]):
+        slots = [s for s, _ in req]
+        longest = max(len(ids) for _, ids in req)
+        assert h.scan(req, S, V) == longest
+        nb, lb = bucket(len(req), default_session_buckets(S)), bucket(longest, (1, 2, 4, 8, 16, 32, 64))
+        hin = np.full(nb * lb + 3 * nb, -9, np.int64)
+        h.fill(req, hin, nb, lb, length, S)
+        want = np.full(nb * lb + 3 * nb, -1, np.int64)
+        pack_inputs([ids for _, ids in req], np.array(slots), nb, lb, length, S, want)
+        np.testing.assert_array_equal(hin, want)
+        before = length.copy()
+        h.advance(length, hin, nb, lb, len(req))
+        add = np.zeros(S, np.int64)
+        add[slots] = [len(ids) for _, ids in req]
+        np.testing.assert_array_equal(length - before, add)
     declined = [
-        [(1, [2, 3])],                          # more than one token: the general path
         [(1, (2,))],                            # ids not a list
         [(True, [2])],                          # int subclass (valid for the reference; the general path takes it)
         [(1, [np.int64(2)])],                   # not an int (the general path raises)
         [(1, [2]), (1, [3])],                   # duplicate slot
-        [(S, [2])], [(-1, [2])], [(1, [V])], [(1, [-2])], [(2 ** 70, [1])], [(1, [2 ** 70])],
-        [(1, [])], [(1, [2], 3)], [1], [("1", [2])],
-        [(s, [1]) for s in range(nb + 1)],      # more rows than the bucket
+        [(S, [2])], [(-1, [2])], [(1, [V])], [(1, [2, -2])], [(2 ** 70, [1])], [(1, [2 ** 70])],
+        [(1, [])], [(1, [2], 3)], [1], [("1", [2])], [],
     ]
     for bad in declined:
-        assert h.pack_tokens(bad, S, V, np.zeros(4 * nb, np.int64), nb, length, out) == -1, bad
-    assert h.pack_tokens(tuple(req), S, V, hin, nb, length, out) == -1  # requests not a list
+        assert h.scan(bad, S, V) == -1, bad
+    assert h.scan(tuple([(1, [2])]), S, V) == -1  # requests not a list
 
 
 def test_streaming_guard_fast_path_errors_match_reference():
