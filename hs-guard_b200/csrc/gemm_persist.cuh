@@ -3,6 +3,13 @@
 // accumulator double-buffered in TMEM, so that draining tile i (TMEM -> registers -> shared -> TMA store, in
 // 32-token chunks) overlaps the loads and MMAs of tile i + 1, and the load ring runs on across tiles.
 //
+// A tile is `halves` x 128 weight rows by tn tokens. With two halves (256 weight rows x 128 tokens, two N = 128
+// accumulators side by side in TMEM) one 64-wide K block moves 64 KB for the same MMA work that 80 KB feeds in a
+// 128 x 256 tile (the activation operand is a hi/lo pair, so it dominates the stage), in three stages instead of two.
+// Measured at 22,528 tokens: ~10 % faster for the split-K reduce-add shapes (out_proj, down: N = 1024), 6-11 %
+// slower for the store and SiLU-mul shapes (in_proj, gate/up), so the planner takes it for the former only. A weight
+// tile whose upper half lies beyond the matrix skips that half.
+//
 // Roles in a 192-thread CTA: warp 0 lane 0 issues the TMA loads (a STAGES-deep ring of [A | B_hi | B_lo] stages
 // shared by all of the CTA's tiles); warp 1 owns TMEM and its lane 0 issues tcgen05.mma, committing each stage back to
 // the producer and each finished accumulator to the epilogue; warps 2-5 are the epilogue, warp w reading accumulator
@@ -20,6 +27,8 @@ constexpr int GPC_CHUNK = 32;  // tokens per epilogue chunk (one TMA store)
 struct GemmPcArgs {
   int tiles_w, tb, splits, kps, k_blocks_total;
   int tn;       // tokens per tile: 128 or 256
+  int halves;   // 128-row weight halves per tile: 1 or 2 (halves * tn <= 256: two accumulators fit TMEM)
+  int n_w;      // weight rows
   int m;        // valid tokens (chunks wholly beyond are not stored)
   int use_lo, stages, mode;
   int* err;
@@ -28,22 +37,26 @@ struct GemmPcArgs {
 __host__ __device__ inline int gpc_chunk_bytes(int mode) {
   return mode == GEMM_SILU_MUL ? 2 * GPC_CHUNK * 64 * 2 : GPC_CHUNK * 128 * 4;
 }
-__host__ __device__ inline int gpc_smem(int tn, int use_lo, int stages, int mode) {
-  return stages * gemm_stage_bytes(tn, use_lo) + 2 * gpc_chunk_bytes(mode) + (2 * stages + 5) * 8 + 16 + 1024;
+__host__ __device__ inline int gpc_stage_bytes(int tn, int use_lo, int halves) {
+  return gemm_stage_bytes(tn, use_lo) + (halves - 1) * GEMM_A_BYTES;
+}
+__host__ __device__ inline int gpc_smem(int tn, int use_lo, int stages, int mode, int halves) {
+  return stages * gpc_stage_bytes(tn, use_lo, halves) + 2 * gpc_chunk_bytes(mode) + (2 * stages + 5) * 8 + 16 + 1024;
 }
 
 __device__ __forceinline__ void bulk_wait_read_1() { asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory"); }
 
-// Output maps: STORE / ATOMIC: tm_o0 = fp32 Y [tokens][N] with a [128 x 32] box; SILU_MUL: tm_o0 / tm_o1 = bf16
-// act_hi / act_lo [tokens][N/2] with [64 x 32] boxes.
+// tm_w: a [64 x 128 * halves] box. Output maps: STORE / ATOMIC: tm_o0 = fp32 Y [tokens][N] with a [128 x 32] box;
+// SILU_MUL: tm_o0 / tm_o1 = bf16 act_hi / act_lo [tokens][N/2] with [64 x 32] boxes.
 __global__ void __launch_bounds__(GPC_THREADS, 1)
 gemm_pc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_xhi,
                const __grid_constant__ CUtensorMap tm_xlo, const __grid_constant__ CUtensorMap tm_o0,
                const __grid_constant__ CUtensorMap tm_o1, const GemmPcArgs args) {
   extern __shared__ __align__(1024) uint8_t gpc_smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(gpc_smem_raw) + 1023) & ~uintptr_t(1023));
-  const int S = args.stages, tn = args.tn;
-  const int stage_bytes = gemm_stage_bytes(tn, args.use_lo);
+  const int S = args.stages, tn = args.tn, halves = args.halves;
+  const int a_bytes = halves * GEMM_A_BYTES;
+  const int stage_bytes = gpc_stage_bytes(tn, args.use_lo, halves);
   const int chunk_bytes = gpc_chunk_bytes(args.mode);
   uint8_t* outbuf = smem + S * stage_bytes;                                   // [2] epilogue chunks
   uint64_t* full = reinterpret_cast<uint64_t*>(outbuf + 2 * chunk_bytes);
@@ -56,11 +69,12 @@ gemm_pc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int total = args.tiles_w * args.tb * args.splits;
+  const int acc_cols = halves * tn;  // one accumulator buffer: the halves side by side
   uint32_t ncols = 32;
-  while (ncols < (uint32_t)(2 * tn)) ncols <<= 1;
+  while (ncols < (uint32_t)(2 * acc_cols)) ncols <<= 1;
   auto decode = [&](int j, int& wrow0, int& tok0, int& kb0, int& nk) {
     const int wt = j % args.tiles_w, r = j / args.tiles_w;
-    wrow0 = wt * 128;
+    wrow0 = wt * 128 * halves;
     tok0 = (r % args.tb) * tn;
     kb0 = (r / args.tb) * args.kps;
     nk = min(args.kps, args.k_blocks_total - kb0);
@@ -104,7 +118,7 @@ gemm_pc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__
           const int s = cnt % S, r = cnt / S;
           if (r > 0 && !mbar_wait(&empty[s], (r - 1) & 1, args.err, ERR_TIMEOUT_MMA)) { ok = false; break; }
           uint8_t* a = smem + s * stage_bytes;
-          uint8_t* bh = a + GEMM_A_BYTES;
+          uint8_t* bh = a + a_bytes;
           uint8_t* bl = bh + tn * GEMM_BK * 2;
           const int kx = (kb0 + i) * GEMM_BK;
           mbar_arrive_expect_tx(&full[s], stage_bytes);
@@ -125,21 +139,25 @@ gemm_pc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__
         int wrow0, tok0, kb0, nk;
         decode(j, wrow0, tok0, kb0, nk);
         const int buf = lt & 1;
+        const int nh = (halves > 1 && wrow0 + 128 < args.n_w) ? 2 : 1;  // weight halves inside the matrix
         if (lt >= 2 && !mbar_wait(&acc_empty[buf], ((lt >> 1) - 1) & 1, args.err, ERR_TIMEOUT_MMA)) break;
         tc_fence_after();
-        const uint32_t d = tmem + (uint32_t)(buf * tn);
         for (int i = 0; i < nk; ++i, ++cnt) {
           const int s = cnt % S, r = cnt / S;
           if (!mbar_wait(&full[s], r & 1, args.err, ERR_TIMEOUT_TMA)) { ok = false; break; }
           tc_fence_after();
-          const uint32_t a = smem_u32(smem + s * stage_bytes);
-          const uint32_t bh = a + GEMM_A_BYTES;
+          const uint32_t a0 = smem_u32(smem + s * stage_bytes);
+          const uint32_t bh = a0 + a_bytes;
           const uint32_t bl = bh + tn * GEMM_BK * 2;
+          for (int hf = 0; hf < nh; ++hf) {
+            const uint32_t d = tmem + (uint32_t)(buf * acc_cols + hf * tn);
+            const uint32_t a = a0 + hf * GEMM_A_BYTES;  // weight rows 128 hf .. of the box
 #pragma unroll
-          for (int kk = 0; kk < GEMM_BK / 16; ++kk) {
-            const uint64_t da = sw128_desc(a + kk * 32);
-            mma_bf16(d, da, sw128_desc(bh + kk * 32), idesc, (i > 0 || kk > 0) ? 1u : 0u);
-            if (args.use_lo) mma_bf16(d, da, sw128_desc(bl + kk * 32), idesc, 1u);
+            for (int kk = 0; kk < GEMM_BK / 16; ++kk) {
+              const uint64_t da = sw128_desc(a + kk * 32);
+              mma_bf16(d, da, sw128_desc(bh + kk * 32), idesc, (i > 0 || kk > 0) ? 1u : 0u);
+              if (args.use_lo) mma_bf16(d, da, sw128_desc(bl + kk * 32), idesc, 1u);
+            }
           }
           mma_commit(&empty[s]);
           progress[1] = cnt + 1;
@@ -159,14 +177,16 @@ gemm_pc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__
       int wrow0, tok0, kb0, nk;
       decode(j, wrow0, tok0, kb0, nk);
       const int buf = lt & 1;
+      const int nh = (halves > 1 && wrow0 + 128 < args.n_w) ? 2 : 1;
       if (!named_sync_and_id<3, 128>(mbar_wait(&acc_full[buf], (lt >> 1) & 1, args.err, ERR_TIMEOUT_MMA))) break;
       tc_fence_after();
-      for (int c = 0; c < tn; c += GPC_CHUNK, ++seq) {
+      for (int q = 0; q < nh * tn; q += GPC_CHUNK, ++seq) {
+        const int hf = q / tn, c = q % tn, wr = wrow0 + 128 * hf;  // weight half, token chunk, first weight row
         uint8_t* cb = outbuf + (seq & 1) * chunk_bytes;
         if (issuer) bulk_wait_read_1();  // the store issued from this buffer two chunks ago has read it
         named_sync_id<3, 128>();
         float v[32];
-        tmem_ld32(lane_base + (uint32_t)(buf * tn + c), v);
+        tmem_ld32(lane_base + (uint32_t)(buf * acc_cols + q), v);
         if (args.mode == GEMM_SILU_MUL) {
           // rows (2f, 2f+1) hold (gate, up) of feature f: the even lane keeps even tokens, the odd lane odd ones
           __nv_bfloat16* sh = reinterpret_cast<__nv_bfloat16*>(cb);  // [32][64]
@@ -201,12 +221,12 @@ gemm_pc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__
         if (issuer) {
           if (tok0 + c < args.m) {
             if (args.mode == GEMM_SILU_MUL) {
-              tma_store_2d(&tm_o0, cb, wrow0 / 2, tok0 + c);
-              tma_store_2d(&tm_o1, cb + GPC_CHUNK * 64 * 2, wrow0 / 2, tok0 + c);
+              tma_store_2d(&tm_o0, cb, wr / 2, tok0 + c);
+              tma_store_2d(&tm_o1, cb + GPC_CHUNK * 64 * 2, wr / 2, tok0 + c);
             } else if (args.mode == GEMM_STORE) {
-              tma_store_2d(&tm_o0, cb, wrow0, tok0 + c);
+              tma_store_2d(&tm_o0, cb, wr, tok0 + c);
             } else {
-              tma_reduce_add_2d(&tm_o0, cb, wrow0, tok0 + c);
+              tma_reduce_add_2d(&tm_o0, cb, wr, tok0 + c);
             }
           }
           bulk_commit();

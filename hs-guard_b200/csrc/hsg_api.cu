@@ -119,6 +119,7 @@ static int make_map(CUtensorMap* map, const void* base, int rows, int k, int box
 struct GemmPlan {
   int tb, tn, splits, kps, stages, smem;
   int persist;  // 1: gemm_pc_kernel (persistent, double-buffered accumulator), one CTA per SM
+  int halves;   // gemm_pc_kernel: 128-row weight halves per tile
 };
 
 static constexpr int SM_COUNT = 148;
@@ -141,7 +142,7 @@ static long gemm_cost(int tiles, int KB, int tb, int tn, int splits, int kps, in
 
 static GemmPlan plan_gemm(int n_w, int K, int M, int mode, int use_lo) {
   const int tiles = n_w / 128, KB = K / 64;
-  GemmPlan best{0, 0, 0, 0, 0, 0, 0};
+  GemmPlan best{0, 0, 0, 0, 0, 0, 0, 1};
   long best_cost = -1;
   const int max_tb = (M + 15) / 16;
   for (int tb = 1; tb <= max_tb; ++tb) {
@@ -155,7 +156,7 @@ static GemmPlan plan_gemm(int n_w, int K, int M, int mode, int use_lo) {
       const long cost = gemm_cost(tiles, KB, tb, tn, splits, kps, mode, use_lo);
       if (best_cost < 0 || cost < best_cost) {
         best_cost = cost;
-        best = {tb, tn, splits, kps, 0, 0, 0};
+        best = {tb, tn, splits, kps, 0, 0, 0, 1};
       }
     }
   }
@@ -172,14 +173,15 @@ static GemmPlan plan_gemm(int n_w, int K, int M, int mode, int use_lo) {
     // / 486 / 519 with 128-token tiles; at 2,048 tokens in_proj 520 against 443. Split-K reduce-add GEMMs keep the
     // per-tile kernel below 4 waves of full tiles, where its K splits fill the machine better.
     best.persist = 1;
-    best.tn = 256;
-    best.tb = tb_full;
+    best.halves = mode == GEMM_ATOMIC ? 2 : 1;  // 256 x 128 tiles for the reduce-add shapes, else 128 x 256
+    best.tn = 256 / best.halves;
+    best.tb = (M + best.tn - 1) / best.tn;
     best.splits = 1;
     best.kps = KB;
     int st = 6;
-    while (st > 2 && gpc_smem(best.tn, use_lo, st, mode) > SMEM_MAX) --st;
+    while (st > 2 && gpc_smem(best.tn, use_lo, st, mode, best.halves) > SMEM_MAX) --st;
     best.stages = st;
-    best.smem = gpc_smem(best.tn, use_lo, st, mode);
+    best.smem = gpc_smem(best.tn, use_lo, st, mode, best.halves);
     return best;
   }
   best.smem = gemm_smem(best.tn, use_lo, best.stages);
@@ -220,7 +222,7 @@ static int launch_gemm(cudaStream_t st, const void* w, int n_w, int K, const voi
   }
   CUtensorMap tw, th, tl, t0, t1;
   int rc;
-  if ((rc = make_map(&tw, w, n_w, K, 128)) != HSG_OK) return rc;
+  if ((rc = make_map(&tw, w, n_w, K, 128 * p.halves)) != HSG_OK) return rc;
   if ((rc = make_map(&th, xhi, m_alloc, K, p.tn)) != HSG_OK) return rc;
   if ((rc = make_map(&tl, use_lo ? xlo : xhi, m_alloc, K, p.tn)) != HSG_OK) return rc;
   const int out_rows = p.persist ? GPC_CHUNK : p.tn;  // the persistent kernel stores 32-token chunks
@@ -239,7 +241,9 @@ static int launch_gemm(cudaStream_t st, const void* w, int n_w, int K, const voi
   }
   if (p.persist) {
     GemmPcArgs a;
-    a.tiles_w = n_w / 128;
+    a.halves = p.halves;
+    a.n_w = n_w;
+    a.tiles_w = (n_w / 128 + p.halves - 1) / p.halves;
     a.tb = p.tb;
     a.splits = 1;
     a.kps = K / 64;

@@ -299,11 +299,12 @@ def test_ring_attention_config3_with_ring_write(L):
         assert torch.equal(ring_k[s, :, col], nk[s, :, 0]), s
 
 
-@pytest.mark.parametrize("mode", [0, 1, 2])
-def test_gemm_large_m_two_ctas_per_sm(L, mode):
-    """Long-running grids (>= 4 waves of 256-token tiles) take 128-token, two-stage tiles (two CTAs per SM)."""
+@pytest.mark.parametrize("mode,n", [(0, 1024), (1, 1024), (2, 1024), (1, 1152)])
+def test_gemm_large_m_persistent(L, mode, n):
+    """Long-running grids (>= 4 waves of 256-token tiles) take the persistent kernel: 128 x 256 tiles, or for the
+    reduce-add mode 256 x 128 tiles (n = 1152: the last tile's upper weight half lies beyond the matrix)."""
     torch.manual_seed(3)
-    m, n, k = 19000, 1024, 1024
+    m, k = 19000, 1024
     w = (torch.randn(n, k, device="cuda") * 0.03).to(torch.bfloat16)
     x = torch.randn(m, k, device="cuda")
     hi, lo = _split(x)
