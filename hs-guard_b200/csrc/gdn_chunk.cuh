@@ -15,7 +15,10 @@
 //
 // Warp roles (same grid and pipeline skeleton as gdn_tc.cuh):
 //  * producer (warp 9): per (row, head) item, TMA loads of the fp16 state tile (two swizzled halves), the row's
-//    q|k|v projection slices for all lb tokens (FUSED) or bf16 q|k|v (RAW), the conv history;
+//    q|k|v projection slices for all lb tokens (FUSED) or bf16 q|k|v (RAW), the conv history. The inputs and the
+//    state have their own barriers: the next item's inputs are requested as soon as the consumers and the prologue
+//    have read this item's for the last time (during the last sub-chunk), its state once this item's state has been
+//    stored; the item metadata (slot, length) is double-buffered;
 //  * prologue (warps 10, 11), per sub-chunk, into a double-buffered scratch area: conv + SiLU (or widening) of q, k
 //    (warp 10: channels 0-95, warp 11: 96-127), v (warp 11) and the gates; the k/q MMA operand columns (fp16 hi/lo),
 //    per-token norm factors and cumulative decays; then warp 10 the decay-masked q.k table and K~ = (Gam_C/Gam_s) k^_s
@@ -151,9 +154,11 @@ gdn_chunk_kernel(const __grid_constant__ GdntMaps maps, const GdnArgs args) {
   float* igl = ipart + GDNC_MAX_LB * 8;                               // [64] log decays
   float* ibe = igl + GDNC_MAX_LB;                                     // [64] betas
   GdnMeta* meta = reinterpret_cast<GdnMeta*>(ibe + GDNC_MAX_LB);
+  // One stage (the host passes stages = 1): full[0] the item's inputs landed, full[1] its state tile landed;
+  // empty[0] the state region is free (epilogue's store has read it), empty[1] the input region is free.
   uint64_t* full = reinterpret_cast<uint64_t*>(meta + GDN_MAX_STAGES);  // producer -> prologue, consumers
   uint64_t* done = full + GDN_MAX_STAGES;                               // consumers -> epilogue
-  uint64_t* empty = done + GDN_MAX_STAGES;                              // epilogue -> producer
+  uint64_t* empty = done + GDN_MAX_STAGES;                              // epilogue, readers -> producer
   uint64_t* sfull = empty + GDN_MAX_STAGES;                             // [2] prologue -> consumers (sub-chunk)
   uint64_t* sdone = sfull + 2;                                          // [2] consumers -> prologue (buffer free)
   uint64_t* cdone = sdone + 2;                                          // consumers' conv -> prologue (per item)
@@ -169,11 +174,11 @@ gdn_chunk_kernel(const __grid_constant__ GdntMaps maps, const GdnArgs args) {
   auto scr = [&](int j) { return scr0 + (j & 1) * GDNC_SCRATCH; };
 
   if (tid == 0) {
-    for (int s = 0; s < S; ++s) {
-      mbar_init(&full[s], 1);
-      mbar_init(&done[s], GDNT_CONS);
-      mbar_init(&empty[s], 1);
-    }
+    mbar_init(&full[0], 1);
+    mbar_init(&full[1], 1);
+    mbar_init(&done[0], GDNT_CONS);
+    mbar_init(&empty[0], 1);
+    mbar_init(&empty[1], GDNT_CONS + 64);  // every consumer and prologue thread, once per item
     for (int b = 0; b < 2; ++b) {
       mbar_init(&sfull[b], 64);
       mbar_init(&sdone[b], GDNT_CONS);
@@ -194,7 +199,7 @@ gdn_chunk_kernel(const __grid_constant__ GdntMaps maps, const GdnArgs args) {
   float4 cw = make_float4(0.f, 0.f, 0.f, 0.f);
   if (FUSED) cw = (reinterpret_cast<const float4*>(args.conv_w) + h * GDN_D)[cpart * KEY_DIM + cch];
   const float negA = -expf(args.A_log[h]), dtb = args.dt_bias[h];
-  auto team_conv = [&](int s, int n, int len) {
+  auto team_conv = [&](int s, int n, int len, int64_t slot) {
     float* x = x_of(s);
     const float* hist = tail_of(s);
     float w[3] = {hist[(0 * 3 + cpart) * GDN_D + cch], hist[(1 * 3 + cpart) * GDN_D + cch],
@@ -208,7 +213,7 @@ gdn_chunk_kernel(const __grid_constant__ GdntMaps maps, const GdnArgs args) {
         if (!(lane & 1)) ipart[((tb + reduce16_index(lane)) * 4 + (warp & 3)) * 2 + cpart] = tot;
       }
     }
-    float* gp = args.conv_pool + (size_t)meta[s].slot * CONV_KEEP * CONV_DIM + cpart * KEY_DIM + h * GDN_D + cch;
+    float* gp = args.conv_pool + (size_t)slot * CONV_KEEP * CONV_DIM + cpart * KEY_DIM + h * GDN_D + cch;
     gp[0] = hh[0];
     gp[CONV_DIM] = hh[1];
     gp[2 * CONV_DIM] = hh[2];
@@ -226,11 +231,10 @@ gdn_chunk_kernel(const __grid_constant__ GdntMaps maps, const GdnArgs args) {
   };
   // FUSED roles other than the consumers: wait for item i's stage, take part in its conv
   auto join_conv = [&](int i) {
-    const int s = i % S;
-    if (!mbar_wait(&full[s], (i / S) & 1, args.err, ERR_TIMEOUT_TMA)) return false;
-    const int len = meta[s].len;
+    if (!mbar_wait(&full[0], i & 1, args.err, ERR_TIMEOUT_TMA)) return false;
+    const int len = meta[i & 1].len;
     if (len > 0) {
-      team_conv(s, row_of(i), len);
+      team_conv(0, row_of(i), len, meta[i & 1].slot);
       mbar_arrive(cdone);
     }
     return true;
@@ -238,14 +242,9 @@ gdn_chunk_kernel(const __grid_constant__ GdntMaps maps, const GdnArgs args) {
 
   if (warp == GDNT_PROD_WARP) {
     // ===================================== producer =====================================
-    int held_len[GDN_MAX_STAGES] = {};
-    int64_t my_len = 0, my_slot = 0, nxt_len = 0, nxt_slot = 0;
-    if (lane < n_items && lane < S) {
-      my_len = args.lens[row_of(lane)];
-      my_slot = args.slots[row_of(lane)];
-    }
-    auto issue_state = [&](int i, int64_t len64, int64_t slot) {
-      const int s = i % S;
+    int held_len[2] = {};
+    int64_t held_slot[2] = {};
+    auto take = [&](int i, int64_t len64, int64_t slot) {  // item i's checked length and slot (metadata i & 1)
       int len = (int)len64;
       if (len64 < 0 || len64 > lb) {
         if (lane == 0) set_error(args.err, ERR_BAD_LEN);
@@ -255,49 +254,59 @@ gdn_chunk_kernel(const __grid_constant__ GdntMaps maps, const GdnArgs args) {
         if (lane == 0) set_error(args.err, ERR_BAD_SLOT);
         len = 0;
       }
-      held_len[s] = len;
-      uint8_t* st = stage_ptr(s);
+      held_len[i & 1] = len;
+      held_slot[i & 1] = slot;
+    };
+    auto issue_state = [&](int i) {
+      const int len = held_len[i & 1];
       if (lane == 0) {
-        meta[s].slot = slot;
-        meta[s].len = len;
-        if (len > 0)  // whole boxes: padded tokens' rows are fetched too (in bounds) and never used
-          mbar_arrive_expect_tx(&full[s], GDNT_TILE + (FUSED ? lb * 3 * GDN_D * 4 + 9 * GDN_D * 4
-                                                             : lb * 3 * GDN_D * 2));
+        if (len > 0)
+          mbar_arrive_expect_tx(&full[1], GDNT_TILE);
         else
-          mbar_arrive(&full[s]);
+          mbar_arrive(&full[1]);
       }
       __syncwarp();
       if (len == 0 || lane != 0) return;
-      tma_load_2d(st, tm_state, 0, tile_row(slot), &full[s]);
-      tma_load_2d(st + GDNT_HALF, tm_state, 64, tile_row(slot), &full[s]);
-      if (FUSED) tma_load_3d(tail_of(s), &maps.in0, h * GDN_D, 0, (int)slot * CONV_KEEP, &full[s]);
+      uint8_t* st = stage_ptr(0);
+      tma_load_2d(st, tm_state, 0, tile_row(held_slot[i & 1]), &full[1]);
+      tma_load_2d(st + GDNT_HALF, tm_state, 64, tile_row(held_slot[i & 1]), &full[1]);
     };
-    auto issue_inputs = [&](int i) {
-      const int s = i % S, n = row_of(i);
-      if (held_len[s] == 0 || lane != 0) return;
-      if (FUSED) tma_load_3d(x_of(s), &maps.in1, h * GDN_D, 0, n * lb, &full[s]);
-      else tma_load_3d(tail_of(s), &maps.in0, h * GDN_D, 0, n * lb, &full[s]);
+    auto issue_inputs = [&](int i) {  // metadata, then the inputs (whole boxes: padded tokens' rows too, in bounds)
+      const int len = held_len[i & 1], n = row_of(i);
+      if (lane == 0) {
+        meta[i & 1].slot = held_slot[i & 1];
+        meta[i & 1].len = len;
+        if (len > 0)
+          mbar_arrive_expect_tx(&full[0], FUSED ? lb * 3 * GDN_D * 4 + 9 * GDN_D * 4 : lb * 3 * GDN_D * 2);
+        else
+          mbar_arrive(&full[0]);
+      }
+      __syncwarp();
+      if (len == 0 || lane != 0) return;
+      if (FUSED) {
+        tma_load_3d(tail_of(0), &maps.in0, h * GDN_D, 0, (int)held_slot[i & 1] * CONV_KEEP, &full[0]);
+        tma_load_3d(x_of(0), &maps.in1, h * GDN_D, 0, n * lb, &full[0]);
+      } else {
+        tma_load_3d(tail_of(0), &maps.in0, h * GDN_D, 0, n * lb, &full[0]);
+      }
     };
-    const int pre = n_items < S ? n_items : S;
-    for (int i = 0; i < pre; ++i)
-      issue_state(i, __shfl_sync(0xffffffffu, my_len, i), __shfl_sync(0xffffffffu, my_slot, i));
-    if (pre < n_items) {
-      nxt_len = args.lens[row_of(pre)];
-      nxt_slot = args.slots[row_of(pre)];
+    if (n_items > 0) {
+      take(0, args.lens[row_of(0)], args.slots[row_of(0)]);
+      issue_state(0);  // the state pool is this kernel's own: requested before the dependency wait
     }
     pdl_wait();
-    for (int i = 0; i < pre; ++i) issue_inputs(i);
+    if (n_items > 0) issue_inputs(0);
     for (int i = 0; i < n_items; ++i) {
-      if (i >= pre) {
-        if (!mbar_wait(&empty[i % S], ((i / S) - 1) & 1, args.err, ERR_TIMEOUT_TMA)) break;
-        issue_state(i, nxt_len, nxt_slot);
-        if (i + 1 < n_items) {
-          nxt_len = args.lens[row_of(i + 1)];
-          nxt_slot = args.slots[row_of(i + 1)];
-        }
-        issue_inputs(i);
+      if (i > 0) {
+        if (!mbar_wait(&empty[0], (i - 1) & 1, args.err, ERR_TIMEOUT_TMA)) break;  // item i - 1 stored
+        issue_state(i);
       }
       if (FUSED && !join_conv(i)) break;
+      if (i + 1 < n_items) {
+        take(i + 1, args.lens[row_of(i + 1)], args.slots[row_of(i + 1)]);
+        if (!mbar_wait(&empty[1], i & 1, args.err, ERR_TIMEOUT_TMA)) break;  // item i's inputs read for the last time
+        issue_inputs(i + 1);
+      }
     }
     return;
   }
@@ -306,10 +315,10 @@ gdn_chunk_kernel(const __grid_constant__ GdntMaps maps, const GdnArgs args) {
     // ===================================== epilogue =====================================
     pdl_wait();  // the outputs may still be read by an earlier kernel
     for (int i = 0; i < n_items; ++i) {
-      const int s = i % S, n = row_of(i);
+      const int s = 0, n = row_of(i);
       if (FUSED && !join_conv(i)) break;
-      if (!mbar_wait(&done[s], (i / S) & 1, args.err, ERR_TIMEOUT_TMA)) break;
-      const int len = meta[s].len;
+      if (!mbar_wait(&done[0], i & 1, args.err, ERR_TIMEOUT_TMA)) break;
+      const int len = meta[i & 1].len;
       if (len == 0) {  // a padding row: zero outputs (the consumers write the outputs of real rows)
         for (int t = 0; t < lb; ++t) {
           const size_t row = (size_t)n * lb + t;
@@ -323,13 +332,13 @@ gdn_chunk_kernel(const __grid_constant__ GdntMaps maps, const GdnArgs args) {
       }
       if (lane == 0) {
         if (len > 0) {  // the new state back to the pool
-          const int row = tile_row(meta[s].slot);
+          const int row = tile_row(meta[i & 1].slot);
           tma_store_2d(tm_state, stage_ptr(s), 0, row);
           tma_store_2d(tm_state, stage_ptr(s) + GDNT_HALF, 64, row);
           bulk_commit();
           bulk_wait_read_all();  // the stores have read the stage
         }
-        mbar_arrive(&empty[s]);
+        mbar_arrive(&empty[0]);
       }
       __syncwarp();
     }
@@ -347,12 +356,15 @@ gdn_chunk_kernel(const __grid_constant__ GdntMaps maps, const GdnArgs args) {
     if (FUSED) pdl_wait();  // the conv history written below may still be read by an earlier kernel
     int jsub = 0, item_seq = 0;
     for (int i = 0; i < n_items; ++i) {
-      const int s = i % S;
-      bool ok = FUSED ? join_conv(i) : mbar_wait(&full[s], (i / S) & 1, args.err, ERR_TIMEOUT_TMA);
-      const int len = ok ? meta[s].len : 1;
+      const int s = 0;
+      bool ok = FUSED ? join_conv(i) : mbar_wait(&full[0], i & 1, args.err, ERR_TIMEOUT_TMA);
+      const int len = ok ? meta[i & 1].len : 1;
       if (ok && len > 0) ok = mbar_wait(cdone, item_seq & 1, args.err, ERR_TIMEOUT_TMA);
       if (!named_sync_and_id<2, 64>(ok)) return;
-      if (len == 0) continue;
+      if (len == 0) {
+        mbar_arrive(&empty[1]);
+        continue;
+      }
       ++item_seq;
       const float* x = x_of(s);
       const __nv_bfloat16* raw = reinterpret_cast<const __nv_bfloat16*>(tail_of(s));
@@ -558,6 +570,7 @@ gdn_chunk_kernel(const __grid_constant__ GdntMaps maps, const GdnArgs args) {
         }
         mbar_arrive(&sfull[jsub & 1]);
       }
+      mbar_arrive(&empty[1]);  // this item's inputs are not read by the prologue again
     }
     return;
   }
@@ -577,16 +590,17 @@ gdn_chunk_kernel(const __grid_constant__ GdntMaps maps, const GdnArgs args) {
   int jsub = 0;
   bool alive = true;
   for (int i = 0; i < n_items && alive; ++i) {
-    const int s = i % S, n = row_of(i);
-    if (!mbar_wait(&full[s], (i / S) & 1, args.err, ERR_TIMEOUT_TMA)) break;
-    const int len = meta[s].len;
+    const int s = 0, n = row_of(i);
+    if (!mbar_wait(&full[0], i & 1, args.err, ERR_TIMEOUT_TMA)) break;
+    const int len = meta[i & 1].len;
+    if (len == 0) mbar_arrive(&empty[1]);
     if (len > 0) {
       float* x = x_of(s);
       const float* hist = tail_of(s);
       const __nv_bfloat16* raw = reinterpret_cast<const __nv_bfloat16*>(tail_of(s));
       // ---- conv + SiLU (FUSED, shared with the other warps) or widening of all tokens; partial sums; gates ----
       if (FUSED) {
-        team_conv(s, n, len);
+        team_conv(s, n, len, meta[i & 1].slot);
       } else if (qk_thread) {  // the isolated kernel's q, k: widened from bf16
         for (int tb = 0; tb < lb; tb += GDNC_SUB) {
           float psq[GDNC_SUB], psk[GDNC_SUB];
@@ -618,6 +632,7 @@ gdn_chunk_kernel(const __grid_constant__ GdntMaps maps, const GdnArgs args) {
           x[(t * XS + SV) * GDN_D + cc] = t < len ? __bfloat162float(raw[(t * 3 + 2) * GDN_D + cc]) : 0.f;
       }
       mbar_arrive(cdone);  // the prologue may build this item's tables
+      if (!mbar_wait(&full[1], i & 1, args.err, ERR_TIMEOUT_TMA)) break;  // the state tile landed
       const uint32_t half_base = smem_u32(stage_ptr(s)) + (warp >> 2) * GDNT_HALF;
       float sv[8][8];
 #pragma unroll
@@ -683,6 +698,7 @@ gdn_chunk_kernel(const __grid_constant__ GdntMaps maps, const GdnArgs args) {
             xv[nt][2 + e] = be * (vr[8] - Gm * rk * pk[nt][2 + e]);
             gq[nt][e] = Gm * rq;  // o = Gam_t rq_t (S^T q_t) + ...
           }
+        if (sc == nsub - 1) mbar_arrive(&empty[1]);  // this item's inputs are not read by the consumers again
         // ---- U^T = X T^T ----
         uint32_t xh[4], xl[4];
         split_half2x(xv[0][0], xv[0][1], xh[0], xl[0]);
@@ -809,7 +825,7 @@ gdn_chunk_kernel(const __grid_constant__ GdntMaps maps, const GdnArgs args) {
                           pack_half2(sv[kt][6], sv[kt][7]));
     }
     fence_proxy_async();   // this thread's writes to the stage are visible to the TMA store
-    mbar_arrive(&done[s]);
+    mbar_arrive(&done[0]);
   }
 }
 
