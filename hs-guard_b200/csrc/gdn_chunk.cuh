@@ -178,7 +178,9 @@ gdn_chunk_kernel(const __grid_constant__ GdntMaps maps, const GdnArgs args) {
     mbar_init(&full[1], 1);
     mbar_init(&done[0], GDNT_CONS);
     mbar_init(&empty[0], 1);
-    mbar_init(&empty[1], GDNT_CONS + 64);  // every consumer and prologue thread, once per item
+    // every consumer, prologue and epilogue thread, once per item: the epilogue warp counts too, so that the inputs
+    // barrier cannot complete twice before it has waited for it (runs of padding items release their inputs at once)
+    mbar_init(&empty[1], GDNT_CONS + 64 + 32);
     for (int b = 0; b < 2; ++b) {
       mbar_init(&sfull[b], 64);
       mbar_init(&sdone[b], GDNT_CONS);
@@ -316,7 +318,8 @@ gdn_chunk_kernel(const __grid_constant__ GdntMaps maps, const GdnArgs args) {
     pdl_wait();  // the outputs may still be read by an earlier kernel
     for (int i = 0; i < n_items; ++i) {
       const int s = 0, n = row_of(i);
-      if (FUSED && !join_conv(i)) break;
+      if (FUSED ? !join_conv(i) : !mbar_wait(&full[0], i & 1, args.err, ERR_TIMEOUT_TMA)) break;
+      mbar_arrive(&empty[1]);  // seen this item's inputs (it reads them only in the conv)
       if (!mbar_wait(&done[0], i & 1, args.err, ERR_TIMEOUT_TMA)) break;
       const int len = meta[i & 1].len;
       if (len == 0) {  // a padding row: zero outputs (the consumers write the outputs of real rows)
@@ -593,7 +596,12 @@ gdn_chunk_kernel(const __grid_constant__ GdntMaps maps, const GdnArgs args) {
     const int s = 0, n = row_of(i);
     if (!mbar_wait(&full[0], i & 1, args.err, ERR_TIMEOUT_TMA)) break;
     const int len = meta[i & 1].len;
-    if (len == 0) mbar_arrive(&empty[1]);
+    if (len == 0) {
+      mbar_arrive(&empty[1]);
+      // a padding item's state barrier completes with a plain arrive, issued after the producer has seen the
+      // previous item stored; waiting for it keeps this item's done (and so its stored signal) behind that
+      if (!mbar_wait(&full[1], i & 1, args.err, ERR_TIMEOUT_TMA)) break;
+    }
     if (len > 0) {
       float* x = x_of(s);
       const float* hist = tail_of(s);

@@ -185,3 +185,26 @@ def test_engine_32_token_ticks_vs_oracle(weights_seed0, state_dtype):
         np.testing.assert_array_equal(eng.pools()["ring_pos"][:2].cpu().numpy(), orc.ring_pos[:2].numpy())
     finally:
         eng.close()
+
+
+def test_engine_64_token_tick_with_trailing_padding_rows(weights_seed0):
+    """A 64-token tick whose row bucket ends in a run of padding rows (100 requests in the 128-row bucket, so every
+    CTA of the chunked delta rule ends on several empty items, which release their inputs at once) completes without a
+    device error and scores the slots it shares with an unpadded tick (96 requests in the 96-row bucket) the same, on
+    that tick and on a following 32-token tick that carries the state on."""
+    from hs_guard_b200.engine import SlotEngine
+    rng = np.random.default_rng(21)
+    first = [[int(x) for x in rng.integers(0, 248320, 64)] for _ in range(100)]
+    second = [[int(x) for x in rng.integers(0, 248320, 32)] for _ in range(100)]
+    eng = SlotEngine(weights_seed0, 128)
+    try:
+        runs = []
+        for n in (96, 100):
+            eng.reset()
+            a = eng.step([(s, first[s]) for s in range(n)])
+            b = eng.step([(s, second[s]) for s in range(n)])
+            runs.append([np.stack(r[role][:96]) for r in (a, b) for role in ("user", "assistant")])
+        for x, y in zip(*runs):
+            assert np.abs(x - y).max() < 1e-4
+    finally:
+        eng.close()
