@@ -202,6 +202,15 @@ gdn_chunk_kernel(const __grid_constant__ GdntMaps maps, const GdnArgs args) {
   if (FUSED) cw = (reinterpret_cast<const float4*>(args.conv_w) + h * GDN_D)[cpart * KEY_DIM + cch];
   const float negA = -expf(args.A_log[h]), dtb = args.dt_bias[h];
   auto team_conv = [&](int s, int n, int len, int64_t slot) {
+    // the gate inputs first: issued after the conv-history stores below, these global loads could not be moved
+    // above them (possible aliasing) and would add a full round trip to every item's conv
+    const bool gate_thread = cpart == 2 && cch < lb;
+    float xa = 0.f, xb = 0.f;
+    if (gate_thread && cch < len) {
+      const size_t rt = (size_t)n * lb + cch;
+      xa = args.proj[rt * GDN_IN + GDN_A_OFF + h];
+      xb = args.proj[rt * GDN_IN + GDN_B_OFF + h];
+    }
     float* x = x_of(s);
     const float* hist = tail_of(s);
     float w[3] = {hist[(0 * 3 + cpart) * GDN_D + cch], hist[(1 * 3 + cpart) * GDN_D + cch],
@@ -219,13 +228,12 @@ gdn_chunk_kernel(const __grid_constant__ GdntMaps maps, const GdnArgs args) {
     gp[0] = hh[0];
     gp[CONV_DIM] = hh[1];
     gp[2 * CONV_DIM] = hh[2];
-    if (cpart == 2 && cch < lb) {  // gates of token cch: log decay -exp(A_log) softplus(a + dt_bias), beta
+    if (gate_thread) {  // gates of token cch: log decay -exp(A_log) softplus(a + dt_bias), beta
       float gl = 0.f, be = 0.f;
       if (cch < len) {
-        const size_t rt = (size_t)n * lb + cch;
-        const float xg = args.proj[rt * GDN_IN + GDN_A_OFF + h] + dtb;
+        const float xg = xa + dtb;
         gl = negA * (xg > 20.f ? xg : log1pf(expf(xg)));
-        be = sigmoidf_(args.proj[rt * GDN_IN + GDN_B_OFF + h]);
+        be = sigmoidf_(xb);
       }
       igl[cch] = gl;
       ibe[cch] = be;
