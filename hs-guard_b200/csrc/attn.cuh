@@ -66,47 +66,65 @@ __global__ void __launch_bounds__(256) attn_prep_kernel(const AttnArgs args) {
       sincosf(ang, &sn[j], &cs[j]);
     }
   }
-  for (int job = warp; job < ATT_HQ + 2 * ATT_HKV; job += 8) {
+  // this warp's jobs (heads): warp and warp + 8. Every input and norm weight is requested before the first output
+  // store: a load issued after a global store cannot be moved above it (possible aliasing), which would cost warps
+  // with two jobs a second round trip.
+  constexpr int NJOB = ATT_HQ + 2 * ATT_HKV;
+  float x[2][8], wn[2][8];
+#pragma unroll
+  for (int r = 0; r < 2; ++r) {
+    const int job = warp + 8 * r;
+    if (job >= NJOB) break;
     const float* src;
     const float* w = nullptr;
     if (job < ATT_HQ) { src = row + job * 2 * ATT_D; w = args.q_norm; }
     else if (job < ATT_HQ + ATT_HKV) { src = row + ATT_K_OFF + (job - ATT_HQ) * ATT_D; w = args.k_norm; }
     else src = row + ATT_V_OFF + (job - ATT_HQ - ATT_HKV) * ATT_D;
-    float x[8];
     const float4 a = reinterpret_cast<const float4*>(src)[lane * 2];
     const float4 b = reinterpret_cast<const float4*>(src)[lane * 2 + 1];
-    x[0] = a.x; x[1] = a.y; x[2] = a.z; x[3] = a.w; x[4] = b.x; x[5] = b.y; x[6] = b.z; x[7] = b.w;
+    x[r][0] = a.x; x[r][1] = a.y; x[r][2] = a.z; x[r][3] = a.w; x[r][4] = b.x; x[r][5] = b.y; x[r][6] = b.z; x[r][7] = b.w;
     if (w) {
+      const float4 c = reinterpret_cast<const float4*>(w)[lane * 2];
+      const float4 d = reinterpret_cast<const float4*>(w)[lane * 2 + 1];
+      wn[r][0] = c.x; wn[r][1] = c.y; wn[r][2] = c.z; wn[r][3] = c.w; wn[r][4] = d.x; wn[r][5] = d.y; wn[r][6] = d.z; wn[r][7] = d.w;
+    }
+  }
+#pragma unroll
+  for (int r = 0; r < 2; ++r) {
+    const int job = warp + 8 * r;
+    if (job >= NJOB) break;
+    float* xr = x[r];
+    if (job < ATT_HQ + ATT_HKV) {  // q and k heads: RMSNorm (1 + w) and RoPE
       float ss = 0.f;
 #pragma unroll
-      for (int j = 0; j < 8; ++j) ss += x[j] * x[j];
-      const float r = 1.0f / sqrtf(warp_sum(ss) * (1.0f / ATT_D) + args.eps);
+      for (int j = 0; j < 8; ++j) ss += xr[j] * xr[j];
+      const float rs = 1.0f / sqrtf(warp_sum(ss) * (1.0f / ATT_D) + args.eps);
 #pragma unroll
-      for (int j = 0; j < 8; ++j) x[j] = x[j] * r * w[lane * 8 + j];
+      for (int j = 0; j < 8; ++j) xr[j] = xr[j] * rs * wn[r][j];
       // rotate-half over dims 0..63: partner of dim d < 32 is d + 32 (lane + 4)
       float partner[8];
 #pragma unroll
-      for (int j = 0; j < 8; ++j) partner[j] = __shfl_xor_sync(0xffffffffu, x[j], 4);
+      for (int j = 0; j < 8; ++j) partner[j] = __shfl_xor_sync(0xffffffffu, xr[j], 4);
       if (lane < 8) {
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
           const float rot = lane < 4 ? -partner[j] : partner[j];
-          x[j] = x[j] * cs[j] + rot * sn[j];
+          xr[j] = xr[j] * cs[j] + rot * sn[j];
         }
       }
     }
     if (job < ATT_HQ) {
       const int kvh = job / ATT_G, g = job % ATT_G;
       float* dst = args.qbuf + (((size_t)n * ATT_HKV + kvh) * (ATT_G * args.lb) + g * args.lb + t) * ATT_D + lane * 8;
-      reinterpret_cast<float4*>(dst)[0] = make_float4(x[0], x[1], x[2], x[3]);
-      reinterpret_cast<float4*>(dst)[1] = make_float4(x[4], x[5], x[6], x[7]);
+      reinterpret_cast<float4*>(dst)[0] = make_float4(xr[0], xr[1], xr[2], xr[3]);
+      reinterpret_cast<float4*>(dst)[1] = make_float4(xr[4], xr[5], xr[6], xr[7]);
     } else {
       const bool is_k = job < ATT_HQ + ATT_HKV;
       const int kvh = is_k ? job - ATT_HQ : job - ATT_HQ - ATT_HKV;
       __half* dst = (is_k ? args.knew : args.vnew) + (((size_t)n * ATT_HKV + kvh) * args.lb + t) * ATT_D + lane * 8;
       __half2 h4[4];
 #pragma unroll
-      for (int j = 0; j < 4; ++j) h4[j] = __floats2half2_rn(x[2 * j], x[2 * j + 1]);
+      for (int j = 0; j < 4; ++j) h4[j] = __floats2half2_rn(xr[2 * j], xr[2 * j + 1]);
       *reinterpret_cast<uint4*>(dst) = *reinterpret_cast<uint4*>(h4);
     }
   }

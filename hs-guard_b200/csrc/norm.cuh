@@ -79,6 +79,11 @@ __global__ void __launch_bounds__(256) head_finish_kernel(const float* hbuf, con
   const int e0 = role * HEAD_E + t * 4;
   float4 x = *reinterpret_cast<const float4*>(hbuf + (size_t)m * (N_ROLES * HEAD_E) + e0);
   const float4 bb = *reinterpret_cast<const float4*>(b1 + e0);
+  // the LayerNorm and classifier weights too, ahead of the reductions' barriers
+  const float4 lw = *reinterpret_cast<const float4*>(ln_w + e0), lb = *reinterpret_cast<const float4*>(ln_b + e0);
+  float4 w2r[N_CLS];
+#pragma unroll
+  for (int c = 0; c < N_CLS; ++c) w2r[c] = *reinterpret_cast<const float4*>(w2 + ((size_t)role * N_CLS + c) * HEAD_E + t * 4);
   x.x += bb.x; x.y += bb.y; x.z += bb.z; x.w += bb.w;
   // mean
   float s = warp_sum(x.x + x.y + x.z + x.w);
@@ -93,13 +98,12 @@ __global__ void __launch_bounds__(256) head_finish_kernel(const float* hbuf, con
   const float var = (red[role * 4][1] + red[role * 4 + 1][1] + red[role * 4 + 2][1] + red[role * 4 + 3][1]) *
                     (1.0f / HEAD_E);
   const float r = 1.0f / sqrtf(var + eps);
-  const float4 lw = *reinterpret_cast<const float4*>(ln_w + e0), lb = *reinterpret_cast<const float4*>(ln_b + e0);
   const float y[4] = {silu(d0 * r * lw.x + lb.x), silu(d1 * r * lw.y + lb.y), silu(d2 * r * lw.z + lb.z),
                       silu(d3 * r * lw.w + lb.w)};
   float logit[N_CLS];
 #pragma unroll
   for (int c = 0; c < N_CLS; ++c) {
-    const float4 w = *reinterpret_cast<const float4*>(w2 + ((size_t)role * N_CLS + c) * HEAD_E + t * 4);
+    const float4 w = w2r[c];
     logit[c] = warp_sum(y[0] * w.x + y[1] * w.y + y[2] * w.z + y[3] * w.w);
   }
   if (lane == 0) { red[warp][2] = logit[0]; red[warp][3] = logit[1]; }
