@@ -246,29 +246,29 @@ class SlotEngine:
         return self.run_arrays([ids for _, ids in requests], slots)
 
     def step(self, requests):
-        """requests [(slot, token_ids)], each slot at most once -> {role: [np.ndarray [L_i, 3]]}
-        (reference slot_engine_v7.py:147-167): long requests run as consecutive <=64-token ticks."""
+        """requests [(slot, token_ids)], each slot at most once -> {role: [np.ndarray [L_i, 3]]}.
+
+        Long requests run as consecutive <=64-token ticks with the reference's schedule (slot_engine_v7.py:147-167):
+        round r carries token piece r of every request longer than 64 r, in request order, in groups of at most the
+        largest row bucket. Each request's probabilities are written into one preallocated array per role."""
         if len({s for s, _ in requests}) != len(requests):
             raise ValueError("a session may appear once per tick")
         if requests and self.fits_one_tick(requests):
             probs, lens = self.tick(requests)
             return {role: [probs[r, row, :n] for row, n in enumerate(lens.tolist())]
                     for r, role in enumerate(self.roles)}
-        largest, rows = TOKEN_BUCKETS[-1], self.session_buckets[-1]
-        results = {role: [[] for _ in requests] for role in self.roles}
-        pending = [(i, s, list(ids)) for i, (s, ids) in enumerate(requests)]
-        while pending:
-            batch = [(i, s, ids[:largest]) for i, s, ids in pending]
-            for start in range(0, len(batch), rows):
-                part = batch[start:start + rows]
-                probs, lens = self.run_arrays([c for _, _, c in part],
-                                              np.fromiter((s for _, s, _ in part), dtype=np.int64, count=len(part)))
-                for r, role in enumerate(self.roles):
-                    for row, (i, _, _) in enumerate(part):
-                        results[role][i].append(probs[r, row, :lens[row]])
-            pending = [(i, s, ids[largest:]) for i, s, ids in pending if len(ids) > largest]
-        return {role: [c[0] if len(c) == 1 else np.concatenate(c) for c in rows_]
-                for role, rows_ in results.items()}
+        piece = TOKEN_BUCKETS[-1]
+        sizes = [len(ids) for _, ids in requests]
+        out = np.empty((len(self.roles), sum(sizes), 3), dtype=np.float32)
+        first = np.concatenate([[0], np.cumsum(sizes)[:-1]]).astype(np.int64)  # each request's offset in ``out``
+        for group, off in _tick_schedule(sizes, piece, self.session_buckets[-1]):
+            chunks = [requests[i][1][off:off + piece] for i in group]
+            probs, lens = self.run_arrays(chunks, np.fromiter((requests[i][0] for i in group), dtype=np.int64,
+                                                              count=len(group)))
+            for row, (i, n) in enumerate(zip(group, lens.tolist())):
+                out[:, first[i] + off:first[i] + off + n] = probs[:, row, :n]
+        return {role: [out[r, first[i]:first[i] + n] for i, n in enumerate(sizes)]
+                for r, role in enumerate(self.roles)}
 
     # ---- measurement helpers ----
     def profile_tick(self, chunks, slots):
@@ -287,6 +287,17 @@ class SlotEngine:
 
     def launches_per_step(self, nb, lb):
         return int(self._lib.hsg_launches_per_step(self.handle, nb, lb))
+
+
+def _tick_schedule(sizes, piece, rows):
+    """The ticks that carry requests of ``sizes`` tokens in pieces of ``piece``: yields (request indices, token
+    offset) per tick. Round r (offset r * piece) holds every request still longer than the offset, in request order,
+    split into groups of at most ``rows``; a request's pieces therefore run in order, one per round."""
+    rounds = max((n + piece - 1) // piece for n in sizes) if sizes else 0
+    for r in range(rounds):
+        live = [i for i, n in enumerate(sizes) if n > r * piece]
+        for g in range(0, len(live), rows):
+            yield live[g:g + rows], r * piece
 
 
 def _from_device(addr, numel, dtype, device):

@@ -1,127 +1,164 @@
 """Decision rules over streamed scores: when a conversation's per-token scores should stop (fire on) a response.
 
-Host-side counterpart of the reference demo's rule layer (examples/demo/server.py:59-117 ``parse_rule``,
-``probabilities``, ``token_score``, ``first_fire`` and :248-284 ``RuleTracker``). A rule is a dict with
+Host-side layer with the decision semantics of the reference demo (examples/demo/server.py:59-117 ``parse_rule``,
+``token_score``, ``first_fire``; :248-284 ``RuleTracker``), which golden vectors produced by those functions pin
+(tests/golden/make_rules_golden.py). A rule is a dict:
 
-- ``rule``: ``threshold`` (``k`` consecutive tokens above ``tau``), ``ema`` (exponential moving average of the score's
-  logit, weight ``alpha``, above logit(``tau``)), ``argmax2`` (the same risky label as arg-max on two consecutive
-  tokens), ``endpoint`` (the last token above ``tau``) or ``off``;
-- ``score``: ``unsafe`` (p(unsafe)) or ``cut`` (1 - p(safe)), computed after a softmax at temperature ``T``.
+- ``rule``: ``threshold`` (``k`` consecutive tokens whose score exceeds ``tau``), ``ema`` (an exponential moving
+  average, weight ``alpha``, of the score's logit exceeds logit(``tau``)), ``argmax2`` (two consecutive tokens share
+  the same risky arg-max label), ``endpoint`` (the message's last token exceeds ``tau``) or ``off``;
+- ``score``: ``unsafe`` (p(unsafe)) or ``cut`` (1 - p(safe)) of a softmax at temperature ``T``.
 
-The engine returns probabilities, not logits; a probability row p is accepted directly (its log is a logit vector
-for the same distribution, so the temperature softmax is unchanged). Trackers are fed one committed token at a time
-and keep O(1) state per conversation, so a server can run one per slot beside StreamingGuard.step.
+Here a tracker is a running maximum plus one small detector object per rule kind, each fed (score, row) per token,
+so a server keeps O(1) state per conversation beside StreamingGuard.step. The engine returns probabilities, not
+logits; a probability row is accepted through ``feed_probs`` (its log is a logit vector of the same distribution, so
+the tempered softmax is unchanged).
 """
 from __future__ import annotations
 
 import math
 
 RULE_KINDS = ("threshold", "ema", "argmax2", "endpoint", "off")
+SCORE_KINDS = ("unsafe", "cut")
+# numeric parameters: (key, default, conversion, lower bound, lower bound allowed, upper bound, upper bound allowed)
+_NUMERIC = (("T", 1.0, float, 0.0, False, 20.0, True),
+            ("tau", 0.5, float, 0.0, False, 1.0, False),
+            ("k", 1, int, 1, True, 256, True),
+            ("alpha", 0.1, float, 0.0, False, 1.0, True))
+_CLAMP = 1e-9  # scores are kept inside (0, 1) before taking their logit
+
+
+def _within(x, lo, lo_ok, hi, hi_ok):
+    return (x >= lo if lo_ok else x > lo) and (x <= hi if hi_ok else x < hi)
 
 
 def parse_rule(value):
-    """Validated rule dict with defaults (reference server.py:59-71); ValueError on anything else."""
+    """A validated rule dict with every parameter present (defaults filled in); ValueError for anything else."""
     if not isinstance(value, dict):
-        raise ValueError("rule must be an object")
-    rule = {"rule": value.get("rule"), "score": value.get("score", "unsafe"), "T": float(value.get("T", 1.0)),
-            "tau": float(value.get("tau", 0.5)), "k": int(value.get("k", 1)), "alpha": float(value.get("alpha", 0.1))}
-    if rule["rule"] not in RULE_KINDS:
-        raise ValueError("unknown rule")
-    if rule["score"] not in ("unsafe", "cut"):
-        raise ValueError("score must be unsafe or cut")
-    in_range = (0 < rule["T"] <= 20, 0 < rule["tau"] < 1, 1 <= rule["k"] <= 256, 0 < rule["alpha"] <= 1)
-    if not all(in_range):
-        raise ValueError("rule parameters out of range")
-    return rule
+        raise ValueError("a rule must be a JSON object")
+    numbers = {key: conv(value.get(key, default)) for key, default, conv, *_ in _NUMERIC}
+    kind, score = value.get("rule"), value.get("score", "unsafe")
+    if kind not in RULE_KINDS:
+        raise ValueError(f"unknown rule kind {kind!r}")
+    if score not in SCORE_KINDS:
+        raise ValueError(f"score must be one of {SCORE_KINDS}")
+    outside = [key for key, _, _, *bounds in _NUMERIC if not _within(numbers[key], *bounds)]
+    if outside:
+        raise ValueError("rule parameters out of range: " + ", ".join(outside))
+    return {"rule": kind, "score": score, **numbers}
 
 
 def softmax_t(logits, temperature):
-    """Softmax of ``logits / temperature`` (max-shifted), as floats."""
-    z = [x / temperature for x in logits]
-    m = max(z)
-    e = [math.exp(x - m) for x in z]
-    s = sum(e)
-    return [x / s for x in e]
+    """Softmax of ``logits / temperature``, shifted by the maximum, as a list of floats."""
+    scaled = [x / temperature for x in logits]
+    shift = max(scaled)
+    weights = [math.exp(x - shift) for x in scaled]
+    total = sum(weights)
+    return [w / total for w in weights]
 
 
 def logits_of(probs):
-    """A logit vector for a probability row (log p; zero probabilities map to a very negative logit)."""
+    """A logit vector for a probability row (log p; a zero probability maps to a very negative logit)."""
     return [math.log(p) if p > 0 else -1e30 for p in probs]
 
 
 def token_score(logits, rule):
+    """The rule's score of one token: p(unsafe), or 1 - p(safe), after the tempered softmax."""
     p = softmax_t(logits, rule["T"])
     return p[1] if rule["score"] == "unsafe" else 1.0 - p[0]
 
 
-def _risky_labels(rule):
-    return (1,) if rule["score"] == "unsafe" else (1, 2)
+def _logit(p):
+    return math.log(p / (1 - p))
 
 
-def _argmax3(row):
-    best = 0
-    for j in (1, 2):
-        if row[j] > row[best]:
-            best = j
-    return best
+def _top_label(row):
+    """Index of the first maximal entry of a 3-class row."""
+    top = 0
+    for j in range(1, 3):
+        if row[j] > row[top]:
+            top = j
+    return top
 
 
-def first_fire(rows, rule):
-    """Index of the first token (of one message's content tokens, in order) at which ``rule`` fires, else -1."""
-    kind = rule["rule"]
-    if kind == "off" or not rows:
-        return -1
-    if kind == "endpoint":
-        return len(rows) - 1 if token_score(rows[-1], rule) > rule["tau"] else -1
-    tracker = RuleTracker(rule)
-    for row in rows:
-        tracker.feed(row)
-        if tracker.fired_k >= 0:
-            return tracker.fired_k
-    return -1
+class _ConsecutiveAbove:
+    """Fires once ``k`` scores in a row exceed ``tau``."""
+
+    def __init__(self, rule):
+        self.tau, self.k, self.streak = rule["tau"], rule["k"], 0
+
+    def update(self, score, row):
+        self.streak = self.streak + 1 if score > self.tau else 0
+        return self.streak >= self.k
+
+
+class _LogitAverage:
+    """Fires once the exponential moving average of the clamped score's logit exceeds logit(tau); the average
+    starts at the first token's logit."""
+
+    def __init__(self, rule):
+        self.alpha, self.bound, self.value = rule["alpha"], _logit(rule["tau"]), None
+
+    def update(self, score, row):
+        x = _logit(min(max(score, _CLAMP), 1 - _CLAMP))
+        self.value = x if self.value is None else self.alpha * x + (1 - self.alpha) * self.value
+        return self.value > self.bound
+
+
+class _RepeatedRiskyLabel:
+    """Fires when a token's arg-max label is risky (unsafe; with the cut score also controversial) and equals the
+    previous token's label."""
+
+    def __init__(self, rule):
+        self.risky = (1,) if rule["score"] == "unsafe" else (1, 2)
+        self.last = None
+
+    def update(self, score, row):
+        label = _top_label(row)
+        fired = label in self.risky and label == self.last
+        self.last = label
+        return fired
+
+
+_DETECTORS = {"threshold": _ConsecutiveAbove, "ema": _LogitAverage, "argmax2": _RepeatedRiskyLabel}
 
 
 class RuleTracker:
-    """Streaming form of ``first_fire`` plus the running maximum score (reference server.py:248-284).
-
-    ``feed(row)`` takes one token's logits; ``feed_probs(p)`` one token's probabilities. ``fired_k`` is the index of
-    the token that fired the rule (-1 while it has not; ``endpoint`` and ``off`` never fire here, a caller applies
-    ``endpoint`` at the end of the message), ``best`` / ``best_k`` the maximum score so far and its index.
-    """
+    """Feeds one committed token at a time: ``fired_k`` is the index of the token at which the rule fired (-1 until
+    then; ``endpoint`` and ``off`` never fire here, a caller applies ``endpoint`` at the end of the message), ``best``
+    and ``best_k`` the largest score so far and the first index where it was reached (``best`` starts at -1)."""
 
     def __init__(self, rule):
         self.rule = rule
-        self.bound = math.log(rule["tau"] / (1 - rule["tau"]))
         self.reset()
 
     def reset(self):
-        self.count, self.run, self.ema, self.previous = 0, 0, None, None
-        self.fired_k, self.best_k, self.best = -1, -1, -1.0
+        make = _DETECTORS.get(self.rule["rule"])
+        self._detector = make(self.rule) if make else None
+        self.count, self.fired_k, self.best_k, self.best = 0, -1, -1, -1.0
 
     def feed_probs(self, probs):
         self.feed(logits_of(probs))
 
     def feed(self, logits):
-        rule, index = self.rule, self.count
-        s = token_score(logits, rule)
-        if s > self.best:
-            self.best, self.best_k = s, index
+        index = self.count
         self.count += 1
-        kind = rule["rule"]
-        if self.fired_k >= 0 or kind in ("off", "endpoint"):
-            return
-        if kind == "argmax2":
-            label = _argmax3(logits)
-            if label in _risky_labels(rule) and label == self.previous:
-                self.fired_k = index
-            self.previous = label
-        elif kind == "threshold":
-            self.run = self.run + 1 if s > rule["tau"] else 0
-            if self.run >= rule["k"]:
-                self.fired_k = index
-        else:  # ema of the score's logit
-            c = min(max(s, 1e-9), 1 - 1e-9)
-            margin = math.log(c / (1 - c))
-            self.ema = margin if self.ema is None else rule["alpha"] * margin + (1 - rule["alpha"]) * self.ema
-            if self.ema > self.bound:
-                self.fired_k = index
+        score = token_score(logits, self.rule)
+        if score > self.best:
+            self.best, self.best_k = score, index
+        if self.fired_k < 0 and self._detector is not None and self._detector.update(score, logits):
+            self.fired_k = index
+
+
+def first_fire(rows, rule):
+    """Index of the first token (of one message's content tokens, in order) at which ``rule`` fires, else -1."""
+    if rule["rule"] == "off" or not rows:
+        return -1
+    if rule["rule"] == "endpoint":
+        return len(rows) - 1 if token_score(rows[-1], rule) > rule["tau"] else -1
+    tracker = RuleTracker(rule)
+    for row in rows:
+        tracker.feed(row)
+        if tracker.fired_k >= 0:
+            break
+    return tracker.fired_k

@@ -104,6 +104,20 @@ def stream_script(seed=7):
     return ticks
 
 
+LONG_CONTEXTS = (8000, 2048, 512, 1000)  # the headline's 512 / 2,048 / 8,000-token contexts, plus a ragged one
+LONG_STEPS = 256
+
+
+def long_script(seed=4):
+    """Headline-shaped streams for len(LONG_CONTEXTS) slots: one request per slot carrying its whole initial context
+    (the engine splits it into 64-token ticks, as the benchmark's prefill does; the 1,000-token context ends in a
+    40-token tick), then LONG_STEPS ticks of one token for every slot. Returns a list of ticks."""
+    r = _rng(seed)
+    prefill = [(s, [int(x) for x in r.integers(0, VOCAB, n)]) for s, n in enumerate(LONG_CONTEXTS)]
+    draws = r.integers(0, VOCAB, (LONG_STEPS, len(LONG_CONTEXTS)))
+    return [prefill] + [[(s, [int(t)]) for s, t in enumerate(row)] for row in draws]
+
+
 def sample_index(numel, seed, count=8192):
     """Sorted random flat indices used to compare large state pools by sample."""
     return np.sort(_rng(1000 + seed).choice(numel, size=min(count, numel), replace=False)).astype(np.int64)

@@ -269,6 +269,24 @@ def test_streaming_guard_single_tick_path_matches_generic_path():
         np.testing.assert_array_equal(fast.engine.length, slow.engine.length)
 
 
+def test_long_request_tick_schedule():
+    """Requests longer than 64 tokens run in rounds of 64-token pieces, each round in request order and split into
+    groups of at most the largest row bucket (the reference's schedule, slot_engine_v7.py:147-167)."""
+    from hs_guard_b200.engine import _tick_schedule
+    got = [(list(g), off) for g, off in _tick_schedule([130, 5, 64, 65], 64, 2)]
+    assert got == [([0, 1], 0), ([2, 3], 0), ([0, 3], 64), ([0], 128)]
+    assert list(_tick_schedule([], 64, 4)) == []
+    eng = _fake_engine(8)
+    rng = np.random.default_rng(4)
+    reqs = [(s, [int(x) for x in rng.integers(0, 1000, n)]) for s, n in zip((6, 2, 0), (150, 1, 64))]
+    out = eng.step(reqs)
+    for r, role in enumerate(("user", "assistant")):
+        for (s, ids), p in zip(reqs, out[role]):
+            safe = np.array([_fake_safe(s, t, tok) for t, tok in enumerate(ids)], np.float32)
+            np.testing.assert_array_equal(p[:, 0], safe if r == 0 else safe / 2)
+    assert eng.length[6] == 150 and eng.length[2] == 1 and eng.length[0] == 64
+
+
 def test_host_scan_fill_layout_and_fallbacks():
     """_hsg_host.scan accepts exactly (int slot, [int ids]) lists under the reference's rules; fill writes
     pack_inputs' layout; advance adds each row's length."""
