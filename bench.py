@@ -204,6 +204,165 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
+# ---- isolated kernels: configs 2 and 3 ------------------------------------------------------------------------------
+class L2Flush:
+    """Writes a 256 MB buffer (twice the 126 MB L2) so that the next kernel reads its inputs from HBM."""
+
+    def __init__(self):
+        import torch
+        self.buf = torch.empty(64 << 20, dtype=torch.float32, device="cuda")
+
+    def __call__(self, stream):
+        import torch
+        with torch.cuda.stream(stream):
+            self.buf.fill_(1.0)
+
+
+def hbm_peak():
+    try:
+        peaks = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))
+        return peaks["hbm_gbs"], "measured"
+    except (OSError, ValueError, KeyError):
+        return 6650.0, "fallback"
+
+
+def bench_c2(lib, steps=1000, reps=5, cold_samples=50):
+    """Config 2: the isolated gated-delta-rule step (hsg_gdn_step, fp32 state) on 16 slots x 16 heads, dk = dv = 128,
+    state ~ N(0, 0.02), q/k/v bf16 ~ N(0, 1) (the kernel L2-normalises q and k per head), raw a, b ~ N(0, 1) with
+    A_log = dt_bias = 0 so that g = -softplus(a) and beta = sigmoid(b); ``steps`` consecutive single-token steps in
+    one CUDA graph (seed 2). The state (16.8 MB) stays in L2 across graph steps, so the graph figure is per-step
+    latency; ``cold`` times single steps after an L2 flush, the HBM-bound case the roofline fraction uses."""
+    import torch
+    from hs_guard_b200 import _lib
+    n, H, D = 16, 16, 128
+    g = torch.Generator(device="cuda").manual_seed(2)
+    packed = torch.randn(steps, n, 1, 3 * H * D, device="cuda", generator=g).to(torch.bfloat16)
+    a = torch.randn(steps, n, 1, H, device="cuda", generator=g)
+    b = torch.randn(steps, n, 1, H, device="cuda", generator=g)
+    state = torch.zeros(n + 1, H, D, D, device="cuda")
+    state[:n] = torch.randn(n, H, D, D, device="cuda", generator=g) * 0.02
+    zeros = torch.zeros(H, device="cuda")
+    slots = torch.arange(n, dtype=torch.int64, device="cuda")
+    lens = torch.ones(n, dtype=torch.int64, device="cuda")
+    o = torch.empty(steps, n, 1, H, D, device="cuda")
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    stream = torch.cuda.Stream()
+
+    def step(t):
+        _lib.check(lib.hsg_gdn_step(packed[t].data_ptr(), a[t].data_ptr(), b[t].data_ptr(), zeros.data_ptr(),
+                                    zeros.data_ptr(), state.data_ptr(), _lib.HSG_STATE_F32, slots.data_ptr(),
+                                    lens.data_ptr(), n, 1, n, o[t].data_ptr(), err.data_ptr(), stream.cuda_stream))
+    with torch.cuda.stream(stream):
+        for t in range(3):
+            step(t)
+    stream.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream, capture_error_mode="relaxed"):
+        for t in range(steps):
+            step(t)
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        graph.replay()
+        start.record(stream)
+        for _ in range(reps):
+            graph.replay()
+        end.record(stream)
+    end.synchronize()
+    graph_us = start.elapsed_time(end) * 1e3 / (reps * steps)
+    flush = L2Flush()
+    cold = []
+    for t in range(cold_samples):
+        flush(stream)
+        s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s0.record(stream)
+        step(t)
+        s1.record(stream)
+        s1.synchronize()
+        cold.append(s0.elapsed_time(s1) * 1e3)
+    assert int(err.item()) == 0, "device error in config 2"
+    state_bytes = 2 * n * H * D * D * 4                      # read + write, fp32
+    io_bytes = n * (3 * H * D * 2 + 2 * H * 4 + H * D * 4)   # q|k|v bf16, a, b, o fp32
+    peak, src = hbm_peak()
+    cold_us = float(np.median(cold))
+    achieved = (state_bytes + io_bytes) / (cold_us * 1e-6) / 1e9
+    return {"workload": "C2: gated-delta-rule single-token step, 16 slots x 16 heads, dk = dv = 128, fp32 state, "
+                        f"{steps} consecutive steps in one CUDA graph, seed 2",
+            "us_per_step_graph": graph_us, "us_per_step_cold": cold_us,
+            "algorithmic_bytes_per_step": state_bytes + io_bytes,
+            "roofline": {"kernel": "gdn_step_kernel (fp32 state, isolated)", "bound": "hbm", "achieved": achieved,
+                         "peak": peak, "unit": "GB/s", "frac": achieved / peak, "peak_source": src,
+                         "timing": "median of single steps after an L2 flush"},
+            "graph_gbs_l2_resident": (state_bytes + io_bytes) / (graph_us * 1e-6) / 1e9}
+
+
+def c3_inputs(n=64, window=512, hkv=2, groups=4, dim=256, seed=3):
+    """Config 3: 64 slots, rings [n+1][2][513][256] fp16 and the new key/value ~ N(0, 1), q ~ N(0, 1) for 4 query
+    heads per KV head; per slot a write position ~ U[0, 512) and a filled length ~ U[1, 512] (rings wrap when the
+    filled length exceeds the write position), one query token each. Returns device tensors and the filled lengths."""
+    import torch
+    r = np.random.Generator(np.random.PCG64(seed))
+    f16 = lambda shape: torch.from_numpy(r.standard_normal(shape, dtype=np.float32)).to(torch.bfloat16).half().cuda()
+    q = torch.from_numpy(r.standard_normal((n, hkv, groups, dim), dtype=np.float32)).to(torch.bfloat16).float().cuda()
+    ring_k, ring_v = f16((n + 1, hkv, window + 1, dim)), f16((n + 1, hkv, window + 1, dim))
+    new_k, new_v = f16((n, hkv, 1, dim)), f16((n, hkv, 1, dim))
+    wp = r.integers(0, window, n)
+    filled = r.integers(1, window + 1, n)
+    ring_pos = np.full((n + 1, window + 1), -1, dtype=np.int64)
+    starts = np.zeros(n, dtype=np.int64)
+    for s in range(n):
+        start = int(wp[s]) + (window if filled[s] > wp[s] else 0)
+        starts[s] = start
+        for p in range(start - int(filled[s]), start):
+            ring_pos[s, p % window] = p
+    dev = lambda x: torch.from_numpy(x).cuda()
+    return (q, ring_k, ring_v, new_k, new_v, dev(ring_pos), dev(np.arange(n, dtype=np.int64)), dev(starts),
+            dev(np.ones(n, dtype=np.int64))), filled
+
+
+def bench_c3(lib, samples=50):
+    """Config 3: the isolated ring-window GQA decode (hsg_ring_attention, one query token per slot, with the ring
+    write) on 64 slots whose rings are partly filled and wrapped; each sample after an L2 flush (the rings, 67 MB,
+    would otherwise stay in L2), CUDA events on the launching stream."""
+    import torch
+    from hs_guard_b200 import _lib
+    (q, rk, rv, nk, nv, rp, slots, starts, lens), filled = c3_inputs()
+    n = q.shape[0]
+    out = torch.empty(n, 2, 4, 256, device="cuda")
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    stream = torch.cuda.Stream()
+
+    def call():
+        _lib.check(lib.hsg_ring_attention(q.data_ptr(), rk.data_ptr(), rv.data_ptr(), nk.data_ptr(), nv.data_ptr(),
+                                          rp.data_ptr(), slots.data_ptr(), starts.data_ptr(), lens.data_ptr(), n, 1,
+                                          n, 1.0 / 16.0, out.data_ptr(), 1, err.data_ptr(), stream.cuda_stream))
+    for _ in range(3):
+        call()
+    flush = L2Flush()
+    times = []
+    for _ in range(samples):
+        flush(stream)
+        s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s0.record(stream)
+        call()
+        s1.record(stream)
+        s1.synchronize()
+        times.append(s0.elapsed_time(s1) * 1e3)
+    assert int(err.item()) == 0, "device error in config 3"
+    us = float(np.median(times))
+    filled_bytes = int(filled.sum()) * 2 * 2 * 256 * 2      # keys + values, 2 KV heads, 256 dims, fp16
+    window_bytes = n * 2 * 2 * 512 * 256 * 2
+    peak, src = hbm_peak()
+    achieved = filled_bytes / (us * 1e-6) / 1e9
+    return {"workload": "C3: ring-window GQA decode, 64 slots, window 512, 8 query / 2 KV heads, head_dim 256, "
+                        "write position ~ U[0,512), filled ~ U[1,512] incl. wrapped rings, one query per slot, seed 3",
+            "us_per_call": us, "filled_tokens_mean": float(filled.mean()),
+            "algorithmic_bytes_filled": filled_bytes, "bytes_full_window": window_bytes,
+            "roofline": {"kernel": "ring_decode_kernel (isolated)", "bound": "hbm", "achieved": achieved, "peak": peak,
+                         "unit": "GB/s", "frac": achieved / peak, "peak_source": src,
+                         "timing": "median of calls after an L2 flush"},
+            "full_window_frac": window_bytes / (us * 1e-6) / 1e9 / peak}
+
+
 # ---- ours --------------------------------------------------------------------------------------------------------
 def gdn_bytes_per_launch(nb, lb, state_elem=2):
     """Algorithmic HBM bytes of one gated-delta-rule launch: per row, 16 heads x one 128 x 128 state tile read + write
@@ -225,19 +384,103 @@ def tick_bytes(nb, lb, state_elem=2):
     return weights + nb * per_row
 
 
+def device_steps(eng, S, K, Wm, rng, barrier, max_over_ranks):
+    """K single-token ticks of all S slots as graph replays of packed ticks already resident in HBM (after Wm warm-up
+    replays), CUDA events on the engine's stream, max over ranks: ms per tick. Advances the engine's lengths."""
+    import torch
+    from hs_guard_b200 import _lib
+    from hs_guard_b200.pack import pack_inputs
+    slots = np.arange(S, dtype=np.int64)
+    staged = []
+    length = eng.length.copy()
+    for k in range(Wm + K):
+        buf = np.zeros(S + 3 * S, dtype=np.int64)
+        pack_inputs([[int(t)] for t in rng.integers(0, 248320, S)], slots, S, 1, length, S, buf)
+        length[slots] += 1
+        staged.append(torch.from_numpy(buf).cuda())
+    L = eng._lib
+    for k in range(Wm):
+        _lib.check(L.hsg_launch(eng.handle, staged[k].data_ptr(), S, 1))
+    _lib.check(L.hsg_synchronize(eng.handle))
+    stream = torch.cuda.ExternalStream(L.hsg_stream(eng.handle))
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    start.record(stream)
+    for k in range(Wm, Wm + K):
+        _lib.check(L.hsg_launch(eng.handle, staged[k].data_ptr(), S, 1))
+    end.record(stream)
+    end.synchronize()
+    _lib.check(L.hsg_fetch(eng.handle, S, 1, None))
+    eng.length[:] = length
+    return max_over_ranks(start.elapsed_time(end) / K)
+
+
+def gdn_roofline(eng, S, rng, state_elem, kernel):
+    """The gated-delta-rule kernel of one eager single-token tick, timed live with CUDA events, against the
+    algorithmic bytes of gdn_bytes_per_launch. Returns (roofline dict, per-kernel eager times)."""
+    req = [[int(t)] for t in rng.integers(0, 248320, S)]
+    _, prof = eng.profile_tick(req, np.arange(S, dtype=np.int64))
+    gdn_ms, gdn_n = prof["gdn"]
+    avg = gdn_ms / max(gdn_n, 1)
+    peak, src = hbm_peak()
+    nbytes = gdn_bytes_per_launch(S, 1, state_elem)
+    achieved = nbytes / (avg * 1e-3) / 1e9
+    traffic = None
+    try:
+        key = "gdn_step_c4_" + ("f16" if state_elem == 2 else "f32")
+        traffic = json.load(open(os.path.join(ROOT, "profiles", "traffic.json")))[key]["bytes_per_launch"]
+    except (OSError, ValueError, KeyError):
+        pass
+    return ({"kernel": kernel, "bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+             "frac": achieved / peak, "peak_source": src, "traffic": traffic, "algorithmic_bytes": nbytes,
+             "avg_launch_ms": avg}, {k: round(v[0], 4) for k, v in prof.items() if v[1]})
+
+
+def c4_state_f32(eng16, sd, S, K, Wm, barrier, max_over_ranks):
+    """C4 with the recurrent state stored in fp32 (HSG_FLAG_STATE_F32): an fp32-state engine takes over the fp16 run's
+    prefilled pools (the state widened to fp32; a single-token tick's work does not depend on the values) and times K
+    single-token ticks of all slots the same way as the headline, plus its delta-rule kernel against the fp32 bytes."""
+    import torch
+    from hs_guard_b200.engine import SlotEngine
+    eng = SlotEngine(sd, S, state_dtype="float32")
+    try:
+        torch.cuda.synchronize()
+        src, dst = eng16.pools(), eng.pools()
+        for name in ("rec", "conv", "ring_k", "ring_v", "ring_pos"):
+            dst[name].copy_(src[name])
+        eng.length[:] = eng16.length
+        torch.cuda.synchronize()
+        rng = np.random.default_rng(200)
+        ms = device_steps(eng, S, K, Wm, rng, barrier, max_over_ranks)
+        roof, kernel_ms = gdn_roofline(eng, S, rng, 4, "gdn_step_kernel (fp32 state, fused conv + gated delta rule "
+                                                       "+ gated norm)")
+        step_bytes = tick_bytes(S, 1, 4)
+        peak, _ = hbm_peak()
+        return {"workload": "C4 with fp32 recurrent state: 352 slots after the 512/2048/8000-token prefill, "
+                            "single-token steps", "value": S / (ms * 1e-3), "unit": "tokens/s", "ms_per_step": ms,
+                "steps": K, "warmup": Wm, "gpu_launches": eng.launches_per_step(S, 1) * K, "roofline": roof,
+                "step_roofline": {"bytes": step_bytes, "achieved_gbs": step_bytes / (ms * 1e-3) / 1e9,
+                                  "frac": step_bytes / (ms * 1e-3) / 1e9 / peak},
+                "kernel_ms_eager": kernel_ms}
+    finally:
+        eng.close()
+
+
+def guarded(fn, *a, **k):
+    """Run one of the default line's extra measurements; a failure is reported in its key, not hidden."""
+    try:
+        return fn(*a, **k)
+    except Exception as exc:  # noqa: BLE001 -- the main measurement stands on its own
+        return {"error": f"{type(exc).__name__}: {exc}"}
+
+
 def run_ours(args):
     import torch
     rank, world, local = dist_env()
-    torch.cuda.set_device(local)
-    if world > 1:
-        import torch.distributed as dist
-        from datetime import timedelta
-        dist.init_process_group("nccl", timeout=timedelta(seconds=600), device_id=torch.device("cuda", local))
-    from hs_guard_b200 import _lib
+    barrier, max_over_ranks = dist_setup(local, world)
     from hs_guard_b200 import weights as W
     from hs_guard_b200.build import build
     from hs_guard_b200.engine import SlotEngine
-    from hs_guard_b200.pack import pack_inputs
     from hs_guard_b200.runtime import DEFAULT_METADATA, StreamingGuard
 
     if rank == 0:
@@ -255,46 +498,11 @@ def run_ours(args):
     torch.cuda.synchronize()
     prefill_s = time.perf_counter() - t0
 
-    def barrier():
-        torch.cuda.synchronize()
-        if world > 1:
-            torch.distributed.barrier()
-        torch.cuda.synchronize()
-
-    def max_over_ranks(x):
-        if world == 1:
-            return x
-        t = torch.tensor([x], dtype=torch.float64, device="cuda")
-        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-        return float(t.item())
-
     rng = np.random.default_rng(100 + rank)
     K, Wm = args.steps, args.warmup
-    slots = np.arange(S, dtype=np.int64)
     # ---- device-resident ticks (value) ----
-    staged = []
-    length = eng.length.copy()
-    for k in range(Wm + K):
-        buf = np.zeros(S + 3 * S, dtype=np.int64)
-        pack_inputs([[int(t)] for t in rng.integers(0, 248320, S)], slots, S, 1, length, S, buf)
-        length[slots] += 1
-        staged.append(torch.from_numpy(buf).cuda())
-    L = eng._lib
-    for k in range(Wm):
-        _lib.check(L.hsg_launch(eng.handle, staged[k].data_ptr(), S, 1))
-    _lib.check(L.hsg_synchronize(eng.handle))
-    stream = torch.cuda.ExternalStream(L.hsg_stream(eng.handle))
-    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     clk = Clocks(local).__enter__()
-    barrier()
-    start.record(stream)
-    for k in range(Wm, Wm + K):
-        _lib.check(L.hsg_launch(eng.handle, staged[k].data_ptr(), S, 1))
-    end.record(stream)
-    end.synchronize()
-    _lib.check(L.hsg_fetch(eng.handle, S, 1, None))
-    eng.length[:] = length
-    dev_ms = max_over_ranks(start.elapsed_time(end) / K)
+    dev_ms = device_steps(eng, S, K, Wm, rng, barrier, max_over_ranks)
     launches = eng.launches_per_step(S, 1)
 
     # ---- end to end through StreamingGuard.step (e2e) ----
@@ -308,34 +516,31 @@ def run_ours(args):
             lat.append((time.perf_counter() - t0) * 1e3)
     clk.__exit__(None, None, None)
     clocks = clk.summary()
-    e2e_ms = max_over_ranks(float(np.mean(lat)))
-    p50 = max_over_ranks(float(np.percentile(lat, 50)))
-    p95 = max_over_ranks(float(np.percentile(lat, 95)))
+    own = [float(np.mean(lat)), float(np.percentile(lat, 50)), float(np.percentile(lat, 95))]
+    e2e_ms, p50, p95 = (max_over_ranks(x) for x in own)
+    per_rank = None
+    if world > 1:
+        t = torch.tensor(own + [S / (own[0] * 1e-3), float(len(os.sched_getaffinity(0)))], dtype=torch.float64,
+                         device="cuda")
+        out = [torch.zeros_like(t) for _ in range(world)]
+        torch.distributed.all_gather(out, t)
+        per_rank = [{"rank": r, "e2e_ms": float(x[0]), "p50_ms": float(x[1]), "p95_ms": float(x[2]),
+                     "e2e_tokens_per_s": float(x[3]), "host_cores_visible": int(x[4])} for r, x in enumerate(out)]
 
     # ---- live roofline of the dominant kernel (eager tick with per-kernel CUDA events) ----
-    req = [[int(t)] for t in rng.integers(0, 248320, S)]
-    _, prof = eng.profile_tick(req, slots)
-    gdn_ms, gdn_n = prof["gdn"]
-    gdn_avg_ms = gdn_ms / max(gdn_n, 1)
-    peaks = {}
-    try:
-        peaks = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))
-    except (OSError, ValueError):
-        pass
-    hbm_peak, peak_src = (peaks["hbm_gbs"], "measured") if "hbm_gbs" in peaks else (6650.0, "fallback")
-    gdn_bytes = gdn_bytes_per_launch(S, 1, state_elem)
-    achieved = gdn_bytes / (gdn_avg_ms * 1e-3) / 1e9
-    traffic = None
-    try:
-        key = "gdn_step_c4_" + ("f16" if state_elem == 2 else "f32")
-        traffic = json.load(open(os.path.join(ROOT, "profiles", "traffic.json")))[key]["bytes_per_launch"]
-    except (OSError, ValueError, KeyError):
-        pass
+    roofline, kernel_ms = gdn_roofline(eng, S, rng, state_elem,
+                                       "gdn_tc_kernel (fused conv + gated delta rule + gated norm)"
+                                       if state_elem == 2 else "gdn_step_kernel (fp32 state)")
     step_bytes = tick_bytes(S, 1, state_elem)
+    hbm, _ = hbm_peak()
 
-    cpu = None
-    complete = None
+    cpu = complete = extras = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        extras = {"c2": guarded(bench_c2, eng._lib), "c3": guarded(bench_c3, eng._lib)}
+        if state_elem == 2:
+            extras["c4_f32"] = guarded(c4_state_f32, eng, sd, S, K, Wm, barrier, max_over_ranks)
+        extras["c5"] = guarded(c5_measure, eng, S, 5, 3, rank, world, lens, barrier, max_over_ranks, local,
+                               state_elem)
         cb = cpu_oracle_rate(sd, args.cpu_slots, 3, 1)
         cpu = {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")}
         eng.close()
@@ -362,16 +567,16 @@ def run_ours(args):
                     "d2h_bytes_per_step": 2 * S * 3 * 4 + 4},
             "gpu_launches": launches * K,
             "clocks": clocks,
-            "roofline": {"kernel": "gdn_tc_kernel (fused conv + gated delta rule + gated norm)", "bound": "hbm",
-                         "achieved": achieved, "peak": hbm_peak, "unit": "GB/s", "frac": achieved / hbm_peak,
-                         "peak_source": peak_src, "traffic": traffic, "algorithmic_bytes": gdn_bytes,
-                         "avg_launch_ms": gdn_avg_ms},
+            "roofline": roofline,
             "step_roofline": {"bytes": step_bytes, "achieved_gbs": step_bytes / (dev_ms * 1e-3) / 1e9,
-                              "frac": step_bytes / (dev_ms * 1e-3) / 1e9 / hbm_peak},
-            "kernel_ms_eager": {k: round(v[0], 4) for k, v in prof.items() if v[1]},
+                              "frac": step_bytes / (dev_ms * 1e-3) / 1e9 / hbm},
+            "kernel_ms_eager": kernel_ms,
+            "per_rank": per_rank,
             "cpu_baseline": cpu,
             "complete_message": complete,
         }
+        if extras:
+            line.update(extras)
         print(json.dumps(line), flush=True)
     if eng is not None:
         eng.close()
@@ -380,35 +585,16 @@ def run_ours(args):
         torch.distributed.destroy_process_group()
 
 
-def run_c5(args):
-    """C5 per GPU: 352 slots stream 64-token ticks (the chunked delta-rule path); each slot's conversation has a
-    512, 2,048 or 8,000-token context (one third each, seed 5 + 1000 rank) and the slot is reset and reassigned when it
-    ends or after 4,096 tokens, whichever comes first. Starting points are staggered so that reassignments spread over
-    the ticks; the resets (hsg_reset_slot) are inside the timed region. A step is one tick of 352 x 64 tokens."""
+def c5_measure(eng, S, K, Wm, rank, world, lens, barrier, max_over_ranks, local, state_elem, e2e=True):
+    """The C5 measurement on an engine: 64-token ticks over S slots, each slot's conversation 512, 2,048 or 8,000
+    tokens long (one third each, seed 5 + 1000 rank), reset and reassigned when it ends or after 4,096 tokens; the
+    resets (hsg_reset_slot) are inside the timed region. Returns the figures of the C5 line."""
     import torch
-    rank, world, local = dist_env()
-    torch.cuda.set_device(local)
-    if world > 1:
-        import torch.distributed as dist
-        from datetime import timedelta
-        dist.init_process_group("nccl", timeout=timedelta(seconds=600), device_id=torch.device("cuda", local))
     from hs_guard_b200 import _lib
-    from hs_guard_b200 import weights as W
-    from hs_guard_b200.build import build
-    from hs_guard_b200.engine import SlotEngine
     from hs_guard_b200.pack import pack_inputs
     from hs_guard_b200.runtime import DEFAULT_METADATA, StreamingGuard
-
-    if rank == 0:
-        build()
-    if world > 1:
-        torch.distributed.barrier()
-    S, LB, CAP = args.slots, 64, 4096
-    sd = W.random_state_dict(0)
-    eng = SlotEngine(sd, S, state_dtype=args.state_dtype)
-    state_elem = 2 if args.state_dtype == "float16" else 4
+    LB, CAP = 64, 4096
     guard = StreamingGuard.from_engine(eng, DEFAULT_METADATA)
-    lens = tuple(int(x) for x in args.contexts.split(","))
     rng = np.random.Generator(np.random.PCG64(5 + 1000 * rank))
 
     def conversation():
@@ -416,7 +602,6 @@ def run_c5(args):
 
     left = np.array([conversation() for _ in range(S)], dtype=np.int64)
     left = rng.integers(1, left // LB + 1) * LB  # staggered: each slot starts somewhere inside its first conversation
-    K, Wm = args.steps, args.warmup
     slots = np.arange(S, dtype=np.int64)
 
     def plan(n):
@@ -429,19 +614,6 @@ def run_c5(args):
             out.append((resets.tolist(), rng.integers(0, 248320, (S, LB))))
             left[:] -= LB
         return out
-
-    def barrier():
-        torch.cuda.synchronize()
-        if world > 1:
-            torch.distributed.barrier()
-        torch.cuda.synchronize()
-
-    def max_over_ranks(x):
-        if world == 1:
-            return x
-        t = torch.tensor([x], dtype=torch.float64, device="cuda")
-        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-        return float(t.item())
 
     # ---- device-resident ticks (value) ----
     eng.reset()
@@ -480,20 +652,20 @@ def run_c5(args):
 
     # ---- end to end: slot resets + StreamingGuard.step with host lists ----
     lat = []
-    e2e_ticks = plan(Wm + K)
-    for k, (resets, chunk) in enumerate(e2e_ticks):
-        if k == Wm:
-            barrier()
-        t0 = time.perf_counter()
-        for s in resets:
-            eng.reset_slot(s)
-        guard.step([(int(s), row) for s, row in zip(slots, chunk.tolist())], role="assistant")
-        if k >= Wm:
-            lat.append((time.perf_counter() - t0) * 1e3)
+    if e2e:
+        for k, (resets, chunk) in enumerate(plan(Wm + K)):
+            if k == Wm:
+                barrier()
+            t0 = time.perf_counter()
+            for s in resets:
+                eng.reset_slot(s)
+            guard.step([(int(s), row) for s, row in zip(slots, chunk.tolist())], role="assistant")
+            if k >= Wm:
+                lat.append((time.perf_counter() - t0) * 1e3)
     clk.__exit__(None, None, None)
-    e2e_ms = max_over_ranks(float(np.mean(lat)))
-    p50 = max_over_ranks(float(np.percentile(lat, 50)))
-    p95 = max_over_ranks(float(np.percentile(lat, 95)))
+    e2e_ms = max_over_ranks(float(np.mean(lat))) if lat else None
+    p50 = max_over_ranks(float(np.percentile(lat, 50))) if lat else None
+    p95 = max_over_ranks(float(np.percentile(lat, 95))) if lat else None
 
     # ---- per-kernel CUDA events of one eager tick ----
     _, prof = eng.profile_tick(rng.integers(0, 248320, (S, LB)).tolist(), slots)
@@ -504,44 +676,92 @@ def run_c5(args):
         pass
     tflops_peak, tsrc = (peaks["bf16_tflops_sustained"], "measured sustained") if "bf16_tflops_sustained" in peaks \
         else (1400.0, "fallback sustained")
-    hbm_peak, hsrc = (peaks["hbm_gbs"], "measured") if "hbm_gbs" in peaks else (6650.0, "fallback")
+    hbm, hsrc = hbm_peak()
     gemm_ms = sum(v[0] for k, v in prof.items() if k.startswith("gemm") or k == "head_gemm")
     gemm_n = sum(v[1] for k, v in prof.items() if k.startswith("gemm") or k == "head_gemm")
     gemm_flops = 2.0 * 498_113_344 * S * LB  # algorithmic (the hi/lo activation pair executes twice this)
     gdn_ms, gdn_n = prof["gdn"]
     gdn_bytes = gdn_bytes_per_launch(S, LB, state_elem)
-    launches = eng.launches_per_step(S, LB)
+    achieved = gemm_flops / (gemm_ms * 1e-3) / 1e12
+    tokens = S * LB * world
+    return {
+        "value": tokens / (dev_ms * 1e-3), "ms_per_step": dev_ms, "tokens_per_tick": S * LB,
+        "resets_in_timed_ticks": n_resets, "clocks": clk.summary(),
+        "latency_ms": {"p50": p50, "p95": p95, "device_per_step": dev_ms},
+        "e2e": None if e2e_ms is None else {"value": tokens / (e2e_ms * 1e-3), "unit": "tokens/s",
+                                            "h2d_bytes_per_step": (S * LB + 3 * S) * 8,
+                                            "d2h_bytes_per_step": 2 * S * LB * 3 * 4 + 4},
+        "gpu_launches": eng.launches_per_step(S, LB) * K,
+        "roofline": {"kernel": "gemm_pc_kernel + gemm_tc_kernel (all projections of one tick)", "bound": "tensor",
+                     "achieved": achieved, "peak": tflops_peak, "unit": "TFLOP/s", "frac": achieved / tflops_peak,
+                     "peak_source": tsrc, "traffic": None, "algorithmic_flops": gemm_flops,
+                     "tick_ms": gemm_ms, "launches": gemm_n},
+        "gdn_chunk": {"kernel": "gdn_chunk_kernel", "avg_launch_ms": gdn_ms / max(gdn_n, 1),
+                      "algorithmic_bytes": gdn_bytes,
+                      "achieved_gbs": gdn_bytes / (gdn_ms / max(gdn_n, 1) * 1e-3) / 1e9,
+                      "hbm_frac": gdn_bytes / (gdn_ms / max(gdn_n, 1) * 1e-3) / 1e9 / hbm, "peak_source": hsrc},
+        "kernel_ms_eager": {k: round(v[0], 4) for k, v in prof.items() if v[1]},
+    }
+
+
+def dist_setup(local, world):
+    import torch
+    torch.cuda.set_device(local)
+    if world > 1:
+        import torch.distributed as dist
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=600), device_id=torch.device("cuda", local))
+
+    def barrier():
+        torch.cuda.synchronize()
+        if world > 1:
+            torch.distributed.barrier()
+        torch.cuda.synchronize()
+
+    def max_over_ranks(x):
+        if world == 1:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device="cuda")
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        return float(t.item())
+    return barrier, max_over_ranks
+
+
+def run_c5(args):
+    """C5 per GPU: 352 slots stream 64-token ticks (the chunked delta-rule path) with slot reset and reassignment
+    (c5_measure); a step is one tick of 352 x 64 tokens."""
+    import torch
+    rank, world, local = dist_env()
+    barrier, max_over_ranks = dist_setup(local, world)
+    from hs_guard_b200 import weights as W
+    from hs_guard_b200.build import build
+    from hs_guard_b200.engine import SlotEngine
+
     if rank == 0:
-        tokens = S * LB * world
-        value = tokens / (dev_ms * 1e-3)
-        achieved = gemm_flops / (gemm_ms * 1e-3) / 1e12
+        build()
+    if world > 1:
+        torch.distributed.barrier()
+    S = args.slots
+    sd = W.random_state_dict(0)
+    eng = SlotEngine(sd, S, state_dtype=args.state_dtype)
+    state_elem = 2 if args.state_dtype == "float16" else 4
+    lens = tuple(int(x) for x in args.contexts.split(","))
+    r = c5_measure(eng, S, args.steps, args.warmup, rank, world, lens, barrier, max_over_ranks, local, state_elem)
+    if rank == 0:
         line = {
-            "metric": "scored tokens/s/GPU at 352 slots (C5: 64-token ticks)", "value": value, "unit": "tokens/s",
-            "n_gpus": world, "steps": K, "warmup": Wm, "ms_per_step": dev_ms, "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None,
+            "metric": "scored tokens/s/GPU at 352 slots (C5: 64-token ticks)", "value": r["value"], "unit": "tokens/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": r["ms_per_step"],
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
             "dtype": f"f32 (norms, conv history, accumulation; {args.state_dtype} recurrent state; bf16 hi/lo "
                      "tensor-core operands; fp16 ring)",
             "data": "synthetic (uniform random token ids; random-init weights, seed 0)",
             "config": {"workload": "C5: 64-token ticks over 352 slots per GPU, contexts 512/2048/8000 (seed 5), "
                                    "slot reset and reassignment at the end of a conversation or after 4096 tokens",
-                       "slots_per_gpu": S, "tokens_per_tick": S * LB, "contexts": list(lens), "reassign_after": CAP,
-                       "resets_in_timed_ticks": n_resets, "parallelism": f"slot-sharded x{world}",
+                       "slots_per_gpu": S, "tokens_per_tick": S * 64, "contexts": list(lens), "reassign_after": 4096,
+                       "resets_in_timed_ticks": r["resets_in_timed_ticks"], "parallelism": f"slot-sharded x{world}",
                        "l2": "no flush: each tick touches > 10 GB (> 126 MB L2)"},
-            "latency_ms": {"p50": p50, "p95": p95, "device_per_step": dev_ms},
-            "e2e": {"value": tokens / (e2e_ms * 1e-3), "unit": "tokens/s",
-                    "h2d_bytes_per_step": (S * LB + 3 * S) * 8, "d2h_bytes_per_step": 2 * S * LB * 3 * 4 + 4},
-            "gpu_launches": launches * K,
-            "clocks": clk.summary(),
-            "roofline": {"kernel": "gemm_pc_kernel + gemm_tc_kernel (all projections of one tick)", "bound": "tensor",
-                         "achieved": achieved, "peak": tflops_peak, "unit": "TFLOP/s", "frac": achieved / tflops_peak,
-                         "peak_source": tsrc, "traffic": None, "algorithmic_flops": gemm_flops,
-                         "tick_ms": gemm_ms, "launches": gemm_n},
-            "gdn_chunk": {"kernel": "gdn_chunk_kernel", "avg_launch_ms": gdn_ms / max(gdn_n, 1),
-                          "algorithmic_bytes": gdn_bytes,
-                          "achieved_gbs": gdn_bytes / (gdn_ms / max(gdn_n, 1) * 1e-3) / 1e9,
-                          "hbm_frac": gdn_bytes / (gdn_ms / max(gdn_n, 1) * 1e-3) / 1e9 / hbm_peak,
-                          "peak_source": hsrc},
-            "kernel_ms_eager": {k: round(v[0], 4) for k, v in prof.items() if v[1]},
+            "latency_ms": r["latency_ms"], "e2e": r["e2e"], "gpu_launches": r["gpu_launches"], "clocks": r["clocks"],
+            "roofline": r["roofline"], "gdn_chunk": r["gdn_chunk"], "kernel_ms_eager": r["kernel_ms_eager"],
             "cpu_baseline": None,
         }
         print(json.dumps(line), flush=True)

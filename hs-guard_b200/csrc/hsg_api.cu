@@ -2,6 +2,7 @@
 // bucket, and the C ABI declared in include/hsg.h.
 #include <cudaTypedefs.h>
 
+#include <atomic>
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
@@ -1050,26 +1051,67 @@ static __device__ __align__(256) __nv_bfloat16 g_noalloc_operands[2 * (size_t)HS
 
 namespace {
 constexpr int kNoallocMaxDevices = 64;
-std::mutex g_noalloc_mu;
-__nv_bfloat16* g_noalloc_base[kNoallocMaxDevices];  // scratch address per device, looked up on first use
 
-// The current device's copy of the scratch area; the first call on a device resolves its address.
+// Per device: the CUDA context in which the scratch address was looked up and the GEMM kernels' shared-memory
+// attributes were set, and that address. A call compares the device's current context with the recorded one and
+// repeats the set-up when they differ (a cudaDeviceReset or a rebuilt primary context loads the module again, which
+// may move the scratch area and drops the attributes), so the address a kernel is given always belongs to the live
+// context. The fast path reads two atomics and takes no lock; the mutex only serialises the set-up itself.
+struct NoallocDevice {
+  std::atomic<void*> ctx{nullptr};
+  std::atomic<__nv_bfloat16*> base{nullptr};
+};
+NoallocDevice g_noalloc[kNoallocMaxDevices];
+std::mutex g_noalloc_mu;
+PFN_cuCtxGetCurrent_v4000 g_ctx_current = nullptr;
+
+int current_context(void** out) {
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &fn, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess && fn)
+      g_ctx_current = reinterpret_cast<PFN_cuCtxGetCurrent_v4000>(fn);
+  });
+  if (!g_ctx_current) return fail(HSG_ERR_CUDA, "cuCtxGetCurrent is unavailable");
+  CUcontext c = nullptr;
+  if (g_ctx_current(&c) != CUDA_SUCCESS || !c) return fail(HSG_ERR_CUDA, "no current CUDA context");
+  *out = c;
+  return HSG_OK;
+}
+
+// The current device's copy of the scratch area. The first call in a context sets the two GEMM kernels' dynamic
+// shared-memory limit and resolves the area's address with cudaGetSymbolAddress; that call may also be where the
+// CUDA runtime loads the library's device code (lazy module loading) and so places the area: the one call of this
+// entry point that can allocate.
 int noalloc_scratch(__nv_bfloat16** out) {
   int dev = 0;
   CU(cudaGetDevice(&dev));
   if (dev < 0 || dev >= kNoallocMaxDevices)
     return fail(HSG_ERR_UNSUPPORTED, "device ordinal %d is beyond the %d the scratch table covers", dev,
                 kNoallocMaxDevices);
+  int rc;
+  void* ctx = nullptr;
+  if ((rc = current_context(&ctx)) != HSG_OK) return rc;
+  NoallocDevice& d = g_noalloc[dev];
+  if (d.ctx.load(std::memory_order_acquire) == ctx) {
+    *out = d.base.load(std::memory_order_relaxed);
+    return HSG_OK;
+  }
   std::lock_guard<std::mutex> lock(g_noalloc_mu);
-  if (!g_noalloc_base[dev]) {
+  if (d.ctx.load(std::memory_order_acquire) != ctx) {
+    CU(cudaFuncSetAttribute(gemm_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_MAX));
+    CU(cudaFuncSetAttribute(gemm_pc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_MAX));
     void* p = nullptr;
     const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_operands);
     if (e != cudaSuccess || !p)
       return fail(HSG_ERR_CUDA, "cudaGetSymbolAddress of the GEMM scratch area failed on device %d: %s", dev,
                   cudaGetErrorString(e));
-    g_noalloc_base[dev] = static_cast<__nv_bfloat16*>(p);
+    d.base.store(static_cast<__nv_bfloat16*>(p), std::memory_order_relaxed);
+    d.ctx.store(ctx, std::memory_order_release);
   }
-  *out = g_noalloc_base[dev];
+  *out = d.base.load(std::memory_order_relaxed);
   return HSG_OK;
 }
 
@@ -1103,7 +1145,6 @@ extern "C" int hsg_gemm_f32_noalloc(const void* w, int n, int k, const float* x,
   if (mode != GEMM_SILU_MUL && !y) return fail(HSG_ERR_INVALID, "y is NULL");
   if (mode == GEMM_SILU_MUL && (!act_hi || !act_lo)) return fail(HSG_ERR_INVALID, "act_hi/act_lo are NULL");
   int rc;
-  if ((rc = set_kernel_attributes()) != HSG_OK) return rc;
   __nv_bfloat16* hi = nullptr;
   if ((rc = noalloc_scratch(&hi)) != HSG_OK) return rc;
   __nv_bfloat16* lo = hi + HSG_NOALLOC_MAX_ELEMS;

@@ -170,11 +170,14 @@ int hsg_gemm(const void* w, int n, int k, const void* x_hi, const void* x_lo, in
 
 /* hsg_gemm for fp32 activations x [m][k] (16-byte aligned) that allocates nothing: the bf16 (hi, lo) operand pair
  * is built in a fixed scratch area compiled into the library (HSG_NOALLOC_MAX_ELEMS elements of each half,
- * 8 MiB in all, one per device), then the same tensor-core GEMM runs on it. Other arguments and results are as in
- * hsg_gemm. m * k above HSG_NOALLOC_MAX_ELEMS is rejected with HSG_ERR_INVALID. The first call on a device looks
- * the scratch area up (cudaGetSymbolAddress); make it before capturing the stream into a graph. Calls on one
- * device share the scratch area: calls on the same stream are ordered, calls that overlap in time on different
- * streams race. No counterpart in the reference (its GEMMs allocate through PyTorch). */
+ * 8 MiB in all, one per device, held until the process exits), then the same tensor-core GEMM runs on it. Other
+ * arguments and results are as in hsg_gemm. m * k above HSG_NOALLOC_MAX_ELEMS is rejected with HSG_ERR_INVALID.
+ * The first call on a device (in each CUDA context of it) does a one-time set-up: it resolves the scratch area's
+ * address (cudaGetSymbolAddress) and sets the GEMM kernels' shared-memory limit. With lazy module loading that first
+ * call is also where the runtime may load the library's device code and place the area, so it is the one call that
+ * can allocate; make it before capturing the stream into a graph. Later calls allocate nothing. Calls on one device
+ * share the scratch area: calls on the same stream are ordered, calls that overlap in time on different streams
+ * race. No counterpart in the reference (its GEMMs allocate through PyTorch). */
 #define HSG_NOALLOC_MAX_ELEMS (1 << 21)
 int hsg_gemm_f32_noalloc(const void* w, int n, int k, const float* x, int m, float* y, void* act_hi, void* act_lo,
                          int mode, int splits, int* err, void* stream);

@@ -154,9 +154,11 @@ def test_gdn_step_padding_and_permuted_slots(L):
 
 
 def test_gdn_config2_size(L):
-    """16 slots x 16 heads, fp32 state N(0, 0.02), 100 consecutive single-token steps vs the oracle; then the same
-    tokens as one 64-token tick + 36 more must land on the same state (tick-size independence)."""
-    steps, n = 100, 16
+    """Config 2 in full: 16 slots x 16 heads, fp32 state N(0, 0.02), 1,000 consecutive single-token steps vs the
+    oracle (outputs at every step, final state within 1e-3 relative: ten times tighter than the 1e-2 state bound);
+    then the same tokens as 64-token ticks plus one 40-token tick must land on the same state (tick-size
+    independence)."""
+    steps, n = 1000, 16
     packed, a, b, state = gdn_raw(n, steps, 2)
     pool = torch.zeros(n + 1, 16, 128, 128, device="cuda")
     pool[:n] = state.cuda()
@@ -166,15 +168,19 @@ def test_gdn_config2_size(L):
     slots = np.arange(n)
     outs = []
     for t in range(steps):
-        outs.append(_gdn_gpu(L, packed[:, t:t + 1], a[:, t:t + 1], b[:, t:t + 1], pool, slots, [1] * n))
+        outs.append(_gdn_gpu(L, packed[:, t:t + 1], a[:, t:t + 1], b[:, t:t + 1], pool, slots, [1] * n).cpu())
     ref_o = K.gdn_slot_step(packed, a, b, torch.zeros(16), torch.zeros(16), ref_pool, torch.arange(n),
                             torch.full((n,), steps))
-    torch.testing.assert_close(torch.cat(outs, 1).cpu(), ref_o, rtol=2e-3, atol=2e-4)
-    rel = (pool.cpu() - ref_pool).norm() / ref_pool.norm()
-    assert rel < 1e-4, rel
-    _gdn_gpu(L, packed[:, :64], a[:, :64], b[:, :64], pool2, slots, [64] * n)
-    _gdn_gpu(L, packed[:, 64:], a[:, 64:], b[:, 64:], pool2, slots, [36] * n)
-    assert ((pool2 - pool).norm() / pool.norm()) < 1e-5
+    got = torch.cat(outs, 1)
+    print(f"config 2, 1000 steps: max |do| {float((got - ref_o).abs().max()):.3g}")
+    torch.testing.assert_close(got, ref_o, rtol=2e-3, atol=2e-4)
+    rel = float((pool.cpu() - ref_pool).norm() / ref_pool.norm())
+    print(f"config 2, 1000 steps: state relative error {rel:.3g}")
+    assert rel < 1e-3, rel
+    for t0 in range(0, steps, 64):
+        t1 = min(t0 + 64, steps)
+        _gdn_gpu(L, packed[:, t0:t1], a[:, t0:t1], b[:, t0:t1], pool2, slots, [t1 - t0] * n)
+    assert ((pool2 - pool).norm() / pool.norm()) < 1e-4
 
 
 def test_gdn_config2_size_fp16_state(L):

@@ -73,3 +73,26 @@ def test_stream_oracle_matches_reference_engine(golden, weights_seed0):
     # complete-message scores of slot 0's stream agree with the streamed ones (the reference's own invariant)
     cm = score_complete(sd, DEFAULT, [t for tick in stream_script() for s, ids in tick if s == 0 for t in ids])
     np.testing.assert_allclose(cm.numpy(), golden["cm_slot0_probs"], atol=5e-5)
+
+
+def test_long_golden_fixture(weights_seed0):
+    """tests/golden/golden_long.npz (the reference on the headline's context lengths, make_golden_long.py): lengths and
+    ring positions are the exact windows the script implies, the reference's own stream agrees with its
+    complete-message scores, and the oracle's complete-message scorer reproduces the reference's on the ragged
+    1,000-token slot."""
+    import os
+    from golden_inputs import LONG_CONTEXTS, LONG_STEPS, long_script, ring_positions
+    g = np.load(os.path.join(os.path.dirname(__file__), "golden", "golden_long.npz"))
+    assert W.state_dict_digest(weights_seed0) == str(g["weights_digest"])
+    lengths = np.asarray(LONG_CONTEXTS) + LONG_STEPS
+    np.testing.assert_array_equal(g["stream_length"], lengths)
+    for s, n in enumerate(lengths):
+        np.testing.assert_array_equal(g["stream_ring_pos"][s], ring_positions(int(n), 512))
+    assert (g["stream_ring_pos"][len(lengths)] == -1).all()
+    for r, role in enumerate(("user", "assistant")):
+        assert np.abs(g[f"stream_probs_{role}"] - g["cm_probs"][r]).max() < 1e-4
+    s = 3
+    ids = [t for tick in long_script() for slot, chunk in tick if slot == s for t in chunk]
+    off = int(np.sum(lengths[:s]))
+    cm = score_complete(weights_seed0, DEFAULT, ids)
+    np.testing.assert_allclose(cm.numpy(), g["cm_probs"][:, off:off + len(ids)], atol=5e-5)

@@ -63,14 +63,23 @@ def test_noalloc_gemm_matches_hsg_gemm(L, mode, m, n, k, splits):
     _sync_ok(err)
     ref = value(ref_out)
     scale = float(ref.abs().max())
+    x = (hi.float() + lo.float()).clone()
+    out = outputs()
+    y, ah, al = ptrs(out)
     for call in range(2):
-        # a fresh fp32 input each call, holding the same values, so the second call cannot reuse the first's split
-        x = (hi.float() + lo.float()).clone()
-        out = outputs()
-        y, ah, al = ptrs(out)
+        # the same fp32 values rewritten in place each call, so the second call cannot reuse the first's split
+        x.copy_(hi.float() + lo.float())
+        for t in out:
+            if t is not None:
+                t.zero_()
+        torch.cuda.synchronize()
+        free_before, held_before = torch.cuda.mem_get_info()[0], torch.cuda.memory_allocated()
         L.check(lib.hsg_gemm_f32_noalloc(w.data_ptr(), n, k, x.data_ptr(), m, y, ah, al, mode, splits,
                                          err.data_ptr(), None))
         _sync_ok(err)
+        if call == 1:  # the first call on a device may load the module; every later call allocates nothing
+            assert torch.cuda.mem_get_info()[0] == free_before, "device memory changed across the call"
+            assert torch.cuda.memory_allocated() == held_before
         diff = float((value(out) - ref).abs().max())
         assert diff <= 1e-5 * scale + 1e-6, f"call {call}: max |diff| {diff} (scale {scale})"
 
