@@ -50,6 +50,41 @@ def gdn_slot_step(packed, a, b, A_log, dt_bias, state, slots, lens, heads=16, he
     return o
 
 
+def gdn_chunked(q, k, v, g, beta, state, chunk=64):
+    """The gated delta rule over one sequence in its chunked (WY) form: the published algorithm behind FLA's
+    ``chunk_gated_delta_rule`` (chunk.py:29-114) and transformers' ``torch_chunk_gated_delta_rule``, which the
+    reference's complete-message path runs (runtime.py:78-89). Same result as the token-by-token recurrence.
+
+    q, k, v [T, H, D] (q, k already L2-normalised, q scaled), g, beta [T, H] (log decay <= 0, write strength),
+    state [H, D, D] (updated in place). Per chunk of C tokens with cumulative log decay gam (within the chunk):
+      A[t, s] = beta_t e^(gam_t - gam_s) k_t . k_s (s < t),   T = (I + A)^-1 (unit lower triangular solve),
+      Delta = T (beta v) - T (beta e^gam k) S,   O = (e^gam q) S + ([s <= t] e^(gam_t - gam_s) q_t . k_s) Delta,
+      S <- e^(gam_C) S + (e^(gam_C - gam) k)^T Delta.
+    Every exponent is <= 0. Returns o [T, H, D]."""
+    T, H, D = q.shape
+    out = torch.empty(T, H, D)
+    for c0 in range(0, T, chunk):
+        c1 = min(c0 + chunk, T)
+        n = c1 - c0
+        qc, kc, vc = (x[c0:c1].transpose(0, 1).float() for x in (q, k, v))       # [H, n, D]
+        gam = torch.cumsum(g[c0:c1].t().float(), -1)                             # [H, n]
+        bc = beta[c0:c1].t().float()
+        diff = gam[:, :, None] - gam[:, None, :]
+        lower = torch.ones(n, n, dtype=torch.bool).tril()
+        decay = torch.where(lower, torch.exp(torch.where(lower, diff, torch.zeros_like(diff))), torch.zeros_like(diff))
+        a = (bc[:, :, None] * (kc @ kc.transpose(-1, -2)) * decay).tril(-1)
+        eye = torch.eye(n).expand(H, n, n)
+        u = torch.linalg.solve_triangular(eye + a, bc[..., None] * vc, upper=False, unitriangular=True)
+        w = torch.linalg.solve_triangular(eye + a, (bc * torch.exp(gam))[..., None] * kc, upper=False,
+                                          unitriangular=True)
+        delta = u - w @ state
+        o = (qc * torch.exp(gam)[..., None]) @ state + ((qc @ kc.transpose(-1, -2)) * decay) @ delta
+        last = gam[:, -1:]
+        state.mul_(torch.exp(last)[..., None]).add_((kc * torch.exp(last - gam)[..., None]).transpose(-1, -2) @ delta)
+        out[c0:c1] = o.transpose(0, 1)
+    return out
+
+
 def causal_conv_step(qkv, pool, weight, slots, lens):
     """silu(causal depthwise conv, kernel K) over [K-1 saved rows | L new rows], then roll the history of rows
     with ``lens > 0`` (reference fused_kernels.py:94-136 without its bf16 roundings; bucketed_engine.py:94-98).

@@ -14,7 +14,7 @@ import numpy as np
 import torch
 import torch.nn.functional as F
 
-from .kernels import causal_conv_step, gdn_decay, l2norm
+from .kernels import causal_conv_step, gdn_chunked, gdn_decay, l2norm
 from .pack import pack_inputs
 
 SESSION_BUCKETS = (1, 2, 4, 8, 16, 32, 48, 64, 96, 128, 160, 192, 224, 256, 320, 352, 384, 448, 512)
@@ -265,14 +265,7 @@ def score_complete(sd, cfg, ids, window=512, w=None):
             k = l2norm(conv[:, kd:2 * kd].reshape(T, H, D))
             v = conv[:, 2 * kd:].reshape(T, H, D)
             beta, g = torch.sigmoid(b), gdn_decay(a, lay["A_log"], lay["dt_bias"])
-            state = torch.zeros(H, D, D)
-            out = torch.zeros(T, H, D)
-            for t in range(T):
-                state = state * torch.exp(g[t])[:, None, None]
-                kv = torch.einsum("hkv,hk->hv", state, k[t])
-                delta = beta[t][:, None] * (v[t] - kv)
-                state = state + k[t][:, :, None] * delta[:, None, :]
-                out[t] = torch.einsum("hkv,hk->hv", state, q[t])
+            out = gdn_chunked(q, k, v, g, beta, torch.zeros(H, D, D))
             mixed = F.linear(w.gated_norm(lay, out, z).reshape(T, H * D), lay["out_proj"])
         else:
             hq, hkv, d = cfg.attn_heads, cfg.kv_heads, cfg.attn_head_dim

@@ -96,3 +96,39 @@ def test_long_golden_fixture(weights_seed0):
     off = int(np.sum(lengths[:s]))
     cm = score_complete(weights_seed0, DEFAULT, ids)
     np.testing.assert_allclose(cm.numpy(), g["cm_probs"][:, off:off + len(ids)], atol=5e-5)
+
+
+def test_chunked_delta_rule_matches_recurrence_and_reference(golden):
+    """oracle.kernels.gdn_chunked (the chunked WY form of the reference's complete-message path) against the
+    reference's recurrent-rule golden vectors, and against the token-by-token recurrence on long inputs with ragged
+    chunks and strong decay (exponents far below the fp32 range must underflow to 0, not 0/0)."""
+    from oracle.kernels import gdn_chunked, l2norm
+    for name, n, L, seed in (("gdn_a", 3, 5, 21), ("gdn_b", 2, 1, 22)):
+        qr, kr, vr, g, beta, state = __import__("golden_inputs").gdn_inputs(n=n, L=L, seed=seed)
+        for row in range(n):
+            q = l2norm(qr[row]) * 128 ** -0.5
+            k = l2norm(kr[row])
+            st = state[row].clone()
+            o = gdn_chunked(q, k, vr[row], g[row], beta[row], st, chunk=4)
+            np.testing.assert_allclose(o.numpy(), golden[name + "_o"][row], rtol=1e-4, atol=1e-5)
+            np.testing.assert_allclose(st.pow(2).sum((-1, -2)).sqrt().numpy(), golden[name + "_state_norm"][row],
+                                       rtol=1e-5)
+    gen = torch.Generator().manual_seed(3)
+    T, H, D = 150, 2, 128
+    q = l2norm(torch.randn(T, H, D, generator=gen)) * D ** -0.5
+    k = l2norm(torch.randn(T, H, D, generator=gen))
+    v = torch.randn(T, H, D, generator=gen)
+    beta = torch.sigmoid(torch.randn(T, H, generator=gen))
+    for scale in (1.0, 40.0):
+        g = -torch.nn.functional.softplus(torch.randn(T, H, generator=gen)) * scale
+        s0 = torch.randn(H, D, D, generator=gen) * 0.02
+        st, ref = s0.clone(), torch.zeros(T, H, D)
+        for t in range(T):
+            st = st * torch.exp(g[t])[:, None, None]
+            st = st + k[t][:, :, None] * (beta[t][:, None] * (v[t] - torch.einsum("hkv,hk->hv", st, k[t])))[:, None]
+            ref[t] = torch.einsum("hkv,hk->hv", st, q[t])
+        s1 = s0.clone()
+        o = gdn_chunked(q, k, v, g, beta, s1, chunk=64)
+        assert torch.isfinite(o).all()
+        torch.testing.assert_close(o, ref, rtol=1e-4, atol=1e-5)
+        torch.testing.assert_close(s1, st, rtol=1e-4, atol=1e-6)
