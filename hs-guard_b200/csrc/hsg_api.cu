@@ -17,6 +17,7 @@
 #include "gdn.cuh"
 #include "gdn_tc.cuh"
 #include "gdn_chunk.cuh"
+#include "gdn_cols.cuh"
 #include "gemm.cuh"
 #include "gemm_persist.cuh"
 #include "norm.cuh"
@@ -940,7 +941,10 @@ int hsg_gdn_step(const void* packed, const float* a, const float* b, const float
   g.a_raw = a; g.b_raw = b; g.o_raw = o;
   g.A_log = A_log; g.dt_bias = dt_bias; g.state = state; g.err = err;
   const dim3 grid(GDN_H, std::min(n, GDN_CTAS_PER_HEAD));
-  if (state_dtype == HSG_STATE_F16 && lb <= GDNT_MAX_LB) {
+  if (state_dtype == HSG_STATE_F32 && n <= GDNS_MAX_ROWS) {
+    // a small fp32 batch: one CTA per 32-column slice of each (row, head) state, one wave
+    gdn_cols_kernel<float><<<dim3(GDNS_SLICES, GDN_H, n), GDNS_THREADS, 0, (cudaStream_t)stream>>>(g);
+  } else if (state_dtype == HSG_STATE_F16 && lb <= GDNT_MAX_LB) {
     GdntMaps maps;
     if ((rc = make_state_map(&maps.state, state, (int64_t)max_slots + 1)) != HSG_OK) return rc;
     if ((rc = make_map_3d(&maps.in0, packed, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, KEY_DIM, 3, (uint64_t)n * lb,

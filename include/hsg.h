@@ -148,7 +148,9 @@ int hsg_launches_per_step(const hsg_engine* eng, int nb, int lb);
 /* Gated-delta-rule slot step with the contract of the reference's gdn_slot_v8 (engine/fused_kernels.py:197-211):
  * packed [n][lb][6144] bf16 (q | k | v after conv+SiLU), a, b [n][lb][16] fp32 raw projections, A_log, dt_bias [16],
  * state [max_slots+1][16][128][128] (HSG_STATE_F32 or HSG_STATE_F16) updated in place at rows slots[i] with
- * lens[i] > 0; writes o [n][lb][16][128] fp32 (zeros at padded positions). All device pointers. */
+ * lens[i] > 0; writes o [n][lb][16][128] fp32 (zeros at padded positions). All device pointers. fp32 state with
+ * n <= 32 rows runs one CTA per 32-column slice of each (row, head) state (a small batch in one wave); other shapes
+ * the engine's persistent kernels. */
 int hsg_gdn_step(const void* packed, const float* a, const float* b, const float* A_log, const float* dt_bias,
                  void* state, int state_dtype, const int64_t* slots, const int64_t* lens, int n, int lb,
                  int max_slots, float* o, int* err, void* stream);

@@ -153,6 +153,26 @@ def test_gdn_step_padding_and_permuted_slots(L):
     assert torch.equal(gpu_pool[5].cpu(), pool[5]) and torch.equal(gpu_pool[2].cpu(), pool[2])
 
 
+def test_gdn_step_large_batch_fp32(L):
+    """More than 32 rows with fp32 state take the persistent kernel (smaller batches the column-slice kernel):
+    ragged lengths, a padding row and permuted slots against the oracle."""
+    n, lb = 40, 3
+    packed, a, b, state = gdn_raw(n, lb, 9)
+    S = n + 3
+    perm = np.random.default_rng(9).permutation(S)[:n]
+    lens = np.array([lb - (i % 3) for i in range(n)])
+    lens[7] = 0
+    perm[7] = S
+    pool = torch.randn(S + 1, 16, 128, 128) * 0.02
+    A_log, dt = torch.randn(16) * 0.5, torch.randn(16)
+    gpu_pool = pool.cuda()
+    o = _gdn_gpu(L, packed, a, b, gpu_pool, perm, lens, A_log, dt)
+    ref_pool = pool.clone()
+    ref = K.gdn_slot_step(packed, a, b, A_log, dt, ref_pool, torch.from_numpy(perm), torch.from_numpy(lens))
+    torch.testing.assert_close(o.cpu(), ref, rtol=1e-3, atol=1e-4)
+    torch.testing.assert_close(gpu_pool.cpu(), ref_pool, rtol=1e-4, atol=1e-6)
+
+
 def test_gdn_config2_size(L):
     """Config 2 in full: 16 slots x 16 heads, fp32 state N(0, 0.02), 1,000 consecutive single-token steps vs the
     oracle (outputs at every step, final state within 1e-3 relative: ten times tighter than the 1e-2 state bound);
