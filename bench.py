@@ -47,8 +47,9 @@ def parse():
     ap.add_argument("--contexts", default=",".join(map(str, CONTEXTS)))
     ap.add_argument("--cpu-slots", type=int, default=32)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", default="c4", choices=("c4", "c5"),
-                    help="c4: single-token steps after prefill (the headline); c5: 64-token ticks with reassignment")
+    ap.add_argument("--workload", default="c4", choices=("c4", "c5", "c2", "c3"),
+                    help="c4: single-token steps after prefill (the headline); c5: 64-token ticks with reassignment; "
+                         "c2 / c3: the isolated gated-delta-rule step / ring-window decode of configs 2 and 3")
     ap.add_argument("--state-dtype", default="float16", choices=("float16", "float32"),
                     help="recurrent-state storage (float16 = the reference StreamingGuard's)")
     return ap.parse_args()
@@ -226,6 +227,14 @@ def hbm_peak():
         return 6650.0, "fallback"
 
 
+def profile_traffic(key):
+    """DRAM bytes per launch of a kernel from the committed ncu summaries (profiles/traffic.json), or None."""
+    try:
+        return json.load(open(os.path.join(ROOT, "profiles", "traffic.json")))[key]["bytes_per_launch"]
+    except (OSError, ValueError, KeyError):
+        return None
+
+
 def bench_c2(lib, steps=1000, reps=5, cold_samples=50):
     """Config 2: the isolated gated-delta-rule step (hsg_gdn_step, fp32 state) on 16 slots x 16 heads, dk = dv = 128,
     state ~ N(0, 0.02), q/k/v bf16 ~ N(0, 1) (the kernel L2-normalises q and k per head), raw a, b ~ N(0, 1) with
@@ -289,8 +298,9 @@ def bench_c2(lib, steps=1000, reps=5, cold_samples=50):
                         f"{steps} consecutive steps in one CUDA graph, seed 2",
             "us_per_step_graph": graph_us, "us_per_step_cold": cold_us,
             "algorithmic_bytes_per_step": state_bytes + io_bytes,
-            "roofline": {"kernel": "gdn_step_kernel (fp32 state, isolated)", "bound": "hbm", "achieved": achieved,
+            "roofline": {"kernel": "gdn_cols_kernel (fp32 state, isolated)", "bound": "hbm", "achieved": achieved,
                          "peak": peak, "unit": "GB/s", "frac": achieved / peak, "peak_source": src,
+                         "traffic": profile_traffic("gdn_cols_c2"),
                          "timing": "median of single steps after an L2 flush"},
             "graph_gbs_l2_resident": (state_bytes + io_bytes) / (graph_us * 1e-6) / 1e9}
 
@@ -359,6 +369,7 @@ def bench_c3(lib, samples=50):
             "algorithmic_bytes_filled": filled_bytes, "bytes_full_window": window_bytes,
             "roofline": {"kernel": "ring_decode_kernel (isolated)", "bound": "hbm", "achieved": achieved, "peak": peak,
                          "unit": "GB/s", "frac": achieved / peak, "peak_source": src,
+                         "traffic": profile_traffic("ring_decode_c3"),
                          "timing": "median of calls after an L2 flush"},
             "full_window_frac": window_bytes / (us * 1e-6) / 1e9 / peak}
 
@@ -771,12 +782,34 @@ def run_c5(args):
         torch.distributed.destroy_process_group()
 
 
+def run_kernel_config(args):
+    """One JSON line for config 2 or 3 on cuda:0 (rank 0 only): the same measurement as the default line's c2 / c3."""
+    import torch
+    rank, _, local = dist_env()
+    if rank != 0:
+        return
+    torch.cuda.set_device(local)
+    from hs_guard_b200 import _lib
+    from hs_guard_b200.build import build
+    build()
+    r = (bench_c2 if args.workload == "c2" else bench_c3)(_lib.lib())
+    us = r["us_per_step_graph"] if args.workload == "c2" else r["us_per_call"]
+    line = {"metric": "us per step (config 2: gated-delta-rule step)" if args.workload == "c2"
+            else "us per call (config 3: ring-window decode)", "value": us, "unit": "us", "n_gpus": 1,
+            "higher_is_better": False, "dtype": "f32" if args.workload == "c2" else "f16 (fp32 softmax)",
+            "data": "synthetic", "config": {"workload": r["workload"]}, "vs_baseline": None}
+    line.update({k: v for k, v in r.items() if k != "workload"})
+    print(json.dumps(line), flush=True)
+
+
 def main():
     args = parse()
     if args.impl == "reference":
         run_reference(args)
     elif args.workload == "c5":
         run_c5(args)
+    elif args.workload in ("c2", "c3"):
+        run_kernel_config(args)
     else:
         run_ours(args)
 
