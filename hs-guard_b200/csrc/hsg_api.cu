@@ -18,6 +18,7 @@
 #include "gdn_tc.cuh"
 #include "gdn_chunk.cuh"
 #include "gdn_cols.cuh"
+#include "gdn_wy.cuh"
 #include "gemm.cuh"
 #include "gemm_persist.cuh"
 #include "norm.cuh"
@@ -190,6 +191,13 @@ static GemmPlan plan_gemm(int n_w, int K, int M, int mode, int use_lo) {
   return best;
 }
 
+// The chunked delta rule of 32/64-token ticks on tcgen05 (gdn_wy_kernel) when HSG_GDN_WY=1, else the warp-MMA
+// kernel (gdn_chunk_kernel).
+static bool use_wy_chunk() {
+  const char* s = getenv("HSG_GDN_WY");
+  return s && strcmp(s, "1") == 0;
+}
+
 // Kernel launch with the programmatic-stream-serialization attribute (programmatic dependent launch): the kernel may
 // begin while its predecessor drains; every kernel calls pdl_wait() before touching memory its predecessor uses.
 template <typename... KArgs, typename... Args>
@@ -305,6 +313,8 @@ static int set_kernel_attributes() {
   CU(cudaFuncSetAttribute(gdn_tc_kernel<false, 3>, cudaFuncAttributeMaxDynamicSharedMemorySize, GDN_SMEM_LIMIT));
   CU(cudaFuncSetAttribute(gdn_chunk_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, GDN_SMEM_LIMIT));
   CU(cudaFuncSetAttribute(gdn_chunk_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, GDN_SMEM_LIMIT));
+  CU(cudaFuncSetAttribute(gdn_wy_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, GDNW_SMEM));
+  CU(cudaFuncSetAttribute(gdn_wy_kernel<32>, cudaFuncAttributeMaxDynamicSharedMemorySize, GDNW_SMEM));
   CU(cudaFuncSetAttribute(ring_attn_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, attn_smem_bytes(4)));
   CU(cudaFuncSetAttribute(ring_attn_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, attn_smem_bytes(8)));
   CU(cudaFuncSetAttribute(ring_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, rd_smem_bytes()));
@@ -465,6 +475,18 @@ static int enqueue_step(hsg_engine* e, int nb, int lb) {
           else
             CU(launch_k(gdn_tc_kernel<true, 3>, grid, dim3(GDNT_THREADS), gdnt_smem_bytes(lb, true), st, e->pdl,
                         tc_maps, g));
+        } else if (chunked && use_wy_chunk()) {
+          GdntMaps wy;
+          wy.state = e->state_maps[gi];
+          wy.in0 = e->conv_maps[gi];
+          if ((rc = make_map_2d(&wy.in1, e->proj, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, M, GDN_IN, GDN_IN * 4, GDN_D,
+                                lb, CU_TENSOR_MAP_SWIZZLE_NONE)) != HSG_OK)
+            return rc;
+          wy.in2 = wy.in1;
+          if (lb == 64)
+            CU(launch_k(gdn_wy_kernel<64>, grid, dim3(GDNW_THREADS), GDNW_SMEM, st, e->pdl, wy, g));
+          else
+            CU(launch_k(gdn_wy_kernel<32>, grid, dim3(GDNW_THREADS), GDNW_SMEM, st, e->pdl, wy, g));
         } else if (chunked) {
           g.stages = gdnc_stages(lb, true);
           ch_maps.state = e->state_maps[gi];
