@@ -693,6 +693,10 @@ def c5_measure(eng, S, K, Wm, rank, world, lens, barrier, max_over_ranks, local,
     gemm_flops = 2.0 * 498_113_344 * S * LB  # algorithmic (the hi/lo activation pair executes twice this)
     gdn_ms, gdn_n = prof["gdn"]
     gdn_bytes = gdn_bytes_per_launch(S, LB, state_elem)
+    # the chunked delta rule of a 64-token tick: tcgen05 (default) or the warp-MMA comparison (HSG_GDN_WY=0)
+    wy = os.environ.get("HSG_GDN_WY", "1") != "0"
+    gdn_kernel = "gdn_wy_kernel (tcgen05)" if wy else "gdn_chunk_kernel (warp-level mma.sync)"
+    gdn_traffic = profile_traffic("gdn_wy_c5") if wy and S == 352 else None
     achieved = gemm_flops / (gemm_ms * 1e-3) / 1e12
     tokens = S * LB * world
     return {
@@ -707,8 +711,8 @@ def c5_measure(eng, S, K, Wm, rank, world, lens, barrier, max_over_ranks, local,
                      "achieved": achieved, "peak": tflops_peak, "unit": "TFLOP/s", "frac": achieved / tflops_peak,
                      "peak_source": tsrc, "traffic": None, "algorithmic_flops": gemm_flops,
                      "tick_ms": gemm_ms, "launches": gemm_n},
-        "gdn_chunk": {"kernel": "gdn_chunk_kernel", "avg_launch_ms": gdn_ms / max(gdn_n, 1),
-                      "algorithmic_bytes": gdn_bytes,
+        "gdn_chunk": {"kernel": gdn_kernel, "avg_launch_ms": gdn_ms / max(gdn_n, 1),
+                      "algorithmic_bytes": gdn_bytes, "traffic": gdn_traffic,
                       "achieved_gbs": gdn_bytes / (gdn_ms / max(gdn_n, 1) * 1e-3) / 1e9,
                       "hbm_frac": gdn_bytes / (gdn_ms / max(gdn_n, 1) * 1e-3) / 1e9 / hbm, "peak_source": hsrc},
         "kernel_ms_eager": {k: round(v[0], 4) for k, v in prof.items() if v[1]},

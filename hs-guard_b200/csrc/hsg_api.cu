@@ -191,11 +191,11 @@ static GemmPlan plan_gemm(int n_w, int K, int M, int mode, int use_lo) {
   return best;
 }
 
-// The chunked delta rule of 32/64-token ticks on tcgen05 (gdn_wy_kernel) when HSG_GDN_WY=1, else the warp-MMA
-// kernel (gdn_chunk_kernel).
+// The chunked delta rule of 32/64-token ticks runs on tcgen05 (gdn_wy_kernel); HSG_GDN_WY=0 selects the warp-MMA
+// kernel (gdn_chunk_kernel) instead, kept as the comparison.
 static bool use_wy_chunk() {
   const char* s = getenv("HSG_GDN_WY");
-  return s && strcmp(s, "1") == 0;
+  return !(s && strcmp(s, "0") == 0);
 }
 
 // Kernel launch with the programmatic-stream-serialization attribute (programmatic dependent launch): the kernel may
