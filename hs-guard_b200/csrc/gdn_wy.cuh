@@ -50,26 +50,28 @@ constexpr int GDNW_R_ST = GDNW_R_V + GDNW_MAXC * GDN_D * 4;   // S^T fp16 (two K
 constexpr int GDNW_R_KT = GDNW_R_ST + GDN_D * GDN_D * 2;      // K~^T hi | lo, [128 k][64 s] each
 constexpr int GDNW_R_HIST = GDNW_R_KT + 2 * GDN_D * 128;      // conv history [3][3][128] fp32
 constexpr int GDNW_A_STRIDE = GDNW_MAXC + 1;
+constexpr int GDNW_T_STRIDE = GDNW_MAXC + 4;  // rows of the fp32 inverse T (16-byte aligned)
 constexpr int GDNW_R_A = GDNW_R_HIST + 9 * GDN_D * 4;         // A [64][65] fp32 for the triangular solve
 // gam, Gam, beta, rk, rq, g, (Gam_C, gam_C), K~ scale [64] f32 each, the gated-norm weight [128]
 constexpr int GDNW_R_VEC = GDNW_R_A + GDNW_MAXC * GDNW_A_STRIDE * 4;
 constexpr int GDNW_R_PART = GDNW_R_VEC + (8 * GDNW_MAXC + GDN_D) * 4;  // per-token q.q, k.k partials [64][4][2] f32
-constexpr int GDNW_R_ONORM = GDNW_R_PART + GDNW_MAXC * 8 * 4; // output sums of squares [4 column groups][64] f32
-constexpr int GDNW_R_META = GDNW_R_ONORM + 4 * GDNW_MAXC * 4; // item metadata (slot, len) x 2, by item parity
+constexpr int GDNW_R_ONORM = GDNW_R_PART;                     // later: output sums of squares [8 column groups][64]
+constexpr int GDNW_R_META = GDNW_R_PART + GDNW_MAXC * 8 * 4;  // item metadata (slot, len) x 2, by item parity
 constexpr int GDNW_R_CW = GDNW_R_META + 32;                   // this head's conv taps [3 parts][128] float4
 constexpr int GDNW_R_BAR = GDNW_R_CW + 3 * GDN_D * 16;        // mbarriers
 constexpr int GDNW_NBAR = 14;
 constexpr int GDNW_SMEM = GDNW_R_BAR + GDNW_NBAR * 8 + 16 + 1024;
-// Mqk hi | lo (rows t, K = s) inside the q region after T hi | lo; the O product addresses it 64 rows early so that
-// its rows land in TMEM lanes 64 + t, beside R'.
-constexpr int GDNW_MQK = 16384;
 // TMEM column offsets
 constexpr int GDNW_COL_KQ = 0;    // KK in lanes 0 .. C - 1, QK in lanes 64 .. 64 + C - 1 (the stacked operand x K^)
 constexpr int GDNW_COL_P = 64;    // P = S^T K^T, lanes v
 constexpr int GDNW_COL_U = 128;   // U^T, lanes v
+constexpr int GDNW_COL_R2 = 192;  // R' = Q^ S for v < 64 in lanes t (the stacked operand read from row 64)
 constexpr int GDNW_COL_DS = 0;    // dS, lanes k, 128 columns v (written after KK, QK, P, U^T have been read)
-constexpr int GDNW_COL_O = 256;   // O, lanes 64 + t, 128 columns v
-constexpr int GDNW_COL_R = 384;   // [K^; Q^] S: R' = Q^ S in lanes 64 + t, 128 columns v
+constexpr int GDNW_COL_O = 256;   // O for v < 64 in lanes t, then O for v >= 64 in lanes 64 + t (64 columns each)
+constexpr int GDNW_COL_R = 384;   // [K^; Q^] S for v >= 64: R' = Q^ S in lanes 64 + t, 64 columns
+// Mqk hi | lo (rows t, K = s) inside the q region after T hi | lo. The O product for v >= 64 addresses it 64 rows
+// early so that its rows land in TMEM lanes 64 + t, beside R'.
+constexpr int GDNW_MQK = 16384;
 
 // Byte offset of element (row r, K index k) in a K-major SW128 operand whose K blocks of 64 are `kblock` bytes apart.
 __device__ __forceinline__ uint32_t kmaj_off(int r, int k, int kblock) {
@@ -91,6 +93,24 @@ __device__ __forceinline__ void split8(const float (&x)[8], uint4& hi, uint4& lo
   split_half2x(x[4], x[5], hi.z, lo.z);
   split_half2x(x[6], x[7], hi.w, lo.w);
 }
+// Two 32-lane x 16-column TMEM loads with one wait (tmem_ld16 waits after each).
+__device__ __forceinline__ void tmem_ld16x2(uint32_t ta, float (&a)[16], uint32_t tb, float (&b)[16]) {
+  uint32_t r[32];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%32];\n\t"
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%33];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(ta), "r"(tb));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    a[i] = __uint_as_float(r[i]);
+    b[i] = __uint_as_float(r[16 + i]);
+  }
+}
 // 8 fp32 values as bf16 (hi, lo) pairs packed into two 16-byte chunks
 __device__ __forceinline__ void split8_bf16(const float (&x)[8], uint4& hi, uint4& lo) {
   uint32_t* h = reinterpret_cast<uint32_t*>(&hi);
@@ -101,6 +121,25 @@ __device__ __forceinline__ void split8_bf16(const float (&x)[8], uint4& hi, uint
     split_bf16x2(x[2 * j], x[2 * j + 1], a, b);
     h[j] = *reinterpret_cast<uint32_t*>(&a);
     l[j] = *reinterpret_cast<uint32_t*>(&b);
+  }
+}
+
+// Causal conv (4 taps) + SiLU of 16 consecutive tokens of one channel, in place (rows GDN_D floats apart); w = the
+// three raw inputs before the first token; sq = the squared outputs. FULL: all 16 tokens are valid (no masking).
+template <bool FULL>
+__device__ __forceinline__ void wy_conv16(float* xc, float4 c, const float (&w)[3], int tb, int len, float (&sq)[16]) {
+  float in[19];
+  in[0] = w[0];
+  in[1] = w[1];
+  in[2] = w[2];
+#pragma unroll
+  for (int u = 0; u < 16; ++u) in[3 + u] = xc[(tb + u) * GDN_D];
+#pragma unroll
+  for (int u = 0; u < 16; ++u) {
+    const float y = silu_fast(fmaf(c.w, in[u + 3], fmaf(c.z, in[u + 2], fmaf(c.y, in[u + 1], c.x * in[u]))));
+    const float o = FULL || tb + u < len ? y : 0.f;
+    xc[(tb + u) * GDN_D] = o;
+    sq[u] = o * o;
   }
 }
 
@@ -262,11 +301,11 @@ gdn_wy_kernel(const __grid_constant__ GdntMaps maps, const GdnArgs args) {
   } else if (warp == GDNW_MMA_WARP) {
     // ===================================== MMA issuer =====================================
     if (lane == 0) {
-      const uint32_t id_c = idesc_f16(128, C), id_128 = idesc_f16(128, 128);
+      const uint32_t id_c = idesc_f16(128, C), id_128 = idesc_f16(128, 128), id_c64 = idesc_f16(128, 64);
       const uint32_t sm = smem_u32(smem);
       const uint32_t kq_hi = sm + GDNW_R_Q, kq_lo = sm + GDNW_R_K, st = sm + GDNW_R_ST;  // K blocks 16 KB apart
       const uint32_t t_hi = sm + GDNW_R_Q, t_lo = t_hi + C * 128;
-      const uint32_t m_hi = sm + GDNW_R_Q + GDNW_MQK - 64 * 128, m_lo = m_hi + 64 * 128;  // 64 rows early: lanes 64+
+      const uint32_t m_hi = sm + GDNW_R_Q + GDNW_MQK, m_lo = m_hi + 64 * 128;
       const uint32_t x_hi = st, x_lo = st + 128 * 128, u_hi = kq_lo, u_lo = kq_lo + 128 * 128;
       const uint32_t kt_hi = sm + GDNW_R_KT, kt_lo = kt_hi + 128 * 128;
       auto mma = [&](int col, uint32_t a, uint32_t b, int kstride_a, int kstride_b, int ksteps, uint32_t idesc,
@@ -295,8 +334,12 @@ gdn_wy_kernel(const __grid_constant__ GdntMaps maps, const GdnArgs args) {
         tc_fence_after();
         mma(GDNW_COL_P, st, kq_hi, KB, KB, 8, id_c, true);
         mma(GDNW_COL_P, st, kq_lo, KB, KB, 8, id_c, false);
-        mma(GDNW_COL_R, kq_hi, st, KB, KB, 8, id_128, true);
-        mma(GDNW_COL_R, kq_lo, st, KB, KB, 8, id_128, false);
+        mma(GDNW_COL_R, kq_hi, st + 64 * 128, KB, KB, 8, id_c64, true);  // B = S^T rows v >= 64
+        mma(GDNW_COL_R, kq_lo, st + 64 * 128, KB, KB, 8, id_c64, false);
+        // Q^ S again for v < 64 with the A rows read from row 64 (Q^ into lanes 0 .. 63; lanes 64 .. see the rows
+        // after it, unused): the outputs of v < 64 are formed by the warps of lane quadrants 0 and 1
+        mma(GDNW_COL_R2, kq_hi + 64 * 128, st, KB, KB, 8, id_c64, true);
+        mma(GDNW_COL_R2, kq_lo + 64 * 128, st, KB, KB, 8, id_c64, false);
         mma_commit(mma3s);
         // step 6: U^T = X T^T
         if (!mbar_wait(ops6, ph, args.err, ERR_TIMEOUT_MMA)) { ok = false; break; }
@@ -308,9 +351,13 @@ gdn_wy_kernel(const __grid_constant__ GdntMaps maps, const GdnArgs args) {
         // step 8: O = Mqk U (lanes 64 + t), dS = K~^T U (lanes k); B = the U^T operand (rows v, K = s)
         if (!mbar_wait(ops8, ph, args.err, ERR_TIMEOUT_MMA)) { ok = false; break; }
         tc_fence_after();
-        mma(GDNW_COL_O, m_hi, u_hi, 0, 0, C / 16, id_128, true);
-        mma(GDNW_COL_O, m_hi, u_lo, 0, 0, C / 16, id_128, false);
-        mma(GDNW_COL_O, m_lo, u_hi, 0, 0, C / 16, id_128, false);
+        // O for v < 64 (Mqk from row 0: lanes t) and for v >= 64 (Mqk addressed 64 rows early: lanes 64 + t)
+        mma(GDNW_COL_O, m_hi, u_hi, 0, 0, C / 16, id_c64, true);
+        mma(GDNW_COL_O, m_hi, u_lo, 0, 0, C / 16, id_c64, false);
+        mma(GDNW_COL_O, m_lo, u_hi, 0, 0, C / 16, id_c64, false);
+        mma(GDNW_COL_O + 64, m_hi - 64 * 128, u_hi + 64 * 128, 0, 0, C / 16, id_c64, true);
+        mma(GDNW_COL_O + 64, m_hi - 64 * 128, u_lo + 64 * 128, 0, 0, C / 16, id_c64, false);
+        mma(GDNW_COL_O + 64, m_lo - 64 * 128, u_hi + 64 * 128, 0, 0, C / 16, id_c64, false);
         mma_commit(mma8);  // the outputs can start while dS is computed
         mma(GDNW_COL_DS, kt_hi, u_hi, 0, 0, C / 16, id_128, true);
         mma(GDNW_COL_DS, kt_hi, u_lo, 0, 0, C / 16, id_128, false);
@@ -328,10 +375,13 @@ gdn_wy_kernel(const __grid_constant__ GdntMaps maps, const GdnArgs args) {
     const int cc = cg * 32 + lane, tq = quad;
     const float negA = -expf(args.A_log[h]), dtb = args.dt_bias[h];
     const int vrow = quad * 32 + lane;  // this thread's TMEM lane: v (P, U^T), k (dS), 64 + t (O, R')
-    // output rows: quadrants 2 .. 2 + C / 32 - 1 hold token ot in lanes 64 + ot; NOUT threads take part
-    constexpr int NOUT = 4 * C;
-    const bool out_warp = quad >= 2 && quad - 2 < C / 32;
-    const int ot = (quad - 2) * 32 + lane;
+    // outputs: token ot = 32 (quad & 1) + lane in lanes ot (quadrants 0, 1: v < 64) and 64 + ot (quadrants 2, 3:
+    // v >= 64); warp (quad, cg) forms the 16 columns ov0 .. ov0 + 15. NOUT threads take part.
+    constexpr int NOUT = 8 * C;
+    const bool out_warp = (quad & 1) < C / 32;
+    const int ot = (quad & 1) * 32 + lane, ov0 = (quad >> 1) * 64 + cg * 16;
+    const int col_o = GDNW_COL_O + ov0;                                      // this warp's O columns
+    const int col_rr = quad < 2 ? GDNW_COL_R2 + cg * 16 : GDNW_COL_R + cg * 16;  // and R' columns
     int seq = 0;
     bool ok = true;
     if (n_items > 0) pdl_wait();  // z and the gates come from the preceding GEMM; outputs may still be read
@@ -366,33 +416,40 @@ gdn_wy_kernel(const __grid_constant__ GdntMaps maps, const GdnArgs args) {
       if (16 * tq < C) {
         // the q, k, v regions are consecutive: channel part c3's inputs start at xq + c3 * (64 x 128)
         constexpr int XPART = GDNW_MAXC * GDN_D;
+        auto raw = [&](int c3, int t) {  // raw input t of this channel (t < 0: the conv history)
+          return t >= 0 ? xq[c3 * XPART + t * GDN_D + cc] : hist[((t + 3) * 3 + c3) * GDN_D + cc];
+        };
         float w3[3][3];
 #pragma unroll
         for (int c3 = 0; c3 < 3; ++c3)
 #pragma unroll
-          for (int j = 0; j < 3; ++j)
-            w3[c3][j] = tq == 0 ? hist[(j * 3 + c3) * GDN_D + cc] : xq[c3 * XPART + (16 * tq - 3 + j) * GDN_D + cc];
-        named_sync_id<2, 4 * C * 2>();  // every raw history value read before the in-place conv overwrites it
-        const bool last_here = ((len - 1) >> 4) == tq;  // this quarter holds the last token: write the history
+          for (int j = 0; j < 3; ++j) w3[c3][j] = raw(c3, 16 * tq - 3 + j);
+        if (((len - 1) >> 4) == tq) {
+          // this quarter holds the last token: the new history (the last three raw inputs) goes to the pool
+#pragma unroll
+          for (int c3 = 0; c3 < 3; ++c3) {
+            float* gp = args.conv_pool + (size_t)slot * CONV_KEEP * CONV_DIM + c3 * KEY_DIM + h * GDN_D + cc;
+#pragma unroll
+            for (int j = 0; j < 3; ++j) gp[j * CONV_DIM] = raw(c3, len - 3 + j);
+          }
+        }
+        named_sync_id<2, 4 * C * 2>();  // every raw value read before the in-place conv overwrites it
+        const bool full = len >= 16 * tq + 16;
 #pragma unroll 1
         for (int c3 = 0; c3 < 3; ++c3) {
           // selects, not indexing: a register array indexed by the (not unrolled) loop would go to local memory
           const float4 cw = cws[c3 * GDN_D + cc];
-          float wv[3], hh[3] = {0.f, 0.f, 0.f}, sq[16];
+          float wv[3], sq[16];
 #pragma unroll
           for (int j = 0; j < 3; ++j) wv[j] = c3 == 0 ? w3[0][j] : (c3 == 1 ? w3[1][j] : w3[2][j]);
-          conv_block16(xq + c3 * XPART + cc, GDN_D, cw, wv, 16 * tq, len, hh, sq);
+          if (full)
+            wy_conv16<true>(xq + c3 * XPART + cc, cw, wv, 16 * tq, len, sq);
+          else
+            wy_conv16<false>(xq + c3 * XPART + cc, cw, wv, 16 * tq, len, sq);
           if (c3 < 2) {
             const float tot = reduce16(sq, lane);
             if (!(lane & 1)) part[((16 * tq + reduce16_index(lane)) * 4 + cg) * 2 + c3] = tot;
           }
-          if (last_here) {
-            float* gp = args.conv_pool + (size_t)slot * CONV_KEEP * CONV_DIM + c3 * KEY_DIM + h * GDN_D + cc;
-            gp[0] = hh[0];
-            gp[CONV_DIM] = hh[1];
-            gp[2 * CONV_DIM] = hh[2];
-          }
-          asm volatile("" ::: "memory");  // one channel at a time: interleaving the three spills registers
         }
       }
       if (tid < C) {
@@ -527,42 +584,46 @@ gdn_wy_kernel(const __grid_constant__ GdntMaps maps, const GdnArgs args) {
       {
         // Warp (quad, cg) takes the 16 columns [16 cg, 16 cg + 16) of the C (none when 16 cg >= C). Token row t of KK
         // (lanes 0 ..): A[t][s] = beta_t e^(gam_t - gam_s) KK[t][s] (s < t) to amat while P and R' are computed; of
-        // QK (lanes 64 ..): Mqk[t][s] = e^(gam_t - gam_s) QK[t][s] (s <= t) once they are, since its place in the q
-        // region is read by those MMAs (QK stays in TMEM meanwhile).
+        // QK (lanes 64 ..): Mqk[t][s] = e^(gam_t - gam_s) QK[t][s] (s <= t) meanwhile into registers, stored once
+        // those MMAs (which read its place in the q region) are done.
         const bool kk_rows = quad < C / 32, qk_rows = quad >= 2 && quad - 2 < C / 32;
         const int c0 = cg * 16;
         const int t = (kk_rows ? quad : quad - 2) * 32 + lane;
-        if (kk_rows && c0 < C) {
-          const float gt = vgam[t], bt = vbeta[t];
+        uint4 mhi[2], mlo[2];
+        if ((kk_rows || qk_rows) && c0 < C) {
+          const float gt = vgam[t];
           float d16[16];
           tmem_ld16(lane_base + (uint32_t)(GDNW_COL_KQ + c0), d16);
+          if (kk_rows) {
+            const float bt = vbeta[t];
 #pragma unroll
-          for (int e = 0; e < 16; ++e) {
-            const int sx = c0 + e;
-            amat[t * GDNW_A_STRIDE + sx] = sx < t ? bt * __expf(gt - vgam[sx]) * d16[e] : 0.f;
+            for (int e = 0; e < 16; ++e) {
+              const int sx = c0 + e;
+              amat[t * GDNW_A_STRIDE + sx] = sx < t ? bt * __expf(gt - vgam[sx]) * d16[e] : 0.f;
+            }
+          } else {
+#pragma unroll
+            for (int e8 = 0; e8 < 2; ++e8) {
+              float mv[8];
+#pragma unroll
+              for (int e = 0; e < 8; ++e) {
+                const int sx = c0 + 8 * e8 + e;
+                mv[e] = sx <= t ? __expf(gt - vgam[sx]) * d16[8 * e8 + e] : 0.f;
+              }
+              split8(mv, mhi[e8], mlo[e8]);
+            }
           }
         }
         ok = named_sync_and_id<1, GDNW_COMPUTE>(mbar_wait(mma3s, ph, args.err, ERR_TIMEOUT_MMA));
         if (!ok) break;
         tc_fence_after();
         if (qk_rows && c0 < C) {
-          const float gt = vgam[t];
-          float d16[16];
-          tmem_ld16(lane_base + (uint32_t)(GDNW_COL_KQ + c0), d16);
           uint8_t* mop = smem + GDNW_R_Q + GDNW_MQK;  // Mqk hi | lo (rows t, K = s)
 #pragma unroll
           for (int e8 = 0; e8 < 2; ++e8) {
-            float mv[8];
-#pragma unroll
-            for (int e = 0; e < 8; ++e) {
-              const int sx = c0 + 8 * e8 + e;
-              mv[e] = sx <= t ? __expf(gt - vgam[sx]) * d16[8 * e8 + e] : 0.f;
-            }
-            uint4 hi, lo;
-            split8(mv, hi, lo);
             const uint32_t off = kmaj_off(t, c0 + 8 * e8, 0);
-            *reinterpret_cast<uint4*>(mop + off) = hi;
-            *reinterpret_cast<uint4*>(mop + 64 * 128 + off) = lo;
+            *reinterpret_cast<uint4*>(mop + off) = mhi[e8];
+            *reinterpret_cast<uint4*>(mop + 64 * 128 + off) = mlo[e8];
           }
         }
         // X[v][t] = beta_t (v_t[v] - Gam_t P[v][t]) as hi|lo, rows v, K = t (into the S^T region: its MMAs are done)
@@ -588,12 +649,16 @@ gdn_wy_kernel(const __grid_constant__ GdntMaps maps, const GdnArgs args) {
       }
       named_sync_id<1, GDNW_COMPUTE>();  // A complete; v read for the last time (its region holds T below)
       {
-        // Blocked inverse of the unit lower triangular I + A in 16 x 16 blocks (fp32, into tf = the v region):
-        // diagonal blocks by forward substitution (thread = one column of one block), then block rows below the
-        // diagonal level by level: W_ij = sum_{j <= m < i} A_im T_mj, T_ij = -T_ii W_ij.
-        constexpr int NB = C / 16;
-        float* tf = xv;                                // [64][65]
-        float* wbuf = tf + GDNW_MAXC * GDNW_A_STRIDE;  // [NB - 1 blocks][16][17]
+        // Blocked inverse of the unit lower triangular I + A in 16 x 16 blocks (fp32, into tf = the v region, rows
+        // 68 floats apart so a thread reads four consecutive columns with one 16-byte load): the diagonal blocks
+        // T_ii by forward substitution (thread = one column of one block; the entries above the diagonal come out 0),
+        // then A~_im = T_ii A_im for every block below the diagonal at once, then the block rows level by level,
+        // T_ij = -sum_{j <= m < i} A~_im T_mj (each thread four columns of one row). The blocks above the diagonal
+        // are never formed (masked below).
+        constexpr int NB = C / 16, TS = GDNW_T_STRIDE, AS = 17;
+        constexpr int NOFF = NB * (NB - 1) / 2;  // blocks below the diagonal: (i, m) -> i (i - 1) / 2 + m
+        float* tf = xv;                     // [64][68]
+        float* at = tf + GDNW_MAXC * TS;    // A~ [NOFF][16][17]
         if (tid < C) {
           const int b = tid >> 4, j = tid & 15, base = b * 16;
           float col[16];
@@ -605,48 +670,68 @@ gdn_wy_kernel(const __grid_constant__ GdntMaps maps, const GdnArgs args) {
             col[tt] = acc;
           }
 #pragma unroll
-          for (int tt = 0; tt < 16; ++tt) tf[(base + tt) * GDNW_A_STRIDE + base + j] = col[tt];
-        } else {
-          // zero the blocks above the diagonal (T is lower triangular)
-          for (int e = tid - C; e < C * C; e += GDNW_COMPUTE - C) {
-            const int tt = e / C, sx = e % C;
-            if ((sx >> 4) > (tt >> 4)) tf[tt * GDNW_A_STRIDE + sx] = 0.f;
+          for (int tt = 0; tt < 16; ++tt) tf[(base + tt) * TS + base + j] = col[tt];
+        }
+        named_sync_id<1, GDNW_COMPUTE>();
+        if (tid < NOFF * 64) {
+          // A~_im[r][c4 ..] = sum_{x <= r} T_ii[r][x] A_im[x][c4 ..]
+          const int blk = tid >> 6, r = (tid >> 2) & 15, c4 = (tid & 3) * 4;
+          const int bi = blk == 0 ? 1 : (blk < 3 ? 2 : 3), m = blk - bi * (bi - 1) / 2;
+          float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+#pragma unroll
+          for (int x = 0; x < 16; ++x) {
+            const float tv = tf[(bi * 16 + r) * TS + bi * 16 + x];
+            const float* ar = amat + (bi * 16 + x) * GDNW_A_STRIDE + m * 16 + c4;
+            a0 = fmaf(tv, ar[0], a0);
+            a1 = fmaf(tv, ar[1], a1);
+            a2 = fmaf(tv, ar[2], a2);
+            a3 = fmaf(tv, ar[3], a3);
           }
+          float* o = at + (blk * 16 + r) * AS + c4;
+          o[0] = a0;
+          o[1] = a1;
+          o[2] = a2;
+          o[3] = a3;
         }
         named_sync_id<1, GDNW_COMPUTE>();
 #pragma unroll 1
         for (int d = 1; d < NB; ++d) {
-          const int nblk = NB - d;  // blocks (i, j = i - d)
-          for (int e = tid; e < nblk * 256; e += GDNW_COMPUTE) {
-            const int q = e >> 8, r = (e >> 4) & 15, c = e & 15, bi = q + d, bj = q;
-            float acc = 0.f;
+          const int nblk = NB - d;  // blocks (i, j = i - d); task: block tid >> 6, row (tid >> 2) & 15, columns 4 (tid & 3)
+          if (tid < nblk * 64) {
+            const int q = tid >> 6, r = (tid >> 2) & 15, c4 = (tid & 3) * 4, bi = q + d, bj = q;
+            float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll 1
             for (int m = bj; m < bi; ++m) {
+              const float* ar = at + ((bi * (bi - 1) / 2 + m) * 16 + r) * AS;
 #pragma unroll
-              for (int x = 0; x < 16; ++x)
-                acc = fmaf(amat[(bi * 16 + r) * GDNW_A_STRIDE + m * 16 + x], tf[(m * 16 + x) * GDNW_A_STRIDE + bj * 16 + c],
-                           acc);
+              for (int x = 0; x < 16; ++x) {
+                const float a = ar[x];
+                const float4 t4 = *reinterpret_cast<const float4*>(tf + (m * 16 + x) * TS + bj * 16 + c4);
+                acc.x = fmaf(a, t4.x, acc.x);
+                acc.y = fmaf(a, t4.y, acc.y);
+                acc.z = fmaf(a, t4.z, acc.z);
+                acc.w = fmaf(a, t4.w, acc.w);
+              }
             }
-            wbuf[(q * 16 + r) * 17 + c] = acc;
-          }
-          named_sync_id<1, GDNW_COMPUTE>();
-          for (int e = tid; e < nblk * 256; e += GDNW_COMPUTE) {
-            const int q = e >> 8, r = (e >> 4) & 15, c = e & 15, bi = q + d, bj = q;
-            float acc = 0.f;
-#pragma unroll
-            for (int x = 0; x < 16; ++x)
-              acc = fmaf(tf[(bi * 16 + r) * GDNW_A_STRIDE + bi * 16 + x], wbuf[(q * 16 + x) * 17 + c], acc);
-            tf[(bi * 16 + r) * GDNW_A_STRIDE + bj * 16 + c] = -acc;
+            *reinterpret_cast<float4*>(tf + (bi * 16 + r) * TS + bj * 16 + c4) =
+                make_float4(-acc.x, -acc.y, -acc.z, -acc.w);
           }
           named_sync_id<1, GDNW_COMPUTE>();
         }
-        // T as hi|lo operand: rows t, K = s, 16-byte chunks of 8 s
+        // T as hi|lo operand: rows t, K = s, 16-byte chunks of 8 s (zero above the diagonal blocks)
         uint8_t* top = smem + GDNW_R_Q;
         for (int e = tid; e < C * (C / 8); e += GDNW_COMPUTE) {
           const int tt = e / (C / 8), s0 = (e % (C / 8)) * 8;
           float tv[8];
+          if ((s0 >> 4) > (tt >> 4)) {
 #pragma unroll
-          for (int x = 0; x < 8; ++x) tv[x] = tf[tt * GDNW_A_STRIDE + s0 + x];
+            for (int x = 0; x < 8; ++x) tv[x] = 0.f;
+          } else {
+            const float4 a = *reinterpret_cast<const float4*>(tf + tt * TS + s0);
+            const float4 b = *reinterpret_cast<const float4*>(tf + tt * TS + s0 + 4);
+            tv[0] = a.x; tv[1] = a.y; tv[2] = a.z; tv[3] = a.w;
+            tv[4] = b.x; tv[5] = b.y; tv[6] = b.z; tv[7] = b.w;
+          }
           uint4 hi, lo;
           split8(tv, hi, lo);
           const uint32_t off = kmaj_off(tt, s0, 0);
@@ -684,66 +769,50 @@ gdn_wy_kernel(const __grid_constant__ GdntMaps maps, const GdnArgs args) {
       tc_fence_before();
       named_sync_id<1, GDNW_COMPUTE>();
       mbar_arrive(ops8);
-      // the output rows' z (prefetched to L2 with the inputs): the first 16 columns while the last MMAs run, the
-      // other 16 during the sums of squares
-      const float4* zr = reinterpret_cast<const float4*>(args.proj + ((size_t)n * lb + ot) * GDN_IN + GDN_Z_OFF +
-                                                         h * GDN_D + cg * 32);
-      float4 za[4], zb[4];
+      // the output rows' z (prefetched to L2 with the inputs) while the last MMAs run
+      float4 z4[4];
       if (out_warp) {
+        const float4* zr = reinterpret_cast<const float4*>(args.proj + ((size_t)n * lb + ot) * GDN_IN + GDN_Z_OFF +
+                                                           h * GDN_D + ov0);
 #pragma unroll
-        for (int j = 0; j < 4; ++j) za[j] = ot < len ? zr[j] : make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int j = 0; j < 4; ++j) z4[j] = ot < len ? zr[j] : make_float4(0.f, 0.f, 0.f, 0.f);
       }
       // ---- F: outputs (gated RMSNorm of o_t over v) and the new state ----
       ok = named_sync_and_id<1, GDNW_COMPUTE>(mbar_wait(mma8, ph, args.err, ERR_TIMEOUT_MMA));
       if (!ok) break;
       tc_fence_after();
       if (out_warp) {
-        // token ot, v in [32 cg, 32 cg + 32): o = Gam_t R' + O. First the sums of squares (the four column groups'
-        // meet in onorm), then the outputs from a second read of O and R' (TMEM reads are cheap; registers are not)
+        // token ot, v in [ov0, ov0 + 16): o = Gam_t R' + O; the eight column groups' sums of squares meet in onorm
+        float ov[16], rv[16];
+        tmem_ld16x2(lane_base + (uint32_t)col_o, ov, lane_base + (uint32_t)col_rr, rv);
         const float gt = vGam[ot];
         float ss = 0.f;
 #pragma unroll
-        for (int c16 = 0; c16 < 32; c16 += 16) {
-          float ov[16], rv[16];
-          tmem_ld16(lane_base + (uint32_t)(GDNW_COL_O + cg * 32 + c16), ov);
-          tmem_ld16(lane_base + (uint32_t)(GDNW_COL_R + cg * 32 + c16), rv);
-#pragma unroll
-          for (int e = 0; e < 16; ++e) {
-            const float o = fmaf(gt, rv[e], ov[e]);
-            ss = fmaf(o, o, ss);
-          }
+        for (int e = 0; e < 16; ++e) {
+          ov[e] = fmaf(gt, rv[e], ov[e]);
+          ss = fmaf(ov[e], ov[e], ss);
         }
-        onorm[cg * GDNW_MAXC + ot] = ss;
-#pragma unroll
-        for (int j = 0; j < 4; ++j) zb[j] = ot < len ? zr[4 + j] : make_float4(0.f, 0.f, 0.f, 0.f);
+        onorm[((quad >> 1) * 4 + cg) * GDNW_MAXC + ot] = ss;
         named_sync_id<3, NOUT>();
-        const float tot = onorm[ot] + onorm[GDNW_MAXC + ot] + onorm[2 * GDNW_MAXC + ot] + onorm[3 * GDNW_MAXC + ot];
+        float tot = 0.f;
+#pragma unroll
+        for (int g = 0; g < 8; ++g) tot += onorm[g * GDNW_MAXC + ot];
         const float r = ot < len ? rsqrtf(tot * (1.0f / GDN_D) + args.eps) : 0.f;
-        const size_t obase = ((size_t)n * lb + ot) * KEY_DIM + h * GDN_D + cg * 32;
-        const float4* gw4 = reinterpret_cast<const float4*>(gwv + cg * 32);
+        const size_t obase = ((size_t)n * lb + ot) * KEY_DIM + h * GDN_D + ov0;
+        const float4* gw4 = reinterpret_cast<const float4*>(gwv + ov0);
 #pragma unroll
-        for (int c16 = 0; c16 < 32; c16 += 16) {
-          float ov[16], rv[16];
-          tmem_ld16(lane_base + (uint32_t)(GDNW_COL_O + cg * 32 + c16), ov);
-          tmem_ld16(lane_base + (uint32_t)(GDNW_COL_R + cg * 32 + c16), rv);
+        for (int j = 0; j < 2; ++j) {
+          const float4 ga = gw4[2 * j], gb = gw4[2 * j + 1];
+          const float4 z0 = z4[2 * j], z1 = z4[2 * j + 1];
+          const float g8[8] = {ga.x, ga.y, ga.z, ga.w, gb.x, gb.y, gb.z, gb.w};
+          const float zz[8] = {z0.x, z0.y, z0.z, z0.w, z1.x, z1.y, z1.z, z1.w};
+          float y[8];
 #pragma unroll
-          for (int j = 0; j < 2; ++j) {
-            const int c8 = c16 / 8 + j;  // 8-column chunk of this group
-            const float4 ga = gw4[2 * c8], gb = gw4[2 * c8 + 1];
-            const float4 z0 = c16 == 0 ? za[2 * j] : zb[2 * j], z1 = c16 == 0 ? za[2 * j + 1] : zb[2 * j + 1];
-            const float g8[8] = {ga.x, ga.y, ga.z, ga.w, gb.x, gb.y, gb.z, gb.w};
-            const float zz[8] = {z0.x, z0.y, z0.z, z0.w, z1.x, z1.y, z1.z, z1.w};
-            float y[8];
-#pragma unroll
-            for (int e = 0; e < 8; ++e) {
-              const float o = fmaf(gt, rv[8 * j + e], ov[8 * j + e]);
-              y[e] = g8[e] * (o * r) * silu_fast(zz[e]);
-            }
-            uint4 hi, lo;
-            split8_bf16(y, hi, lo);
-            *reinterpret_cast<uint4*>(args.out_hi + obase + 8 * c8) = hi;
-            *reinterpret_cast<uint4*>(args.out_lo + obase + 8 * c8) = lo;
-          }
+          for (int e = 0; e < 8; ++e) y[e] = g8[e] * (ov[8 * j + e] * r) * silu_fast(zz[e]);
+          uint4 hi, lo;
+          split8_bf16(y, hi, lo);
+          *reinterpret_cast<uint4*>(args.out_hi + obase + 8 * j) = hi;
+          *reinterpret_cast<uint4*>(args.out_lo + obase + 8 * j) = lo;
         }
       }
       ok = named_sync_and_id<1, GDNW_COMPUTE>(mbar_wait(mma8s, ph, args.err, ERR_TIMEOUT_MMA));
