@@ -367,7 +367,7 @@ def bench_c3(lib, samples=50):
                         "write position ~ U[0,512), filled ~ U[1,512] incl. wrapped rings, one query per slot, seed 3",
             "us_per_call": us, "filled_tokens_mean": float(filled.mean()),
             "algorithmic_bytes_filled": filled_bytes, "bytes_full_window": window_bytes,
-            "roofline": {"kernel": "ring_decode_kernel (isolated)", "bound": "hbm", "achieved": achieved, "peak": peak,
+            "roofline": {"kernel": "ring_decode_split_kernel (isolated; split-KV over clusters of 2 CTAs)", "bound": "hbm", "achieved": achieved, "peak": peak,
                          "unit": "GB/s", "frac": achieved / peak, "peak_source": src,
                          "traffic": profile_traffic("ring_decode_c3"),
                          "timing": "median of calls after an L2 flush"},

@@ -19,6 +19,7 @@
 #include "gdn_chunk.cuh"
 #include "gdn_cols.cuh"
 #include "gdn_wy.cuh"
+#include "ring_decode_split.cuh"
 #include "gemm.cuh"
 #include "gemm_persist.cuh"
 #include "norm.cuh"
@@ -216,6 +217,31 @@ static cudaError_t launch_k(void (*kernel)(KArgs...), dim3 grid, dim3 block, siz
   return cudaLaunchKernelEx(&cfg, kernel, args...);
 }
 
+// The same with the thread-block-cluster dimension attribute (clusters of cluster_x CTAs along x).
+template <typename... KArgs, typename... Args>
+static cudaError_t launch_cluster(void (*kernel)(KArgs...), dim3 grid, dim3 block, int cluster_x, size_t smem,
+                                  cudaStream_t st, bool pdl, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = cluster_x;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 2 : 1;
+  return cudaLaunchKernelEx(&cfg, kernel, args...);
+}
+
+// Single-token ring decode: with fewer (row, kv head) items than SMs each item is split over a cluster of
+// RDS_SPLIT CTAs (ring_decode_split_kernel), else whole items go to one persistent CTA per SM.
+static bool ring_decode_splits(int nb) { return nb * ATT_HKV < SM_COUNT; }
+
 struct hsg_engine;
 static void prof_mark(hsg_engine* e, int cls);
 
@@ -318,6 +344,7 @@ static int set_kernel_attributes() {
   CU(cudaFuncSetAttribute(ring_attn_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, attn_smem_bytes(4)));
   CU(cudaFuncSetAttribute(ring_attn_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, attn_smem_bytes(8)));
   CU(cudaFuncSetAttribute(ring_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, rd_smem_bytes()));
+  CU(cudaFuncSetAttribute(ring_decode_split_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, rds_smem_bytes()));
   CU(cudaFuncSetAttribute(ring_prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, pf_smem_bytes()));
   CU(cudaFuncSetAttribute(ring_prefill_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, pt_smem_bytes()));
   return HSG_OK;
@@ -530,7 +557,11 @@ static int enqueue_step(hsg_engine* e, int nb, int lb) {
       }
       {
         ProfScope ps(e, HSG_PROF_RING_ATTN);
-        if (lb == 1)
+        if (lb == 1 && ring_decode_splits(nb))
+          CU(launch_cluster(ring_decode_split_kernel, dim3(RDS_SPLIT, nb * ATT_HKV), dim3(RD_THREADS), RDS_SPLIT,
+                            rds_smem_bytes(), st, e->pdl, e->ring_maps[ai][0], e->ring_maps[ai][1], e->new_maps[0],
+                            e->new_maps[1], a));
+        else if (lb == 1)
           CU(launch_k(ring_decode_kernel, dim3(std::min(SM_COUNT, nb * ATT_HKV)), dim3(RD_THREADS), rd_smem_bytes(),
                       st, e->pdl, e->ring_maps[ai][0], e->ring_maps[ai][1], e->new_maps[0], e->new_maps[1], a));
         else if (lb >= 32)
@@ -1031,7 +1062,12 @@ int hsg_ring_attention(const float* q, void* ring_k, void* ring_v, const void* n
         (rc = make_decode_map(&nk, new_k, (uint64_t)n * ATT_HKV)) ||
         (rc = make_decode_map(&nv, new_v, (uint64_t)n * ATT_HKV)))
       return rc;
-    ring_decode_kernel<<<dim3(std::min(SM_COUNT, n * ATT_HKV)), RD_THREADS, rd_smem_bytes(), st>>>(rk, rv, nk, nv, a);
+    if (ring_decode_splits(n))
+      CU(launch_cluster(ring_decode_split_kernel, dim3(RDS_SPLIT, n * ATT_HKV), dim3(RD_THREADS), RDS_SPLIT,
+                        rds_smem_bytes(), st, false, rk, rv, nk, nv, a));
+    else
+      ring_decode_kernel<<<dim3(std::min(SM_COUNT, n * ATT_HKV)), RD_THREADS, rd_smem_bytes(), st>>>(rk, rv, nk, nv,
+                                                                                                   a);
   } else if (lb >= 16) {
     CUtensorMap rk, rv, nk, nv;
     const uint64_t ring_rows = ((uint64_t)max_slots + 1) * ATT_HKV * RING_COLS;

@@ -43,8 +43,9 @@ struct alignas(16) RdMeta {
 };
 
 __host__ __device__ inline int rd_smem_bytes() {
-  // stages | meta x2 | partial scores [4][MAXK][4] f32 | probabilities [4][PSTRIDE] f16 | row sums [4] | barriers
-  return RD_STAGES * RD_TILE_BYTES + 2 * (int)sizeof(RdMeta) + 4 * RD_MAXK * 4 * 4 + 4 * RD_PSTRIDE * 2 + 16 +
+  // stages | meta x2 | partial scores [4][MAXK][4] f32 | probabilities [4][PSTRIDE] f16 | row sums and maxima
+  // [2][4] each | barriers
+  return RD_STAGES * RD_TILE_BYTES + 2 * (int)sizeof(RdMeta) + 4 * RD_MAXK * 4 * 4 + 4 * RD_PSTRIDE * 2 + 64 +
          (2 * RD_STAGES + 4) * 8 + 1024;
 }
 
@@ -59,8 +60,9 @@ ring_decode_kernel(const __grid_constant__ CUtensorMap tm_rk, const __grid_const
   RdMeta* meta = reinterpret_cast<RdMeta*>(smem + RD_STAGES * RD_TILE_BYTES);
   float* scp = reinterpret_cast<float*>(meta + 2);             // [4 dim ranges][MAXK][4 rows] partial scores
   __half* pr = reinterpret_cast<__half*>(scp + 4 * RD_MAXK * 4);  // [4 rows][PSTRIDE] probabilities
-  float* lsum = reinterpret_cast<float*>(pr + 4 * RD_PSTRIDE);    // [4]
-  uint64_t* full = reinterpret_cast<uint64_t*>(lsum + 4);       // [RD_STAGES]
+  float* lsum = reinterpret_cast<float*>(pr + 4 * RD_PSTRIDE);    // [2 key halves][4 rows] sums
+  float* smax = lsum + 8;                                         // [2 key halves][4 rows] maxima
+  uint64_t* full = reinterpret_cast<uint64_t*>(smax + 8);       // [RD_STAGES]
   uint64_t* empty = full + RD_STAGES;                           // [RD_STAGES]
   uint64_t* meta_full = empty + RD_STAGES;                      // [2]
   uint64_t* meta_free = meta_full + 2;                          // [2]
@@ -245,11 +247,13 @@ ring_decode_kernel(const __grid_constant__ CUtensorMap tm_rk, const __grid_const
       }
     }
     if (!named_sync_and<RD_CONS>(ok)) break;
-    // ---- softmax per query row (warp r): sum the four dim ranges, mask, normalise ----
-    if (warp < ATT_G) {
-      const int r = warp, nk = nt * RD_TILE;
+    // ---- softmax per query row r: warps r and r + 4 take alternate 32-key tiles (sum the four dim ranges, mask);
+    // the two halves' maxima and sums meet in shared memory ----
+    {
+      const int r = warp & 3, hf = warp >> 2, nk = nt * RD_TILE;
       float mx = -INFINITY;
-      for (int c = lane; c < nk; c += 32) {
+#pragma unroll 4
+      for (int c = hf * RD_TILE + lane; c < nk; c += 2 * RD_TILE) {
         const int kp = m.kpos[c];
         float sc = -INFINITY;
         if (kp >= 0 && kp <= qpos && kp > qpos - WIN)
@@ -259,15 +263,19 @@ ring_decode_kernel(const __grid_constant__ CUtensorMap tm_rk, const __grid_const
         mx = fmaxf(mx, sc);
       }
       mx = warp_max(mx);
+      if (lane == 0) smax[hf * 4 + r] = mx;
+      named_sync<RD_CONS>();
+      mx = fmaxf(smax[r], smax[4 + r]);
       const float msafe = mx == -INFINITY ? 0.f : mx;
       float sum = 0.f;
-      for (int c = lane; c < nk; c += 32) {
+#pragma unroll 4
+      for (int c = hf * RD_TILE + lane; c < nk; c += 2 * RD_TILE) {
         const float p = __expf(scp[c * 4 + r] - msafe);  // rounded to fp16 below
         pr[r * RD_PSTRIDE + c] = __float2half_rn(p);
         sum += p;
       }
       sum = warp_sum(sum);
-      if (lane == 0) lsum[r] = sum;
+      if (lane == 0) lsum[hf * 4 + r] = sum;
     }
     named_sync<RD_CONS>();
     // ---- pass 2: O^T[dims 32w..32w+31] += V^T P^T ----
@@ -309,7 +317,7 @@ ring_decode_kernel(const __grid_constant__ CUtensorMap tm_rk, const __grid_const
 #pragma unroll
           for (int cc = 0; cc < 2; ++cc) {
             const int r = 2 * c4 + cc;
-            const float l = lsum[r];
+            const float l = lsum[r] + lsum[4 + r];
             const float val = l > 0.f ? o[mb][2 * half + cc] / l : 0.f;
             if (args.out_raw) {
               args.out_raw[(((size_t)n * ATT_HKV + h) * ATT_G + r) * ATT_D + dim] = val;
