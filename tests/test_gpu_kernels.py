@@ -297,11 +297,12 @@ def test_ring_attention_vs_oracle(L, lb):
     torch.testing.assert_close(out.cpu(), ref, rtol=2e-3, atol=2e-3)
 
 
-def test_ring_attention_config3_with_ring_write(L):
-    """64 slots, W = 512, 8/2 heads, D = 256, one query each, write position ~ U[0, 512), fill ~ U[1, 512] with wrap;
-    the new key/value land in column start % 512 of each slot."""
+@pytest.mark.parametrize("n", [64, 96])
+def test_ring_attention_config3_with_ring_write(L, n):
+    """64 slots (config 3), W = 512, 8/2 heads, D = 256, one query each, write position ~ U[0, 512), fill ~ U[1, 512]
+    with wrap; the new key/value land in column start % 512 of each slot. 64 slots (128 items, fewer than the SMs) run
+    the split-KV kernel on 2-CTA clusters, 96 slots the persistent one-CTA-per-SM kernel of the engine's batches."""
     r = np.random.default_rng(3)
-    n = 64
     q = torch.randn(n, 2, 4, 256).bfloat16().float()
     rk = torch.randn(n + 1, 2, 513, 256).half().float()
     rv = torch.randn(n + 1, 2, 513, 256).half().float()
