@@ -30,11 +30,11 @@ constexpr int PT_KVSTAGE = 2 * PF_KV_BYTES;    // K then V of one 32-key tile (3
 constexpr int PT_STAGES = 4;
 constexpr int PT_P = PT_ROWS * 64;             // P [128 rows][32 keys] fp16 (8 KB)
 constexpr int PT_VT = ATT_D * 64;              // V^T [256 dims][32 keys] fp16 (16 KB)
-constexpr uint32_t PT_TMEM_COLS = 512;         // S at columns 0..31, O at 256..511
+constexpr uint32_t PT_TMEM_COLS = 512;         // S double-buffered at columns 0..31 and 32..63, O at 256..511
 constexpr uint32_t PT_O_COL = 256;
 
 __host__ __device__ inline int pt_smem_bytes() {
-  return PT_Q + PT_STAGES * PT_KVSTAGE + PT_P + PT_VT + (int)sizeof(PfMeta) + (PT_STAGES + 2) * 8 + 16 + 1024;
+  return PT_Q + PT_STAGES * PT_KVSTAGE + PT_P + PT_VT + (int)sizeof(PfMeta) + (PT_STAGES + 4) * 8 + 16 + 1024;
 }
 
 // 2^x by the PTX fast approximation (a few ulp of fp32: far below the fp16 rounding the softmax weights then get).
@@ -56,16 +56,19 @@ ring_prefill_tc_kernel(const __grid_constant__ CUtensorMap tm_rk, const __grid_c
   uint8_t* vts = psm + PT_P;                            // V^T [256 rows x 64 B], SW64
   PfMeta* meta = reinterpret_cast<PfMeta*>(vts + PT_VT);
   uint64_t* full = reinterpret_cast<uint64_t*>(meta + 1);  // [STAGES]
-  uint64_t* mmab = full + PT_STAGES;                       // MMA completion, one phase per commit
-  uint64_t* mdone = mmab + 1;                              // every MMA of the CTA complete (teardown)
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mmab + 2);
+  uint64_t* sbar = full + PT_STAGES;                       // [2] S buffer b holds S_t (t % 2 == b): one phase per t
+  uint64_t* pvbar = sbar + 2;                              // PV_t complete: one phase per tile
+  uint64_t* mdone = pvbar + 1;                             // every MMA of the CTA complete (teardown)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mdone + 1);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int n = blockIdx.x, h = blockIdx.y, rb0 = blockIdx.z * PT_ROWS;
   const int lb = args.lb, M = ATT_G * lb;
   if (tid == 0) {
     for (int s = 0; s < PT_STAGES; ++s) mbar_init(&full[s], 1);
-    mbar_init(mmab, 1);
+    mbar_init(&sbar[0], 1);
+    mbar_init(&sbar[1], 1);
+    mbar_init(pvbar, 1);
     mbar_init(mdone, 1);
     fence_barrier_init();
     prefetch_tmap(&tm_rk);
@@ -173,36 +176,39 @@ ring_prefill_tc_kernel(const __grid_constant__ CUtensorMap tm_rk, const __grid_c
     }
   };
   const uint32_t idesc_s = idesc_f16(PT_ROWS, PF_TILE), idesc_o = idesc_f16(PT_ROWS, ATT_D);
-  auto issue_s = [&](int t) {  // thread 0: S = Q K_t^T
+  auto issue_s = [&](int t) {  // thread 0: S_t = Q K_t^T into S buffer t % 2, committed to sbar[t % 2]
     const uint32_t kb = smem_u32(kvs + (t % PT_STAGES) * PT_KVSTAGE), qb = smem_u32(qsm);
+    const uint32_t d = tmem + (uint32_t)((t & 1) * PF_TILE);
 #pragma unroll
     for (int box = 0; box < 4; ++box)
 #pragma unroll
       for (int kk = 0; kk < 4; ++kk)
-        mma_bf16(tmem, sw128_desc(qb + box * PT_QBOX + kk * 32), sw128_desc(kb + box * PF_BOX + kk * 32),
-                      idesc_s, (box > 0 || kk > 0) ? 1u : 0u);
-    mma_commit(mmab);
+        mma_bf16(d, sw128_desc(qb + box * PT_QBOX + kk * 32), sw128_desc(kb + box * PF_BOX + kk * 32), idesc_s,
+                 (box > 0 || kk > 0) ? 1u : 0u);
+    mma_commit(&sbar[t & 1]);
   };
-  int issued = 0, commits = 0;
+  int issued = 0;
   bool ok = true;
   if (tid == 0 && nt > 0) {
     for (; issued < min(nt, PT_STAGES); ++issued) issue(issued);
-    ok = mbar_wait(&full[0], 0, args.err, ERR_TIMEOUT_TMA);  // tile 0
-    if (ok) {
-      tc_fence_after();
-      issue_s(0);
+    for (int t = 0; t < min(nt, 2) && ok; ++t) {  // S_0 and S_1 ahead of the loop
+      ok = mbar_wait(&full[t % PT_STAGES], (t / PT_STAGES) & 1, args.err, ERR_TIMEOUT_TMA);
+      if (ok) {
+        tc_fence_after();
+        issue_s(t);
+      }
     }
   }
+  // Pipeline: S_{t+2} is issued at the end of iteration t (its buffer's S_t has been read), so the scores of the next
+  // tile are ready while this one's softmax runs; PV_t is committed to its own barrier and waited for only where
+  // iteration t + 1 touches what it reads or writes (P, V^T, a rescale of O).
   const float sl2 = args.scale * 1.4426950408889634f;  // scores in log2 units
   float m = -INFINITY, l = 0.f;
   for (int t = 0; t < nt; ++t) {
-    // S_t (and with it PV_{t-1}) complete
-    if (!__syncthreads_and(ok && mbar_wait(mmab, commits & 1, args.err, ERR_TIMEOUT_MMA))) { ok = false; break; }
-    ++commits;
-    tc_fence_after();
     const int s = t % PT_STAGES;
     if (!rowt) {
       // ---- V_t -> V^T [256 dims][32 keys], 64-byte swizzle: thread 128 + i owns dims 2 i, 2 i + 1 ----
+      if (ok) ok = mbar_wait(&full[s], (t / PT_STAGES) & 1, args.err, ERR_TIMEOUT_TMA);
       const int tw = warp - 4;
       const uint8_t* vb = kvs + s * PT_KVSTAGE + PF_KV_BYTES + tw * PF_BOX;  // the box of dims 64 tw .. 64 tw + 63
       const int ch = lane >> 2, sub = (lane & 3) * 4;                         // 16-byte chunk, byte within it
@@ -214,6 +220,7 @@ ring_prefill_tc_kernel(const __grid_constant__ CUtensorMap tm_rk, const __grid_c
         lo[k >> 1] = __byte_perm(a, b, 0x5410);  // (dim d, key k) | (dim d, key k + 1)
         hi[k >> 1] = __byte_perm(a, b, 0x7632);  // (dim d + 1, key k) | (dim d + 1, key k + 1)
       }
+      if (ok && t > 0) ok = mbar_wait(pvbar, (t - 1) & 1, args.err, ERR_TIMEOUT_MMA);  // PV_{t-1} read V^T
       const int d = 2 * (tid - PT_ROWS);
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
@@ -224,7 +231,9 @@ ring_prefill_tc_kernel(const __grid_constant__ CUtensorMap tm_rk, const __grid_c
     } else {
     // ---- this row's scores, mask, running maximum (lazily raised), P ----
     float sc[32];
-    tmem_ld32(lane_base, sc);
+    if (ok) ok = mbar_wait(&sbar[t & 1], (t >> 1) & 1, args.err, ERR_TIMEOUT_MMA);
+    tc_fence_after();
+    tmem_ld32(lane_base + (uint32_t)((t & 1) * PF_TILE), sc);
     const int* kpos = meta->kpos + t * PF_TILE;
     float mt = -INFINITY;
 #pragma unroll
@@ -240,6 +249,8 @@ ring_prefill_tc_kernel(const __grid_constant__ CUtensorMap tm_rk, const __grid_c
       m = mt;
       l *= alpha;
     }
+    // PV_{t-1} read P and accumulates into O: done before P is rewritten or O rescaled
+    if (ok && t > 0) ok = mbar_wait(pvbar, (t - 1) & 1, args.err, ERR_TIMEOUT_MMA);
     if (t > 0 && __any_sync(0xffffffffu, raise)) {  // the warp's rows whose maximum rose: rescale their O
       tc_fence_after();
 #pragma unroll 1
@@ -265,7 +276,7 @@ ring_prefill_tc_kernel(const __grid_constant__ CUtensorMap tm_rk, const __grid_c
     }
     fence_proxy_async();  // P and V^T (generic writes) are read by the tensor cores
     tc_fence_before();
-    __syncthreads();
+    if (!__syncthreads_and(ok)) { ok = false; break; }
     if (tid == 0) {
       tc_fence_after();
       // O += P V^T
@@ -273,23 +284,22 @@ ring_prefill_tc_kernel(const __grid_constant__ CUtensorMap tm_rk, const __grid_c
 #pragma unroll
       for (int kk = 0; kk < 2; ++kk)
         mma_bf16(tmem + PT_O_COL, sw64_desc(pb + kk * 32), sw64_desc(vtb + kk * 32), idesc_o,
-                      (t > 0 || kk > 0) ? 1u : 0u);
-      // the stage of tile t is free (S_t done, V_t transposed): fetch tile t + STAGES; then S_{t+1}
+                 (t > 0 || kk > 0) ? 1u : 0u);
+      mma_commit(pvbar);
+      // the stage of tile t is free (S_t done, V_t transposed): fetch tile t + STAGES; S_{t+2} into S_t's buffer
       if (issued < nt) issue(issued++);
-      if (t + 1 < nt) {
-        if (mbar_wait(&full[(t + 1) % PT_STAGES], ((t + 1) / PT_STAGES) & 1, args.err, ERR_TIMEOUT_TMA)) {
+      if (t + 2 < nt) {
+        if (mbar_wait(&full[(t + 2) % PT_STAGES], ((t + 2) / PT_STAGES) & 1, args.err, ERR_TIMEOUT_TMA)) {
           tc_fence_after();
-          issue_s(t + 1);
+          issue_s(t + 2);
         } else {
-          ok = false;
+          ok = false;  // the rows' wait for S_{t+2} then runs out and reports
         }
-      } else {
-        mma_commit(mmab);  // the last PV
       }
     }
   }
   // ---- epilogue: O / l times sigmoid(gate) ----
-  if (ok && nt > 0) ok = __syncthreads_and(mbar_wait(mmab, commits & 1, args.err, ERR_TIMEOUT_MMA));
+  if (ok && nt > 0) ok = __syncthreads_and(mbar_wait(pvbar, (nt - 1) & 1, args.err, ERR_TIMEOUT_MMA));
   tc_fence_after();
   const float inv = (ok && valid && l > 0.f) ? 1.0f / l : 0.f;
   if (rowt && row < M) {
