@@ -145,7 +145,9 @@ __device__ __forceinline__ void wy_conv16(float* xc, float4 c, const float (&w)[
 
 // maps.state = the fp16 state pool; maps.in0 = the conv history [(S+1)*3][3][2048] fp32, box [3][3][128];
 // maps.in1 = the projection [rows][8320] fp32, box [128 columns][C rows] (one box per q / k / v slice).
-template <int C>
+// PRE: the projection's q | k | v columns already hold conv + SiLU (the input projection's GEMM_CONV epilogue, which
+// also keeps the conv history): this kernel then reads no conv history and forms only the norms in phase A.
+template <int C, bool PRE>
 __global__ void __launch_bounds__(GDNW_THREADS, 1)
 gdn_wy_kernel(const __grid_constant__ GdntMaps maps, const GdnArgs args) {
   static_assert(C == 32 || C == 64, "32- or 64-token chunks");
@@ -253,8 +255,8 @@ gdn_wy_kernel(const __grid_constant__ GdntMaps maps, const GdnArgs args) {
           meta[i & 1].slot = slot;
           meta[i & 1].len = len;
           if (len > 0) {
-            mbar_arrive_expect_tx(in_full, 3 * C * GDN_D * 4 + 9 * GDN_D * 4);
-            tma_load_3d(hist, &maps.in0, h * GDN_D, 0, (int)slot * CONV_KEEP, in_full);
+            mbar_arrive_expect_tx(in_full, 3 * C * GDN_D * 4 + (PRE ? 0 : 9 * GDN_D * 4));
+            if (!PRE) tma_load_3d(hist, &maps.in0, h * GDN_D, 0, (int)slot * CONV_KEEP, in_full);
             tma_load_2d(xq, &maps.in1, 0 * KEY_DIM + h * GDN_D, n * lb, in_full);
             tma_load_2d(xk, &maps.in1, 1 * KEY_DIM + h * GDN_D, n * lb, in_full);
             tma_load_2d(xv, &maps.in1, 2 * KEY_DIM + h * GDN_D, n * lb, in_full);
@@ -413,7 +415,22 @@ gdn_wy_kernel(const __grid_constant__ GdntMaps maps, const GdnArgs args) {
       }
       const uint32_t ph = seq & 1;
       // ---- A: causal conv + SiLU in place, squared norms of q, k, gates ----
-      if (16 * tq < C) {
+      if (PRE && 16 * tq < C) {
+        // the squared norms of q and k over this warp's 32 channels for its 16 tokens (the inputs are conv'd and
+        // zero past len already)
+#pragma unroll
+        for (int c3 = 0; c3 < 2; ++c3) {
+          const float* xc = (c3 == 0 ? xq : xk) + cc;
+          float sq[16];
+#pragma unroll
+          for (int u = 0; u < 16; ++u) {
+            const float x = xc[(16 * tq + u) * GDN_D];
+            sq[u] = x * x;
+          }
+          const float tot = reduce16(sq, lane);
+          if (!(lane & 1)) part[((16 * tq + reduce16_index(lane)) * 4 + cg) * 2 + c3] = tot;
+        }
+      } else if (!PRE && 16 * tq < C) {
         // the q, k, v regions are consecutive: channel part c3's inputs start at xq + c3 * (64 x 128)
         constexpr int XPART = GDNW_MAXC * GDN_D;
         auto raw = [&](int c3, int t) {  // raw input t of this channel (t < 0: the conv history)

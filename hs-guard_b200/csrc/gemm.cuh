@@ -23,6 +23,18 @@ enum GemmMode : int {
   GEMM_STORE = 0,     // Y[t, n] = acc                      (fp32)
   GEMM_ATOMIC = 1,    // Y[t, n] += acc  (TMA bulk reduce-add in L2; split-K partial sums, residual accumulation)
   GEMM_SILU_MUL = 2,  // W rows in (gate, up) pairs: act[t, f] = silu(gate_f) * up_f as a bf16 hi/lo pair
+  GEMM_CONV = 3,      // the fused GDN input projection (persistent kernel only): as GEMM_STORE, with the causal conv
+                      // + SiLU of the q | k | v rows applied along each request's tokens and the conv history kept
+};
+// Per-launch inputs of GEMM_CONV: request r covers tokens r * lb .. r * lb + lb - 1 (lb a multiple of 32), holds
+// lens[r] valid tokens and belongs to slots[r]; pool = the layer's conv history [slots + 1][3][6144] fp32 (raw
+// inputs 3, 2, 1 tokens before a request's first), w = the conv taps [6144] float4 (x: 3 tokens back .. w: the token).
+struct GemmConv {
+  const int64_t* lens;
+  const int64_t* slots;
+  float* pool;
+  const float* w;
+  int lb, max_slots;
 };
 
 struct GemmArgs {

@@ -32,6 +32,7 @@ struct GemmPcArgs {
   int m;        // valid tokens (chunks wholly beyond are not stored)
   int use_lo, stages, mode;
   int* err;
+  GemmConv conv;  // GEMM_CONV only
 };
 
 __host__ __device__ inline int gpc_chunk_bytes(int mode) {
@@ -180,6 +181,10 @@ gemm_pc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__
       const int nh = (halves > 1 && wrow0 + 128 < args.n_w) ? 2 : 1;
       if (!named_sync_and_id<3, 128>(mbar_wait(&acc_full[buf], (lt >> 1) & 1, args.err, ERR_TIMEOUT_MMA))) break;
       tc_fence_after();
+      // GEMM_CONV: this row's conv taps (q | k | v rows only) and the raw inputs carried from chunk to chunk
+      float4 cw = make_float4(0.f, 0.f, 0.f, 0.f);
+      float ch_h0 = 0.f, ch_h1 = 0.f, ch_h2 = 0.f;
+      if (args.mode == GEMM_CONV && wrow0 < CONV_DIM) cw = reinterpret_cast<const float4*>(args.conv.w)[wrow0 + row];
       for (int q = 0; q < nh * tn; q += GPC_CHUNK, ++seq) {
         const int hf = q / tn, c = q % tn, wr = wrow0 + 128 * hf;  // weight half, token chunk, first weight row
         uint8_t* cb = outbuf + (seq & 1) * chunk_bytes;
@@ -187,6 +192,48 @@ gemm_pc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__
         named_sync_id<3, 128>();
         float v[32];
         tmem_ld32(lane_base + (uint32_t)(buf * acc_cols + q), v);
+        if (args.mode == GEMM_CONV && wr < CONV_DIM) {
+          // q | k | v channel ch = this thread's weight row: causal conv (4 taps) + SiLU along the chunk's 32 tokens,
+          // which lie in one request (chunks and requests both start at multiples of 32). The raw inputs of the 3
+          // tokens before the chunk come from the conv history at a request's first chunk, else from the previous
+          // chunk (the same thread drains a tile's chunks in order). Padded tokens (position >= len) give 0; the
+          // request's last three raw inputs go back to the history.
+          const GemmConv& cv = args.conv;
+          const int ch = wr + row, gt = tok0 + c, r = gt / cv.lb, p0 = gt % cv.lb;
+          int len = 0;
+          int64_t slot = 0;
+          if (gt < args.m) {
+            len = (int)cv.lens[r];
+            slot = cv.slots[r];
+            if (len < 0 || len > cv.lb || slot < 0 || slot > cv.max_slots) len = 0;  // reported by the GDN kernel
+          }
+          float* hp = cv.pool + (size_t)slot * CONV_KEEP * CONV_DIM + ch;
+          if (p0 == 0) {
+            ch_h0 = len > 0 ? hp[0] : 0.f;
+            ch_h1 = len > 0 ? hp[CONV_DIM] : 0.f;
+            ch_h2 = len > 0 ? hp[2 * CONV_DIM] : 0.f;
+          }
+          float n0 = 0.f, n1 = 0.f, n2 = 0.f;
+#pragma unroll
+          for (int t = 0; t < 32; ++t) {
+            const float x = v[t];
+            const float y = silu_fast(fmaf(cw.w, x, fmaf(cw.z, ch_h2, fmaf(cw.y, ch_h1, cw.x * ch_h0))));
+            if (p0 + t == len - 1) {
+              n0 = ch_h1;
+              n1 = ch_h2;
+              n2 = x;
+            }
+            v[t] = p0 + t < len ? y : 0.f;
+            ch_h0 = ch_h1;
+            ch_h1 = ch_h2;
+            ch_h2 = x;
+          }
+          if (len > 0 && p0 <= len - 1 && len - 1 < p0 + 32) {
+            hp[0] = n0;
+            hp[CONV_DIM] = n1;
+            hp[2 * CONV_DIM] = n2;
+          }
+        }
         if (args.mode == GEMM_SILU_MUL) {
           // rows (2f, 2f+1) hold (gate, up) of feature f: the even lane keeps even tokens, the odd lane odd ones
           __nv_bfloat16* sh = reinterpret_cast<__nv_bfloat16*>(cb);  // [32][64]
@@ -223,7 +270,7 @@ gemm_pc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__
             if (args.mode == GEMM_SILU_MUL) {
               tma_store_2d(&tm_o0, cb, wr / 2, tok0 + c);
               tma_store_2d(&tm_o1, cb + GPC_CHUNK * 64 * 2, wr / 2, tok0 + c);
-            } else if (args.mode == GEMM_STORE) {
+            } else if (args.mode == GEMM_STORE || args.mode == GEMM_CONV) {
               tma_store_2d(&tm_o0, cb, wr, tok0 + c);
             } else {
               tma_reduce_add_2d(&tm_o0, cb, wr, tok0 + c);

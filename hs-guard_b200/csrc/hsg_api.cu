@@ -169,7 +169,8 @@ static GemmPlan plan_gemm(int n_w, int K, int M, int mode, int use_lo) {
   best.stages = std::min(stages, std::max(2, best.kps));
   const int tb_full = (M + 255) / 256;
   const long full_tiles = (long)tiles * tb_full;
-  if (full_tiles >= 4L * SM_COUNT || (mode != GEMM_ATOMIC && full_tiles >= 2L * SM_COUNT)) {
+  // GEMM_CONV always takes the persistent kernel (its epilogue carries the conv along a tile's 32-token chunks)
+  if (mode == GEMM_CONV || full_tiles >= 4L * SM_COUNT || (mode != GEMM_ATOMIC && full_tiles >= 2L * SM_COUNT)) {
     // A long-running grid: the persistent kernel, one CTA per SM looping over 256-token tiles with the accumulator
     // double-buffered in TMEM (all 512 columns; each tile's epilogue overlaps the next tile's MMAs) and two load
     // stages beside the two epilogue chunk buffers. Measured (algorithmic TFLOP/s, in_proj / gate-up / out_proj /
@@ -196,6 +197,12 @@ static GemmPlan plan_gemm(int n_w, int K, int M, int mode, int use_lo) {
 // kernel (gdn_chunk_kernel) instead, kept as the comparison.
 static bool use_wy_chunk() {
   const char* s = getenv("HSG_GDN_WY");
+  return !(s && strcmp(s, "0") == 0);
+}
+// With the tcgen05 chunked kernel the causal conv + SiLU of q | k | v runs in the input projection's epilogue
+// (GEMM_CONV); HSG_GDN_CONV_GEMM=0 leaves it in the GDN kernel instead.
+static bool use_conv_in_gemm() {
+  const char* s = getenv("HSG_GDN_CONV_GEMM");
   return !(s && strcmp(s, "0") == 0);
 }
 
@@ -248,7 +255,9 @@ static void prof_mark(hsg_engine* e, int cls);
 static int launch_gemm(cudaStream_t st, const void* w, int n_w, int K, const void* xhi, const void* xlo, int m_alloc,
                        int M, int mode, float* y, int ldy, __nv_bfloat16* ahi, __nv_bfloat16* alo, int ld_act,
                        int* err, int force_splits = 0, hsg_engine* prof = nullptr, int prof_cls = -1,
-                       bool pdl = false) {
+                       bool pdl = false, const GemmConv* conv = nullptr) {
+  if (mode == GEMM_CONV && (!conv || conv->lb % GPC_CHUNK != 0 || 256 % conv->lb != 0))
+    return fail(HSG_ERR_INVALID, "GEMM_CONV needs requests of 32 or 64 tokens");
   const int use_lo = xlo != nullptr;
   GemmPlan p = plan_gemm(n_w, K, M, mode, use_lo);
   if (force_splits > 0 && mode == GEMM_ATOMIC && !p.persist) {
@@ -290,6 +299,7 @@ static int launch_gemm(cudaStream_t st, const void* w, int n_w, int K, const voi
     a.stages = p.stages;
     a.mode = mode;
     a.err = err;
+    a.conv = conv ? *conv : GemmConv{};
     const int total = a.tiles_w * a.tb;
     if (prof) prof_mark(prof, prof_cls);
     CU(launch_k(gemm_pc_kernel, dim3(std::min(total, SM_COUNT)), dim3(GPC_THREADS), p.smem, st, pdl, tw, th, tl, t0,
@@ -339,8 +349,10 @@ static int set_kernel_attributes() {
   CU(cudaFuncSetAttribute(gdn_tc_kernel<false, 3>, cudaFuncAttributeMaxDynamicSharedMemorySize, GDN_SMEM_LIMIT));
   CU(cudaFuncSetAttribute(gdn_chunk_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, GDN_SMEM_LIMIT));
   CU(cudaFuncSetAttribute(gdn_chunk_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, GDN_SMEM_LIMIT));
-  CU(cudaFuncSetAttribute(gdn_wy_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, GDNW_SMEM));
-  CU(cudaFuncSetAttribute(gdn_wy_kernel<32>, cudaFuncAttributeMaxDynamicSharedMemorySize, GDNW_SMEM));
+  CU(cudaFuncSetAttribute(gdn_wy_kernel<64, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, GDNW_SMEM));
+  CU(cudaFuncSetAttribute(gdn_wy_kernel<32, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, GDNW_SMEM));
+  CU(cudaFuncSetAttribute(gdn_wy_kernel<64, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, GDNW_SMEM));
+  CU(cudaFuncSetAttribute(gdn_wy_kernel<32, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, GDNW_SMEM));
   CU(cudaFuncSetAttribute(ring_attn_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, attn_smem_bytes(4)));
   CU(cudaFuncSetAttribute(ring_attn_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, attn_smem_bytes(8)));
   CU(cudaFuncSetAttribute(ring_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, rd_smem_bytes()));
@@ -460,6 +472,8 @@ static int enqueue_step(hsg_engine* e, int nb, int lb) {
   }
   // the chunked kernel (fp16 state, ticks of 32 or 64 tokens): the projection's q|k|v columns, [lb][3][128] boxes
   const bool chunked = e->rec_elem == 2 && lb > GDNT_MAX_LB && lb % GDNC_SUB == 0 && lb <= GDNC_MAX_LB;
+  // 32/64-token ticks on the tcgen05 chunked kernel take their conv from the input projection's epilogue
+  const bool pre_conv = chunked && use_wy_chunk() && (lb == 32 || lb == 64) && use_conv_in_gemm();
   GdntMaps ch_maps;
   if (chunked &&
       (rc = make_map_3d(&ch_maps.in1, e->proj, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, KEY_DIM, 3, M, KEY_DIM * 4,
@@ -476,8 +490,10 @@ static int enqueue_step(hsg_engine* e, int nb, int lb) {
     const hsg_layer_weights& L = e->w.layers[i];
     if (!is_attn_layer(i)) {
       {
-        if ((rc = launch_gemm(st, L.w_in, GDN_IN, HIDDEN, e->xhi, lo(e->xlo), e->m_alloc, M, GEMM_STORE, e->proj,
-                              GDN_IN, nullptr, nullptr, 0, e->err, 0, e, HSG_PROF_GEMM_IN, e->pdl)) != HSG_OK)
+        GemmConv cv{lens, slots, e->conv + (size_t)gi * (e->S + 1) * e->conv_slot(), L.conv_w, lb, e->S};
+        if ((rc = launch_gemm(st, L.w_in, GDN_IN, HIDDEN, e->xhi, lo(e->xlo), e->m_alloc, M,
+                              pre_conv ? GEMM_CONV : GEMM_STORE, e->proj, GDN_IN, nullptr, nullptr, 0, e->err, 0, e,
+                              HSG_PROF_GEMM_IN, e->pdl, pre_conv ? &cv : nullptr)) != HSG_OK)
           return rc;
       }
       GdnArgs g{};
@@ -510,10 +526,9 @@ static int enqueue_step(hsg_engine* e, int nb, int lb) {
                                 lb, CU_TENSOR_MAP_SWIZZLE_NONE)) != HSG_OK)
             return rc;
           wy.in2 = wy.in1;
-          if (lb == 64)
-            CU(launch_k(gdn_wy_kernel<64>, grid, dim3(GDNW_THREADS), GDNW_SMEM, st, e->pdl, wy, g));
-          else
-            CU(launch_k(gdn_wy_kernel<32>, grid, dim3(GDNW_THREADS), GDNW_SMEM, st, e->pdl, wy, g));
+          auto kfn = lb == 64 ? (pre_conv ? gdn_wy_kernel<64, true> : gdn_wy_kernel<64, false>)
+                              : (pre_conv ? gdn_wy_kernel<32, true> : gdn_wy_kernel<32, false>);
+          CU(launch_k(kfn, grid, dim3(GDNW_THREADS), GDNW_SMEM, st, e->pdl, wy, g));
         } else if (chunked) {
           g.stages = gdnc_stages(lb, true);
           ch_maps.state = e->state_maps[gi];
