@@ -213,25 +213,43 @@ gemm_pc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__
             ch_h1 = len > 0 ? hp[CONV_DIM] : 0.f;
             ch_h2 = len > 0 ? hp[2 * CONV_DIM] : 0.f;
           }
-          float n0 = 0.f, n1 = 0.f, n2 = 0.f;
+          if (len >= p0 + 32) {
+            // every token of the chunk is valid (the common case): no masks; the history is the chunk's last three
+            // raw inputs if the request ends here
 #pragma unroll
-          for (int t = 0; t < 32; ++t) {
-            const float x = v[t];
-            const float y = silu_fast(fmaf(cw.w, x, fmaf(cw.z, ch_h2, fmaf(cw.y, ch_h1, cw.x * ch_h0))));
-            if (p0 + t == len - 1) {
-              n0 = ch_h1;
-              n1 = ch_h2;
-              n2 = x;
+            for (int t = 0; t < 32; ++t) {
+              const float x = v[t];
+              v[t] = silu_fast(fmaf(cw.w, x, fmaf(cw.z, ch_h2, fmaf(cw.y, ch_h1, cw.x * ch_h0))));
+              ch_h0 = ch_h1;
+              ch_h1 = ch_h2;
+              ch_h2 = x;
             }
-            v[t] = p0 + t < len ? y : 0.f;
-            ch_h0 = ch_h1;
-            ch_h1 = ch_h2;
-            ch_h2 = x;
-          }
-          if (len > 0 && p0 <= len - 1 && len - 1 < p0 + 32) {
-            hp[0] = n0;
-            hp[CONV_DIM] = n1;
-            hp[2 * CONV_DIM] = n2;
+            if (len == p0 + 32) {
+              hp[0] = ch_h0;
+              hp[CONV_DIM] = ch_h1;
+              hp[2 * CONV_DIM] = ch_h2;
+            }
+          } else {
+            float n0 = 0.f, n1 = 0.f, n2 = 0.f;
+#pragma unroll
+            for (int t = 0; t < 32; ++t) {
+              const float x = v[t];
+              const float y = silu_fast(fmaf(cw.w, x, fmaf(cw.z, ch_h2, fmaf(cw.y, ch_h1, cw.x * ch_h0))));
+              if (p0 + t == len - 1) {
+                n0 = ch_h1;
+                n1 = ch_h2;
+                n2 = x;
+              }
+              v[t] = p0 + t < len ? y : 0.f;
+              ch_h0 = ch_h1;
+              ch_h1 = ch_h2;
+              ch_h2 = x;
+            }
+            if (len > 0 && p0 <= len - 1) {
+              hp[0] = n0;
+              hp[CONV_DIM] = n1;
+              hp[2 * CONV_DIM] = n2;
+            }
           }
         }
         if (args.mode == GEMM_SILU_MUL) {
