@@ -375,12 +375,13 @@ def bench_c3(lib, samples=50):
 
 
 # ---- ours --------------------------------------------------------------------------------------------------------
-def gdn_bytes_per_launch(nb, lb, state_elem=2):
+def gdn_bytes_per_launch(nb, lb, state_elem=2, conv_history=True):
     """Algorithmic HBM bytes of one gated-delta-rule launch: per row, 16 heads x one 128 x 128 state tile read + write
-    (``state_elem`` bytes per element: 32 KB fp16 / 64 KB fp32), the fp32 conv history (3 x 6144) read + write, the
-    projection columns it reads (q|k|v|z|a|b) and its bf16 hi/lo output."""
+    (``state_elem`` bytes per element: 32 KB fp16 / 64 KB fp32), the fp32 conv history (3 x 6144) read + write unless
+    the input projection's epilogue keeps it (``conv_history`` False), the projection columns it reads (q|k|v|z|a|b)
+    and its bf16 hi/lo output."""
     state = 16 * 128 * 128 * state_elem * 2
-    conv = 3 * 6144 * 4 * 2
+    conv = 3 * 6144 * 4 * 2 if conv_history else 0
     proj = lb * (6144 + 2048 + 32) * 4
     out = lb * 2048 * 2 * 2
     return nb * (state + conv + proj + out)
@@ -692,11 +693,14 @@ def c5_measure(eng, S, K, Wm, rank, world, lens, barrier, max_over_ranks, local,
     gemm_n = sum(v[1] for k, v in prof.items() if k.startswith("gemm") or k == "head_gemm")
     gemm_flops = 2.0 * 498_113_344 * S * LB  # algorithmic (the hi/lo activation pair executes twice this)
     gdn_ms, gdn_n = prof["gdn"]
-    gdn_bytes = gdn_bytes_per_launch(S, LB, state_elem)
-    # the chunked delta rule of a 64-token tick: tcgen05 (default) or the warp-MMA comparison (HSG_GDN_WY=0)
+    # the chunked delta rule of a 64-token tick: tcgen05 (default) or the warp-MMA comparison (HSG_GDN_WY=0); with the
+    # former the conv + SiLU runs in the input projection's epilogue unless HSG_GDN_CONV_GEMM=0
     wy = os.environ.get("HSG_GDN_WY", "1") != "0"
-    gdn_kernel = "gdn_wy_kernel (tcgen05)" if wy else "gdn_chunk_kernel (warp-level mma.sync)"
-    gdn_traffic = profile_traffic("gdn_wy_c5") if wy and S == 352 else None
+    pre = wy and os.environ.get("HSG_GDN_CONV_GEMM", "1") != "0"
+    gdn_bytes = gdn_bytes_per_launch(S, LB, state_elem, conv_history=not pre)
+    gdn_kernel = ("gdn_wy_kernel (tcgen05" + ("; conv + SiLU in the input projection's epilogue)" if pre else ")")
+                  if wy else "gdn_chunk_kernel (warp-level mma.sync)")
+    gdn_traffic = profile_traffic("gdn_wy_c5") if pre and S == 352 else None
     achieved = gemm_flops / (gemm_ms * 1e-3) / 1e12
     tokens = S * LB * world
     return {
