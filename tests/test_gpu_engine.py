@@ -187,6 +187,40 @@ def test_engine_32_token_ticks_vs_oracle(weights_seed0, state_dtype):
         eng.close()
 
 
+@pytest.mark.parametrize("wy,conv_gemm", [("1", "1"), ("1", "0"), ("0", "1")])
+def test_engine_chunked_paths_vs_oracle(weights_seed0, monkeypatch, wy, conv_gemm):
+    """The 32/64-token chunked delta rule on each of its paths: the tcgen05 kernel with the conv + SiLU in the input
+    projection's epilogue (the default), the same kernel doing the conv itself (HSG_GDN_CONV_GEMM=0), and the
+    warp-MMA comparison kernel (HSG_GDN_WY=0); ragged 64- and 32-token rows, then single tokens, against the CPU
+    oracle of the reference's streaming engine."""
+    monkeypatch.setenv("HSG_GDN_WY", wy)
+    monkeypatch.setenv("HSG_GDN_CONV_GEMM", conv_gemm)
+    from hs_guard_b200 import DEFAULT
+    from hs_guard_b200.engine import SlotEngine
+    from oracle.stream import StreamOracle
+    r = np.random.default_rng(12)
+    ids = lambda n: [int(x) for x in r.integers(0, 248320, n)]
+    ticks = [[(0, ids(40)), (1, ids(64)), (2, ids(2))], [(1, ids(33)), (2, ids(64)), (0, ids(63))],
+             [(0, ids(31)), (2, ids(18))], [(1, ids(1)), (0, ids(1)), (2, ids(1))]]
+    eng = SlotEngine(weights_seed0, 3)
+    orc = StreamOracle(weights_seed0, DEFAULT, 3)
+    try:
+        worst = 0.0
+        for tick in ticks:
+            got, want = eng.step(tick), orc.step(tick)
+            for role in ("user", "assistant"):
+                for g_, w_ in zip(got[role], want[role]):
+                    worst = max(worst, float(np.abs(g_ - w_).max()))
+        print(f"HSG_GDN_WY={wy} HSG_GDN_CONV_GEMM={conv_gemm}: max |dp| {worst:.3g}")
+        assert worst < P_TOL, worst
+        np.testing.assert_array_equal(eng.length, orc.length)
+        pools = eng.pools()
+        np.testing.assert_allclose(pools["conv"][:, :3].float().cpu().numpy(), orc.conv[:, :3].numpy(), rtol=1e-3,
+                                   atol=1e-3)
+    finally:
+        eng.close()
+
+
 def test_engine_64_token_tick_with_trailing_padding_rows(weights_seed0):
     """A 64-token tick whose row bucket ends in a run of padding rows (100 requests in the 128-row bucket, so every
     CTA of the chunked delta rule ends on several empty items, which release their inputs at once) completes without a
