@@ -387,6 +387,17 @@ def gdn_bytes_per_launch(nb, lb, state_elem=2, conv_history=True):
     return nb * (state + conv + proj + out)
 
 
+def gdn_reference_bytes(nb, lb, state_elem=2):
+    """The same launch's bytes at the reference's storage types (bf16 conv history and projections, one bf16 output):
+    the bound a kernel with the reference's layout would face. This engine keeps the conv history in fp32 and writes a
+    hi/lo output pair for precision, so its own algorithmic bytes (gdn_bytes_per_launch) are larger."""
+    state = 16 * 128 * 128 * state_elem * 2
+    conv = 3 * 6144 * 2 * 2
+    proj = lb * (6144 + 2048 + 32) * 2
+    out = lb * 2048 * 2
+    return nb * (state + conv + proj + out)
+
+
 def tick_bytes(nb, lb, state_elem=2):
     """Algorithmic HBM bytes of one whole tick: bf16 weights once (non-embedding), per row the recurrent state
     (18 layers, read + write, ``state_elem`` bytes per element), fp32 conv history (read + write), the fp16 ring
@@ -443,9 +454,12 @@ def gdn_roofline(eng, S, rng, state_elem, kernel):
         traffic = json.load(open(os.path.join(ROOT, "profiles", "traffic.json")))[key]["bytes_per_launch"]
     except (OSError, ValueError, KeyError):
         pass
+    ref_bytes = gdn_reference_bytes(S, 1, state_elem)
     return ({"kernel": kernel, "bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
              "frac": achieved / peak, "peak_source": src, "traffic": traffic, "algorithmic_bytes": nbytes,
-             "avg_launch_ms": avg}, {k: round(v[0], 4) for k, v in prof.items() if v[1]})
+             "avg_launch_ms": avg, "reference_layout_bytes": ref_bytes,
+             "frac_reference_layout": ref_bytes / (avg * 1e-3) / 1e9 / peak},
+            {k: round(v[0], 4) for k, v in prof.items() if v[1]})
 
 
 def c4_state_f32(eng16, sd, S, K, Wm, barrier, max_over_ranks):
