@@ -82,6 +82,7 @@ def lib():
             "hsg_ring_attention": [P, P, P, P, P, P, P, P, P, I, I, I, F, P, I, P, P],
             "hsg_gemm": [P, I, I, P, P, I, I, P, P, P, I, I, P, P],
             "hsg_gemm_f32_noalloc": [P, I, I, P, I, P, P, P, I, I, P, P],
+            "hsg_check_bounded_wait": [I, C.POINTER(C.c_double)],
         }
         for name, args in sig.items():
             fn = getattr(L, name)

@@ -3,6 +3,7 @@
 #include <cudaTypedefs.h>
 
 #include <atomic>
+#include <chrono>
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
@@ -704,7 +705,44 @@ static int get_graph(hsg_engine* e, int nb, int lb, Bucket** out) {
   return HSG_OK;
 }
 
+// One thread waits, with the bounded wait of every kernel here, on an mbarrier that nothing arrives on.
+__global__ void bounded_wait_probe_kernel(int* err) {
+  __shared__ __align__(8) uint64_t bar;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    fence_barrier_init();
+    mbar_wait(&bar, 0, err, ERR_TIMEOUT_TMA);
+  }
+}
+
 extern "C" {
+
+int hsg_check_bounded_wait(int device, double* seconds) {
+  CU(cudaSetDevice(device));
+  cudaStream_t st = nullptr;
+  int* err = nullptr;
+  CU(cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking));
+  cudaError_t ce = cudaMalloc(&err, sizeof(int));
+  int code = -1;
+  double s = 0.0;
+  if (ce == cudaSuccess) ce = cudaMemsetAsync(err, 0, sizeof(int), st);
+  if (ce == cudaSuccess) ce = cudaStreamSynchronize(st);
+  if (ce == cudaSuccess) {
+    const auto t0 = std::chrono::steady_clock::now();
+    bounded_wait_probe_kernel<<<1, 32, 0, st>>>(err);
+    ce = cudaGetLastError();
+    if (ce == cudaSuccess) ce = cudaMemcpyAsync(&code, err, sizeof(int), cudaMemcpyDeviceToHost, st);
+    if (ce == cudaSuccess) ce = cudaStreamSynchronize(st);
+    s = std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
+  }
+  if (err) cudaFree(err);
+  cudaStreamDestroy(st);
+  if (ce != cudaSuccess) return fail(HSG_ERR_CUDA, "bounded-wait probe: %s", cudaGetErrorString(ce));
+  if (seconds) *seconds = s;
+  if (code != ERR_TIMEOUT_TMA)
+    return fail(HSG_ERR_DEVICE, "bounded-wait probe ended without recording its timeout (code %d)", code);
+  return HSG_OK;
+}
 
 const char* hsg_last_error(void) { return g_last_error.c_str(); }
 const char* hsg_version(void) { return "hsg-b200 0.1 (sm_100a)"; }
