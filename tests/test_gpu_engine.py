@@ -247,27 +247,28 @@ def test_engine_64_token_tick_with_trailing_padding_rows(weights_seed0):
 def test_engine_at_max_slots(weights_seed0):
     """The largest engine hsg_create accepts (4,096 slots, ~70 GB of state pools): two single-token ticks over every
     slot (a 4,096-row tick: the persistent GEMM for the projections, 455 items per CTA in the delta rule, 8,192 ring
-    items), then three slots spread over the range against the CPU oracle fed the same tokens (slots are
-    independent, so the oracle runs only those three)."""
+    items), then a 64-token tick over every slot (262,144 tokens: the fused projection holds 2.18e9 floats, past
+    32-bit element offsets), with three slots spread over the range checked against the CPU oracle fed the same
+    tokens (slots are independent, so the oracle runs only those three)."""
     from hs_guard_b200 import DEFAULT
     from hs_guard_b200.engine import SlotEngine
     from oracle.stream import StreamOracle
     S = 4096
     probe = [0, S // 2 - 1, S - 1]
     rng = np.random.default_rng(41)
-    ticks = [rng.integers(0, 248320, S).tolist() for _ in range(2)]
+    ticks = [rng.integers(0, 248320, (S, n)).tolist() for n in (1, 1, 64)]
     eng = SlotEngine(weights_seed0, S)
     try:
         orc = StreamOracle(weights_seed0, DEFAULT, len(probe))
         worst = 0.0
         for tick in ticks:
-            got = eng.step([(s, [tick[s]]) for s in range(S)])
-            want = orc.step([(j, [tick[s]]) for j, s in enumerate(probe)])
+            got = eng.step([(s, tick[s]) for s in range(S)])
+            want = orc.step([(j, tick[s]) for j, s in enumerate(probe)])
             for role in ("user", "assistant"):
                 for j, s in enumerate(probe):
                     worst = max(worst, float(np.abs(got[role][s] - want[role][j]).max()))
         print(f"{S} slots: max |dp| vs oracle on slots {probe} {worst:.3g}")
         assert worst < P_TOL, worst
-        assert (eng.length == 2).all()
+        assert (eng.length == 66).all()
     finally:
         eng.close()
