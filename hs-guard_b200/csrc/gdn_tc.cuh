@@ -244,15 +244,16 @@ gdn_tc_kernel(const __grid_constant__ GdntMaps maps, const GdnArgs args) {
     for (int i = 0; i < n_items; ++i) {
       const int s = i % S;
       if (!mbar_wait(&done[s], (i / S) & 1, args.err, ERR_TIMEOUT_TMA)) break;
+      // the new state back to the pool first, so that the stores read the stage while the output rows are made
+      if (lane == 0 && meta[s].len > 0) {
+        const int row = tile_row(meta[s].slot);
+        tma_store_2d(tm_state, stage_ptr(s), 0, row);
+        tma_store_2d(tm_state, stage_ptr(s) + GDNT_HALF, 64, row);
+        bulk_commit();
+      }
       epilogue(i, s);
       if (lane == 0) {
-        if (meta[s].len > 0) {  // the new state back to the pool
-          const int row = tile_row(meta[s].slot);
-          tma_store_2d(tm_state, stage_ptr(s), 0, row);
-          tma_store_2d(tm_state, stage_ptr(s) + GDNT_HALF, 64, row);
-          bulk_commit();
-          bulk_wait_read_all();  // the stores have read the stage
-        }
+        bulk_wait_read_all();  // the stores have read the stage
         mbar_arrive(&empty[s]);
       }
       __syncwarp();
