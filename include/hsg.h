@@ -185,10 +185,10 @@ int hsg_gemm_f32_noalloc(const void* w, int n, int k, const float* x, int m, flo
                          int mode, int splits, int* err, void* stream);
 
 /* Diagnostic of the failure path every kernel relies on (no counterpart in the reference): one thread on `device`
- * waits, with the kernels' own bounded wait, on a barrier that nothing
- * completes. The wait gives up after its limit (2 s) and records ERR_TIMEOUT_TMA in an error word, as a stalled
- * pipeline in the engine would; the call returns HSG_OK once that word has been read back with the timeout recorded
- * (seconds = how long it took), HSG_ERR_DEVICE if the wait ended without recording it. The GPU stays usable. */
+ * waits, with the kernels' own bounded wait, on a barrier that nothing completes. The wait gives up after its limit
+ * (2 s) and records ERR_TIMEOUT_TMA in an error word, as a stalled pipeline in the engine would; the call returns
+ * HSG_OK once that word has been read back with the timeout recorded (seconds = how long it took), HSG_ERR_DEVICE if
+ * the wait ended without recording it. The GPU stays usable. */
 int hsg_check_bounded_wait(int device, double* seconds);
 
 const char* hsg_last_error(void);
