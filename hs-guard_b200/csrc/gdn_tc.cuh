@@ -56,16 +56,21 @@ struct GdntMaps {
 
 // Stage: state halves | x [lb][4][128] fp32 (q, k, v, z; o replaces q) | ab [lb][32] fp32 | FUSED: conv history
 // [3][3][128] fp32, RAW: bf16 q|k|v [lb][3][128]; rounded up to 1 KB so every stage's tile is 1024-aligned.
-__host__ __device__ inline int gdnt_stage_bytes(int lb, bool fused) {
+__host__ __device__ constexpr int gdnt_stage_bytes(int lb, bool fused) {
   return (GDNT_TILE + lb * 4 * GDN_D * 4 + lb * GDNT_AB * 4 + (fused ? 9 * GDN_D * 4 : lb * 3 * GDN_D * 2) + 1023) &
          ~1023;
 }
 // Per-item scratch, x2 (item parity): operand columns [lb][4][128] fp16 | partial sums of q.q, k.k, q.k from the two
 // prologue warps [lb][2][4] f32 | e^g [lb] | beta [lb]
-__host__ __device__ inline int gdnt_scratch_bytes(int lb) { return lb * 4 * GDN_D * 2 + lb * 8 * 4 + 2 * lb * 4; }
-__host__ __device__ inline int gdnt_fixed_bytes(int lb) {
+__host__ __device__ constexpr int gdnt_scratch_bytes(int lb) { return lb * 4 * GDN_D * 2 + lb * 8 * 4 + 2 * lb * 4; }
+__host__ __device__ constexpr int gdnt_fixed_bytes(int lb) {
   return 2 * ((gdnt_scratch_bytes(lb) + 15) & ~15) + GDN_MAX_STAGES * (16 + 4 * 8) + 1024;
 }
+// At least two stages always fit: with one, the prologue's wait for item i - 2's consumers (the scratch buffer) would
+// be a wait for a barrier phase already followed by another, which never ends.
+static_assert(2 * gdnt_stage_bytes(GDNT_MAX_LB, true) + gdnt_fixed_bytes(GDNT_MAX_LB) <= GDN_SMEM_LIMIT &&
+                  2 * gdnt_stage_bytes(GDNT_MAX_LB, false) + gdnt_fixed_bytes(GDNT_MAX_LB) <= GDN_SMEM_LIMIT,
+              "gdn_tc_kernel needs two stages at its largest tick");
 __host__ __device__ inline int gdnt_stages(int lb, bool fused) {
   int s = (GDN_SMEM_LIMIT - gdnt_fixed_bytes(lb)) / gdnt_stage_bytes(lb, fused);
   return s > GDN_MAX_STAGES ? GDN_MAX_STAGES : (s < 1 ? 1 : s);
